@@ -1,0 +1,93 @@
+"""ctypes binding of the C ABI in include/flare_b200.h (libflare_b200.so, built in-tree).
+
+The library is required: importing the renderer without it raises, there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libflare_b200.so")
+
+c_float_p = ctypes.POINTER(ctypes.c_float)
+c_int_p = ctypes.POINTER(ctypes.c_int)
+vp = ctypes.c_void_p
+
+FWD_TRAINING, FWD_INFERENCE, FWD_INFERENCE_GEOMETRY, FWD_PCA, FWD_MEDIAN = range(5)
+
+
+class Scene(ctypes.Structure):
+    _fields_ = [("m", vp), ("s", vp), ("q", vp), ("RGBA", vp), ("k", vp), ("n", ctypes.c_int),
+                ("cond", vp), ("features", vp), ("A1", vp), ("A2", vp), ("A3", vp),
+                ("b1", vp), ("b2", vp), ("b3", vp)]
+
+
+class ForwardArgs(ctypes.Structure):
+    _fields_ = [("mode", ctypes.c_int), ("O", vp), ("v", vp), ("n_rays", ctypes.c_int),
+                ("bg", ctypes.c_float * 3), ("T_threshold", ctypes.c_float), ("bitmap", vp),
+                ("depth_reg_accums", vp), ("reg_a", ctypes.c_float), ("reg_b", ctypes.c_float),
+                ("depth_and_index", vp), ("surface_normal", vp), ("normal_reg_accums", vp),
+                ("normal", vp), ("alpha", vp), ("expected_depth_numerator", vp), ("override_colors", vp)]
+
+
+class BackwardArgs(ctypes.Structure):
+    _fields_ = [("O", vp), ("v", vp), ("n_rays", ctypes.c_int), ("bg", ctypes.c_float * 3),
+                ("T_threshold", ctypes.c_float), ("I", vp), ("dL_dI", vp),
+                ("dL_dRGB", vp), ("dL_dA", vp), ("dL_dk", vp), ("dL_dm", vp), ("dL_ds", vp), ("dL_dq", vp),
+                ("dL_dcond", vp), ("dL_dfeatures", vp),
+                ("dL_dw1", vp), ("dL_db1", vp), ("dL_dw2", vp), ("dL_db2", vp), ("dL_dw3", vp), ("dL_db3", vp),
+                ("depth_reg_accums", vp), ("depth_normal_reg_prefix_sums", vp), ("lambda_depth", ctypes.c_float),
+                ("reg_a", ctypes.c_float), ("reg_b", ctypes.c_float), ("surface_normal", vp),
+                ("lambda_normal", ctypes.c_float)]
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [("rays", ctypes.c_longlong), ("passes", ctypes.c_longlong), ("hits_composited", ctypes.c_longlong),
+                ("prim_tests", ctypes.c_longlong), ("node_visits", ctypes.c_longlong)]
+
+
+# every entry point declared in include/flare_b200.h
+EXPORTS = {
+    "flare_last_error": (ctypes.c_char_p, []),
+    "flare_version": (ctypes.c_char_p, []),
+    "flare_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.POINTER(vp)]),
+    "flare_destroy": (ctypes.c_int, [vp]),
+    "flare_set_geometry": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, ctypes.c_int, vp]),
+    "flare_render_hits": (ctypes.c_int, [vp, vp, vp, vp, ctypes.c_int, vp, vp, vp]),
+    "flare_generate_rays": (ctypes.c_int, [vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, vp,
+                                           vp]),
+    "flare_forward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(ForwardArgs), vp]),
+    "flare_backward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(BackwardArgs), vp]),
+    "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
+    "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
+    "flare_selftest_mlp": (ctypes.c_int, [vp, ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp]),
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Loads libflare_b200.so and declares every exported signature.  Raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"flare_b200: native library not found at {path}; run `python -m flare_b200.build`")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class FlareError(RuntimeError):
+    pass
+
+
+def check(code: int, what: str = ""):
+    if code != 0:
+        msg = _lib.flare_last_error().decode(errors="replace") if _lib is not None else ""
+        raise FlareError(f"{what} failed (code {code}): {msg}")

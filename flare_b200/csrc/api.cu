@@ -1,0 +1,297 @@
+// api.cu -- the extern "C" entry points of include/flare_b200.h: renderer lifetime, argument checks,
+// error reporting, GenerateRays, and dispatch into bvh.cu / trace.cu / shade.cu.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "renderer.cuh"
+
+namespace flare {
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int check_status(flare_renderer *r, cudaStream_t st, const char *what) {
+    int h = 0;
+    FLARE_CUDA_TRY(cudaMemcpyAsync(&h, r->dstatus, sizeof(int), cudaMemcpyDeviceToHost, st));
+    FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+    if (h) {
+        FLARE_CUDA_TRY(cudaMemsetAsync(r->dstatus, 0, sizeof(int), st));
+        set_error("%s: device reported error bits 0x%x (%s%s%s)", what, h, (h & ERR_STACK) ? "traversal stack overflow " : "",
+                  (h & ERR_MBAR) ? "tensor-core wait timeout " : "", (h & ERR_INDEX) ? "index out of range" : "");
+        return FLARE_E_DEVICE;
+    }
+    return FLARE_OK;
+}
+
+int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
+                 const void *A3, const float *b3, float *Y, cudaStream_t st, int *status);
+
+// GenerateRays (reference GenerateRays.cu:6-39): v = R (a_x x + b_x) + D (a_y y + b_y) + F
+__global__ void generate_rays_kernel(const float *Rp, const float *Dp, const float *Fp, int width, int height,
+                                     float ttx, float tty, float *out) {
+    int tid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tid >= width * height) return;
+    float3 R = make_float3(Rp[0], Rp[1], Rp[2]), D = make_float3(Dp[0], Dp[1], Dp[2]), F = make_float3(Fp[0], Fp[1], Fp[2]);
+    int x = tid % width, y = tid / width;
+    float a_x = ttx / width, b_x = 0.5f * ttx * ((1.0f / width) - 1.0f);
+    float a_y = tty / height, b_y = 0.5f * tty * ((1.0f / height) - 1.0f);
+    float dx = __fmaf_rn(a_x, (float)x, b_x), dy = __fmaf_rn(a_y, (float)y, b_y);
+    out[3 * (size_t)tid + 0] = __fmaf_rn(R.x, dx, __fmaf_rn(D.x, dy, F.x));
+    out[3 * (size_t)tid + 1] = __fmaf_rn(R.y, dx, __fmaf_rn(D.y, dy, F.y));
+    out[3 * (size_t)tid + 2] = __fmaf_rn(R.z, dx, __fmaf_rn(D.z, dy, F.z));
+}
+
+}  // namespace flare
+
+using namespace flare;
+
+#define CHECK_ARG(cond, ...)          \
+    do {                              \
+        if (!(cond)) {                \
+            set_error(__VA_ARGS__);   \
+            return FLARE_E_INVALID;   \
+        }                             \
+    } while (0)
+
+static inline cudaStream_t S(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+extern "C" {
+
+const char *flare_last_error(void) { return g_err; }
+const char *flare_version(void) { return "flare_b200 0.1 (sm_100a)"; }
+
+int flare_create(int number_of_sides, float chi_square_squared_radius, int max_batch_size, int device,
+                 flare_renderer **out) {
+    g_err[0] = 0;
+    CHECK_ARG(out, "flare_create: out is NULL");
+    CHECK_ARG(number_of_sides >= 3 && number_of_sides <= MAX_SIDES, "flare_create: number_of_sides %d not in [3, %d]",
+              number_of_sides, MAX_SIDES);
+    CHECK_ARG(max_batch_size >= 0, "flare_create: max_batch_size %d < 0", max_batch_size);
+    *out = nullptr;
+    int ndev = 0;
+    FLARE_CUDA_TRY(cudaGetDeviceCount(&ndev));
+    CHECK_ARG(device >= 0 && device < ndev, "flare_create: device %d not in [0, %d)", device, ndev);
+    DeviceGuard dg(device);
+    flare_renderer *r = new flare_renderer();
+    r->device = device;
+    r->nsides = number_of_sides;
+    r->chi2 = chi_square_squared_radius;
+    r->max_rays = max_batch_size;
+    cudaDeviceGetAttribute(&r->num_sms, cudaDevAttrMultiProcessorCount, device);
+    r->poly.n = number_of_sides;
+    {
+        const double ap = std::cos(M_PI / number_of_sides);
+        for (int j = 0; j < number_of_sides; ++j) {
+            const double phi = (2.0 * j + 1.0) * M_PI / number_of_sides;
+            r->poly.c[j] = (float)(std::cos(phi) / ap);
+            r->poly.s[j] = (float)(std::sin(phi) / ap);
+        }
+    }
+    size_t R = (size_t)(max_batch_size > 0 ? max_batch_size : 1);
+    cudaError_t e = cudaSuccess;
+#define ALLOC(p, bytes) \
+    if (e == cudaSuccess) e = cudaMalloc(&(p), (bytes))
+    ALLOC(r->t_min, R * sizeof(float));
+    ALLOC(r->T, R * sizeof(float));
+    ALLOC(r->list[0], R * sizeof(int));
+    ALLOC(r->list[1], R * sizeof(int));
+    ALLOC(r->hit_t, R * K_HITS * sizeof(float));
+    ALLOC(r->hit_idx, R * K_HITS * sizeof(int));
+    ALLOC(r->counters, 64 * sizeof(int));
+    ALLOC(r->dw, 16384 * sizeof(float));
+    ALLOC(r->gscale, 64);
+    ALLOC(r->bounds, 64);
+    ALLOC(r->dstatus, 64);
+    ALLOC(r->dstats, ST_NSTATS * sizeof(unsigned long long));
+#undef ALLOC
+    if (e == cudaSuccess) e = cudaMallocHost(&r->h_count, 64);
+    if (e == cudaSuccess) e = cudaMemset(r->dstatus, 0, 64);
+    if (e == cudaSuccess) e = cudaMemset(r->dstats, 0, ST_NSTATS * sizeof(unsigned long long));
+    if (e != cudaSuccess) {
+        set_error("flare_create: %s", cudaGetErrorString(e));
+        flare_destroy(r);
+        return FLARE_E_CUDA;
+    }
+    *out = r;
+    return FLARE_OK;
+}
+
+int flare_destroy(flare_renderer *r) {
+    if (!r) return FLARE_OK;
+    DeviceGuard dg(r->device);
+    void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
+                    r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dw, r->gscale, r->dstatus, r->dstats};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    if (r->h_count) cudaFreeHost(r->h_count);
+    delete r;
+    return FLARE_OK;
+}
+
+int flare_set_geometry(flare_renderer *r, const float *m, const float *scale, const float *q, const float *opacity,
+                       const float *kappa, int n, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r, "flare_set_geometry: renderer is NULL");
+    CHECK_ARG(n >= 0, "flare_set_geometry: n = %d < 0", n);
+    CHECK_ARG(n == 0 || (m && scale && q && opacity && kappa), "flare_set_geometry: NULL tensor");
+    DeviceGuard dg(r->device);
+    int e = build_geometry(r, m, scale, q, opacity, kappa, n, S(stream));
+    if (e) return e;
+    return check_status(r, S(stream), "flare_set_geometry");
+}
+
+int flare_render_hits(flare_renderer *r, const float *O, const float *v, const float *t_min, int n_rays, float *t_out,
+                      int *idx_out, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r, "flare_render_hits: renderer is NULL");
+    CHECK_ARG(n_rays >= 0, "flare_render_hits: n_rays < 0");
+    if (n_rays == 0) return FLARE_OK;
+    CHECK_ARG(O && v && t_min && t_out && idx_out, "flare_render_hits: NULL tensor");
+    DeviceGuard dg(r->device);
+    int e = launch_trace(r, O, v, t_min, nullptr, n_rays, t_out, idx_out, n_rays, S(stream));
+    if (e) return e;
+    return check_status(r, S(stream), "flare_render_hits");
+}
+
+int flare_generate_rays(const float *R, const float *D, const float *F, int width, int height, float fov_x, float fov_y,
+                        float *out, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(R && D && F && out, "flare_generate_rays: NULL tensor");
+    CHECK_ARG(width > 0 && height > 0, "flare_generate_rays: bad size %dx%d", width, height);
+    float ttx = 2.0f * tanf(0.5f * fov_x), tty = 2.0f * tanf(0.5f * fov_y);
+    int n = width * height;
+    generate_rays_kernel<<<(n + 63) / 64, 64, 0, S(stream)>>>(R, D, F, width, height, ttx, tty, out);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+static int check_scene(flare_renderer *r, const flare_scene *sc, const char *who) {
+    CHECK_ARG(sc, "%s: scene is NULL", who);
+    CHECK_ARG(sc->n == r->n, "%s: scene has %d primitives but the last SetGeometry had %d", who, sc->n, r->n);
+    CHECK_ARG(sc->n == 0 || (sc->m && sc->s && sc->q && sc->RGBA && sc->k), "%s: NULL primitive tensor", who);
+    if (sc->cond)
+        CHECK_ARG(sc->features && sc->A1 && sc->A2 && sc->A3 && sc->b1 && sc->b2 && sc->b3,
+                  "%s: decoder tensors missing", who);
+    return FLARE_OK;
+}
+
+int flare_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r && a, "flare_forward: NULL argument");
+    int e = check_scene(r, sc, "flare_forward");
+    if (e) return e;
+    CHECK_ARG(a->n_rays >= 0 && a->n_rays <= r->max_rays, "flare_forward: n_rays %d exceeds max_batch_size %d",
+              a->n_rays, r->max_rays);
+    CHECK_ARG(a->mode >= 0 && a->mode <= FLARE_FWD_MEDIAN, "flare_forward: bad mode %d", a->mode);
+    if (a->n_rays == 0) return FLARE_OK;
+    CHECK_ARG(a->O && a->v, "flare_forward: NULL rays");
+    if (a->mode != FLARE_FWD_MEDIAN) CHECK_ARG(a->bitmap, "flare_forward: bitmap is NULL");
+    if (a->mode == FLARE_FWD_TRAINING)
+        CHECK_ARG(a->depth_reg_accums && a->normal_reg_accums && a->surface_normal,
+                  "flare_forward: training mode needs depth_reg_accums, normal_reg_accums, surface_normal");
+    if (a->mode == FLARE_FWD_MEDIAN) CHECK_ARG(a->depth_and_index, "flare_forward: depth_and_index is NULL");
+    if (a->mode == FLARE_FWD_PCA) CHECK_ARG(a->override_colors, "flare_forward: override_colors is NULL");
+    DeviceGuard dg(r->device);
+    FLARE_CUDA_TRY(cudaMemsetAsync(r->dstats, 0, ST_NSTATS * sizeof(unsigned long long), S(stream)));
+    r->last_stream = S(stream);
+    e = run_forward(r, sc, a, S(stream));
+    if (e) return e;
+    return check_status(r, S(stream), "flare_forward");
+}
+
+int flare_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r && a, "flare_backward: NULL argument");
+    int e = check_scene(r, sc, "flare_backward");
+    if (e) return e;
+    CHECK_ARG(a->n_rays >= 0 && a->n_rays <= r->max_rays, "flare_backward: n_rays %d exceeds max_batch_size %d",
+              a->n_rays, r->max_rays);
+    if (a->n_rays == 0) return FLARE_OK;
+    CHECK_ARG(a->O && a->v && a->I && a->dL_dI, "flare_backward: NULL rays / image");
+    CHECK_ARG(a->dL_dRGB && a->dL_dA && a->dL_dk && a->dL_dm && a->dL_ds && a->dL_dq, "flare_backward: NULL gradient");
+    CHECK_ARG(a->depth_reg_accums && a->depth_normal_reg_prefix_sums && a->surface_normal,
+              "flare_backward: NULL regulariser buffer");
+    if (sc->cond)
+        CHECK_ARG(a->dL_dcond && a->dL_dfeatures, "flare_backward: NULL decoder gradient");
+    DeviceGuard dg(r->device);
+    FLARE_CUDA_TRY(cudaMemsetAsync(r->dstats, 0, ST_NSTATS * sizeof(unsigned long long), S(stream)));
+    r->last_stream = S(stream);
+    e = run_backward(r, sc, a, S(stream));
+    if (e) return e;
+    return check_status(r, S(stream), "flare_backward");
+}
+
+int flare_get_stats(flare_renderer *r, flare_stats *out) {
+    g_err[0] = 0;
+    CHECK_ARG(r && out, "flare_get_stats: NULL argument");
+    DeviceGuard dg(r->device);
+    unsigned long long h[ST_NSTATS];
+    FLARE_CUDA_TRY(cudaMemcpyAsync(h, r->dstats, sizeof(h), cudaMemcpyDeviceToHost, r->last_stream));
+    FLARE_CUDA_TRY(cudaStreamSynchronize(r->last_stream));
+    out->passes = (long long)h[ST_PASSES];
+    out->hits_composited = (long long)h[ST_HITS];
+    out->prim_tests = (long long)h[ST_PRIM_TESTS];
+    out->node_visits = (long long)h[ST_NODES];
+    out->rays = 0;
+    return FLARE_OK;
+}
+
+int flare_get_frames(flare_renderer *r, float *frames_out, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r && frames_out, "flare_get_frames: NULL argument");
+    if (r->n == 0) return FLARE_OK;
+    DeviceGuard dg(r->device);
+    FLARE_CUDA_TRY(cudaMemcpyAsync(frames_out, r->frames, (size_t)r->n * 12 * sizeof(float), cudaMemcpyDeviceToDevice,
+                                   S(stream)));
+    FLARE_CUDA_TRY(cudaStreamSynchronize(S(stream)));
+    return FLARE_OK;
+}
+
+int flare_selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
+                       const void *A3, const float *b3, float *Y, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(X && A1 && b1 && A2 && b2 && A3 && b3 && Y, "flare_selftest_mlp: NULL argument");
+    CHECK_ARG(rows >= 0, "flare_selftest_mlp: rows < 0");
+    int *status = nullptr;
+    FLARE_CUDA_TRY(cudaMalloc(&status, sizeof(int)));
+    cudaMemsetAsync(status, 0, sizeof(int), S(stream));
+    int e = selftest_mlp(X, rows, A1, b1, A2, b2, A3, b3, Y, S(stream), status);
+    int h = 0;
+    if (!e) {
+        cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, S(stream));
+        cudaError_t ce = cudaStreamSynchronize(S(stream));
+        if (ce != cudaSuccess) {
+            set_error("flare_selftest_mlp: %s", cudaGetErrorString(ce));
+            e = FLARE_E_CUDA;
+        } else if (h) {
+            set_error("flare_selftest_mlp: device reported error bits 0x%x", h);
+            e = FLARE_E_DEVICE;
+        }
+    }
+    cudaFree(status);
+    return e;
+}
+
+}  // extern "C"

@@ -1,0 +1,57 @@
+// common.cuh -- shared definitions of the FlaRe B200 render-path library.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/flare_b200.h"
+
+namespace flare {
+
+constexpr int K_HITS = FLARE_HIT_BUFFER_SIZE;  // 16
+constexpr int COND = FLARE_COND_DIM;           // 96
+constexpr int LUT = FLARE_LUT_SIZE;            // 13154 floats
+constexpr int MAX_SIDES = 64;
+constexpr int TRACE_STACK = 64;
+constexpr float LUT_SCALE = 0.29689279887990428378374198030042f;  // 1/sqrt(11.3449)
+
+// Device status word bits (first word of renderer->dstatus).
+enum : int {
+    ERR_STACK = 1,     // traversal stack overflow (hits may be incomplete)
+    ERR_MBAR = 2,      // a tensor-core completion wait timed out
+    ERR_INDEX = 4,     // out-of-range primitive index met
+};
+
+// Counters in renderer->dstats (unsigned long long each).
+enum { ST_PASSES = 0, ST_HITS = 1, ST_PRIM_TESTS = 2, ST_NODES = 3, ST_NSTATS = 8 };
+
+// BVH2 node: both child boxes plus child links; a negative link ~p is a leaf holding sorted primitive p.
+struct __align__(16) Node {
+    float4 a;  // lo0.x lo0.y lo0.z hi0.x
+    float4 b;  // hi0.y hi0.z lo1.x lo1.y
+    float4 c;  // lo1.z hi1.x hi1.y hi1.z
+    int4 d;    // c0 c1 - -
+};
+
+// Polygon edge constants for the hit test (host computes them once per renderer).
+struct PolyConst {
+    int n;
+    float c[MAX_SIDES];
+    float s[MAX_SIDES];
+};
+
+}  // namespace flare
+
+// internal host-side helpers (implemented in api.cu)
+namespace flare {
+void set_error(const char *fmt, ...);
+}
+
+#define FLARE_CUDA_TRY(call)                                                                   \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess) {                                                               \
+            flare::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return FLARE_E_CUDA;                                                               \
+        }                                                                                      \
+    } while (0)

@@ -1,0 +1,69 @@
+// renderer.cuh -- the renderer object and the host-side launchers shared by the library's .cu files.
+#pragma once
+#include "common.cuh"
+
+struct flare_renderer {
+    int device = 0;
+    int nsides = 8;
+    float chi2 = 11.3449f;
+    int max_rays = 0;
+    int num_sms = 148;
+    flare::PolyConst poly{};
+
+    // ---- geometry (rebuilt by every flare_set_geometry) ----
+    int n = 0;              // primitives
+    int cap_n = 0;          // capacity of the geometry buffers
+    float *frames = nullptr;     // (n,12) prim order: m, N, U/(sx rho), V/(sy rho)
+    float4 *rec = nullptr;       // (n,3) float4 sorted order: (m.xyz,N.x) (N.yz,Ua.xy) (Ua.z,Va.xyz)
+    float *aabb = nullptr;       // (n,6) prim order
+    unsigned *morton = nullptr, *morton_sorted = nullptr;
+    int *ids = nullptr, *ids_sorted = nullptr;  // sorted position -> primitive index
+    flare::Node *nodes = nullptr;               // n-1 internal nodes, node 0 is the root
+    int *parent = nullptr;                      // parent of internal node i (n-1) then of leaf j (n)
+    unsigned *refit_flag = nullptr;
+    float *bounds = nullptr;                    // 6 floats (scene centre bounds, ordered-int encoded)
+    void *sort_tmp = nullptr;
+    size_t sort_tmp_bytes = 0;
+
+    // ---- per-ray scratch, sized max_rays ----
+    float *t_min = nullptr;
+    float *T = nullptr;
+    int *list[2] = {nullptr, nullptr};
+    float *hit_t = nullptr;   // (16, max_rays)
+    int *hit_idx = nullptr;   // (16, max_rays)
+    float *ray_aux = nullptr; // (max_rays, 4) per-ray carried state (backward running colour, median)
+    int *counters = nullptr;  // [0] next active count, [1..] scratch
+    int *h_count = nullptr;   // pinned host mirror of counters[0]
+
+    // ---- decoder scratch ----
+    float *dw = nullptr;      // dense weight-gradient accumulators (see shade.cu)
+    float *gscale = nullptr;  // backward gradient scale (1 float)
+
+    // ---- status / statistics ----
+    int *dstatus = nullptr;               // device status bits
+    unsigned long long *dstats = nullptr; // flare::ST_* counters
+    cudaStream_t last_stream = nullptr;
+};
+
+namespace flare {
+
+// bvh.cu
+int build_geometry(flare_renderer *r, const float *m, const float *scale, const float *q, const float *opacity,
+                   const float *kappa, int n, cudaStream_t st);
+
+// trace.cu: traces `count` rays.  Ray j is ray_ids[j] (or j when ray_ids is null); t_min is indexed by
+// ray id; outputs (16, out_stride) slot-major at column j.
+int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
+                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st);
+
+// shade.cu
+struct ShadeArgs;  // defined in shade.cu
+int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st);
+int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
+int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
+                 const void *A3, const float *b3, float *Y, cudaStream_t st);
+
+// api.cu: reads the device status word after a call and turns set bits into an error.
+int check_status(flare_renderer *r, cudaStream_t st, const char *what);
+
+}  // namespace flare

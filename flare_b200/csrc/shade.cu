@@ -1,0 +1,1262 @@
+// shade.cu -- per-hit decode and front-to-back compositing, forward and backward, plus the multi-pass
+// drivers.  Replaces the reference kernels
+//   Forward_training_CUDA_kernel      (CPyOptiXFLARERenderer_CUDA_Forward_training.cu:497-945)
+//   Forward_inference_CUDA_kernel     (CPyOptiXFLARERenderer_CUDA_Forward_inference.cu:501-928)
+//   GetMedianDepth_CUDA_kernel        (CPyOptiXFLARERenderer_CUDA_GetMedianDepth.cu:497-878)
+//   Backward_CUDA_kernel              (CPyOptiXFLARERenderer_CUDA_Backward.cu:1300-2234)
+//   and their *_base twins (constant colour, no decoder)
+// and the host pass loops (e.g. Forward_training.cu:949-1132), whose thrust compaction and per-pass
+// reduce are replaced by an in-kernel warp-aggregated append to the next pass's ray list.
+//
+// Decoder on the 5th-generation tensor core.  A CTA of 128 threads owns 128 rays, one per thread; for
+// each of the 16 hit slots of a pass the CTA decodes one hit per ray as a 128-row tile:
+//   X (128 x 128 f16: LUT 8 | view encoding 24 | descriptor 96) is written to shared memory row by row
+//   (each thread its own row), then one elected thread issues tcgen05.mma
+//     Y1 = X  W1^T (128x64, K=128)   -> TMEM, epilogue Hardswish -> f16 H1 in shared memory
+//     Y2 = H1 W2^T (128x64, K=64)    -> TMEM, epilogue Hardswish -> f16 H2
+//     Y3 = H2 W3^T (128x16, K=64)    -> TMEM, each thread reads its own row's 4 outputs
+// TMEM lane r of the accumulator is row r, i.e. thread r's hit, so no fragment shuffles are needed.
+// The backward recomputes the forward tile, forms delta3 from the compositing gradient and runs the
+// chain on the tensor core as well:
+//   G2 = d3 W3 (K=16), G1 = d2 W2 (K=64), dX = d1 W1 (K=64; only the LUT and descriptor columns),
+// while the weight gradients accumulate in TMEM across all tiles a CTA processes (M=64 accumulators in
+// the two half-subpartitions: dW1|db1 in lanes 0-15, dW2|dW3^T|db2|db3 in lanes 16-31 of each warp),
+// and are flushed once per CTA.  Backward operands are f16 with a per-call power-of-two gradient scale
+// (from max |dL/dI|) so small image gradients do not underflow.
+#include <cuda_fp16.h>
+
+#include "renderer.cuh"
+#include "umma.cuh"
+
+namespace flare {
+
+// ------------------------------------------------------------------------------------------------
+// shared-memory layout of the decoder kernels (bytes)
+// ------------------------------------------------------------------------------------------------
+constexpr int SM_W1 = 0;                  // 64x128 f16, K chunk stride 1024
+constexpr int SM_W2 = SM_W1 + 16384;      // 64x64 f16, K chunk stride 1024
+constexpr int SM_W3 = SM_W2 + 8192;       // 16x64 f16, K chunk stride 256
+constexpr int SM_BIAS = SM_W3 + 2048;     // b1 64, b2 64, b3 16 floats
+constexpr int SM_FWD_LUT = SM_BIAS + 1024;                    // 13154 floats
+constexpr int SM_FWD_TILE = ((SM_FWD_LUT + LUT * 4 + 1023) / 1024) * 1024;  // 128x128 f16
+constexpr int SM_FWD_MISC = SM_FWD_TILE + 32768;
+constexpr int SM_FWD_BYTES = SM_FWD_MISC + 64;
+
+constexpr int SM_BWD_X = ((SM_BIAS + 1024 + 1023) / 1024) * 1024;  // 128x128 f16 (X)
+constexpr int SM_BWD_D3 = SM_BWD_X + 32768;   // 128x16 f16 (delta3, scaled), followed by >= 14 KB of tiles
+constexpr int SM_BWD_ONES = SM_BWD_D3 + 4096; // 128x8 f16 ones column
+constexpr int SM_BWD_H1 = SM_BWD_ONES + 2048; // 128x64 f16 (H1, later delta1)
+constexpr int SM_BWD_H2 = SM_BWD_H1 + 16384;  // 128x64 f16 (H2, later delta2)
+constexpr int SM_BWD_MISC = SM_BWD_H2 + 16384;
+constexpr int SM_BWD_BYTES = SM_BWD_MISC + 64;
+
+constexpr int TM_FWD_COLS = 128;
+constexpr int TM_BWD_COLS = 256;
+constexpr int TM_DW = 112;  // backward: weight-gradient region starts at this column
+
+// dense weight-gradient accumulator layout in renderer->dw (floats)
+constexpr int DW_W1 = 0, DW_B1 = 8192, DW_W2 = 8256, DW_B2 = 12352, DW_W3 = 12416, DW_B3 = 13440;
+constexpr int DW_TOTAL = 13456;
+
+// ------------------------------------------------------------------------------------------------
+struct SceneP {
+    const float *m, *s, *q, *RGBA, *k;
+    const uint4 *cond;  // (N, 12) 16-byte chunks of the f16 descriptor
+    const float *features;
+    const __half *A1, *A2, *A3;
+    const float *b1, *b2, *b3;
+    const float *override_colors;
+    int n;
+};
+
+struct PassP {
+    const float *O, *v;
+    const int *list_in;
+    int count;
+    const float *hit_t;
+    const int *hit_idx;
+    float *T, *t_min;
+    int *list_out;
+    int *count_out;
+    int *status;
+    unsigned long long *stats;
+    float bg0, bg1, bg2, T_thr;
+};
+
+struct FwdOut {
+    float *bitmap, *dacc, *nacc, *normal, *alpha, *edn, *med;
+    const float *surface_normal;
+    float reg_a, reg_b;
+};
+
+struct BwdIO {
+    float *I;
+    const float *dL_dI;
+    float *dRGB, *dA, *dk, *dm, *ds, *dq, *dcond, *dfeat;
+    float *dw;  // dense MLP gradient accumulators (DW_*)
+    const float *dacc;
+    float *prefix;
+    const float *surface_normal;
+    float lambda_depth, reg_a, reg_b, lambda_normal;
+    const float *gscale;  // [0] = scale applied to delta3 operands
+};
+
+// ------------------------------------------------------------------------------------------------
+// per-hit geometry (reference Forward_training.cu:719-783 and Backward.cu:1527-1608)
+// ------------------------------------------------------------------------------------------------
+struct Geo {
+    float sx, sy;            // e^{-s}
+    float U[3], V[3], N[3];  // rotation columns (N unnormalised by the same S as U, V)
+    float S;                 // 2 / |q|^2
+    float q[4];
+    float d[3];              // P - m
+    float u, w;              // local coordinates
+    float kraw, kappa, kinv;
+    float r2, pk, r2k, G;    // r^2, (r^2)^(kappa-1), (r^2)^kappa, exp(-r2k / (2 kappa))
+};
+
+__device__ __forceinline__ void geometry(const SceneP &sc, int idx, float t, float3 O, float3 v, Geo &g) {
+    float2 s = __ldg(reinterpret_cast<const float2 *>(sc.s) + idx);
+    float4 q = __ldg(reinterpret_cast<const float4 *>(sc.q) + idx);
+    g.sx = __expf(-s.x);
+    g.sy = __expf(-s.y);
+    g.q[0] = q.x; g.q[1] = q.y; g.q[2] = q.z; g.q[3] = q.w;
+    float aa = q.x * q.x, bb = q.y * q.y, cc = q.z * q.z, dd = q.w * q.w;
+    float S = __fdividef(2.0f, aa + bb + cc + dd);
+    g.S = S;
+    float bs = q.y * S, cs = q.z * S, ds = q.w * S;
+    float ab = q.x * bs, ac = q.x * cs, ad = q.x * ds;
+    bb *= S;
+    float bc = q.y * cs, bd = q.y * ds;
+    cc *= S;
+    float cd = q.z * ds;
+    dd *= S;
+    g.U[0] = 1.0f - cc - dd; g.U[1] = bc + ad; g.U[2] = bd - ac;
+    g.V[0] = bc - ad; g.V[1] = 1.0f - bb - dd; g.V[2] = cd + ab;
+    g.N[0] = bd + ac; g.N[1] = cd - ab; g.N[2] = 1.0f - bb - cc;
+    g.kraw = __ldg(sc.k + idx);
+    g.kappa = 1.0f + __logf(1.0f + __expf(g.kraw));
+    g.kinv = 1.0f / g.kappa;
+    const float *m = sc.m + 3 * (size_t)idx;
+    g.d[0] = __fmaf_rn(v.x, t, O.x) - __ldg(m);
+    g.d[1] = __fmaf_rn(v.y, t, O.y) - __ldg(m + 1);
+    g.d[2] = __fmaf_rn(v.z, t, O.z) - __ldg(m + 2);
+    g.u = g.sx * __fmaf_rn(g.U[0], g.d[0], __fmaf_rn(g.U[1], g.d[1], g.U[2] * g.d[2]));
+    g.w = g.sy * __fmaf_rn(g.V[0], g.d[0], __fmaf_rn(g.V[1], g.d[1], g.V[2] * g.d[2]));
+    g.r2 = __fmaf_rn(g.u, g.u, g.w * g.w);
+    float pk = __powf(g.r2, g.kappa - 1.0f);
+    if (isnan(pk)) pk = 0.0f;
+    g.pk = pk;
+    g.r2k = g.r2 * pk;
+    g.G = __expf(-0.5f * g.kinv * g.r2k);
+}
+
+__device__ __forceinline__ float hswish(float y) { return (y * fmaxf(fminf(y + 3.0f, 6.0f), 0.0f)) * (1.0f / 6.0f); }
+__device__ __forceinline__ float hswish_d(float y) {
+    float xu = y + 3.0f, xc = fmaxf(fminf(xu, 6.0f), 0.0f);
+    return (xc + ((xu == xc) ? y : 0.0f)) * (1.0f / 6.0f);
+}
+__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+// LUT levels (reference Forward_training.cu:240-263): res {16,25,40,64}, float2 offsets {0,256,881,2481}
+__device__ __forceinline__ int lut_res(int l) { return l == 0 ? 16 : (l == 1 ? 25 : (l == 2 ? 40 : 64)); }
+__device__ __forceinline__ int lut_off(int l) { return l == 0 ? 0 : (l == 1 ? 256 : (l == 2 ? 881 : 2481)); }
+
+struct LutCell {
+    int i00;        // float2 index of the (x0, y0) corner
+    int R;
+    float fx, fy;
+};
+__device__ __forceinline__ LutCell lut_cell(int l, float cu, float cw) {
+    LutCell c;
+    int R = lut_res(l);
+    float xs = __saturatef((cu + 1.0f) * 0.5f), ys = __saturatef((cw + 1.0f) * 0.5f);
+    float scale = (float)R - 1.0f;
+    float px = xs * scale, py = ys * scale;
+    int ix = min(__float2int_rd(px), R - 2), iy = min(__float2int_rd(py), R - 2);
+    c.fx = px - (float)ix;
+    c.fy = py - (float)iy;
+    c.R = R;
+    c.i00 = lut_off(l) + iy * R + ix;
+    return c;
+}
+
+// Writes one 128-wide f16 decoder input row into a K-major interleaved tile (row r).  Returns the
+// LUT values through lut8 for reuse.
+__device__ __forceinline__ void write_x_row(char *tile, int r, const float2 *lut2, const SceneP &sc, int idx,
+                                            float cu, float cw, float3 v, bool zero) {
+    uint4 *T = reinterpret_cast<uint4 *>(tile);
+    if (zero) {
+#pragma unroll
+        for (int kc = 0; kc < 16; ++kc) T[kc * 128 + r] = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    // chunk 0: LUT (level l -> elements 2l, 2l+1)
+    __half2 h[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        LutCell c = lut_cell(l, cu, cw);
+        float2 f00 = lut2[c.i00], f10 = lut2[c.i00 + 1], f01 = lut2[c.i00 + c.R], f11 = lut2[c.i00 + c.R + 1];
+        float ux = c.fx, vx = 1.0f - ux;
+        float r0x = __fmaf_rn(f00.x, vx, f10.x * ux), r0y = __fmaf_rn(f00.y, vx, f10.y * ux);
+        float r1x = __fmaf_rn(f01.x, vx, f11.x * ux), r1y = __fmaf_rn(f01.y, vx, f11.y * ux);
+        float uy = c.fy, vy = 1.0f - uy;
+        h[l] = __floats2half2_rn(__fmaf_rn(r0x, vy, r1x * uy), __fmaf_rn(r0y, vy, r1y * uy));
+    }
+    T[0 * 128 + r] = *reinterpret_cast<uint4 *>(h);
+    // chunks 1..3: view-direction encoding, axis a -> chunk 1+a, octave f -> (sin, cos) at 2f, 2f+1
+    float va[3] = {v.x, v.y, v.z};
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+        __half2 e[4];
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+            float sn, cs;
+            __sincosf(3.14159265358979f * (float)(1 << f) * va[a], &sn, &cs);
+            e[f] = __floats2half2_rn(sn, cs);
+        }
+        T[(1 + a) * 128 + r] = *reinterpret_cast<uint4 *>(e);
+    }
+    // chunks 4..15: the descriptor row, 12 x 16 bytes
+    const uint4 *cr = sc.cond + (size_t)idx * 12;
+#pragma unroll
+    for (int j = 0; j < 12; ++j) T[(4 + j) * 128 + r] = __ldg(cr + j);
+}
+
+// Writes 64 f16 values (8 chunks) as row r of a K-major interleaved 128-row tile.
+__device__ __forceinline__ void write_row64(char *tile, int r, const float *x) {
+    uint4 *T = reinterpret_cast<uint4 *>(tile);
+#pragma unroll
+    for (int kc = 0; kc < 8; ++kc) {
+        __half2 h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(x[8 * kc + 2 * e], x[8 * kc + 2 * e + 1]);
+        T[kc * 128 + r] = *reinterpret_cast<uint4 *>(h);
+    }
+}
+
+// Loads the decoder weights, biases (and optionally the LUT) into shared memory.
+__device__ void load_decoder(char *smem, const SceneP &sc, bool with_lut) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const uint4 *A1 = reinterpret_cast<const uint4 *>(sc.A1);
+    const uint4 *A2 = reinterpret_cast<const uint4 *>(sc.A2);
+    const uint4 *A3 = reinterpret_cast<const uint4 *>(sc.A3);
+    for (int c = tid; c < 64 * 16; c += nt) {  // W1: row o, chunk kc
+        int o = c >> 4, kc = c & 15;
+        *reinterpret_cast<uint4 *>(smem + SM_W1 + kc * 1024 + o * 16) = __ldg(A1 + c);
+    }
+    for (int c = tid; c < 64 * 8; c += nt) {
+        int o = c >> 3, kc = c & 7;
+        *reinterpret_cast<uint4 *>(smem + SM_W2 + kc * 1024 + o * 16) = __ldg(A2 + c);
+    }
+    for (int c = tid; c < 16 * 8; c += nt) {
+        int o = c >> 3, kc = c & 7;
+        *reinterpret_cast<uint4 *>(smem + SM_W3 + kc * 256 + o * 16) = __ldg(A3 + c);
+    }
+    float *bias = reinterpret_cast<float *>(smem + SM_BIAS);
+    for (int i = tid; i < 144; i += nt) bias[i] = i < 64 ? __ldg(sc.b1 + i) : (i < 128 ? __ldg(sc.b2 + i - 64) : __ldg(sc.b3 + i - 128));
+    if (with_lut) {
+        float2 *lut = reinterpret_cast<float2 *>(smem + SM_FWD_LUT);
+        const float2 *src = reinterpret_cast<const float2 *>(sc.features);
+        for (int i = tid; i < LUT / 2; i += nt) lut[i] = __ldg(src + i);
+    }
+}
+
+// One elected thread issues the three forward layers; the others wait on the mbarrier.
+struct Mma {
+    uint32_t tmem;   // accumulator base
+    uint32_t parity;
+    void *mbar;
+    int *abort;
+};
+
+__device__ __forceinline__ bool mma_wait(Mma &mm) {
+    bool ok = (*(volatile int *)mm.abort == 0) && mbar_wait(mm.mbar, mm.parity);
+    mm.parity ^= 1u;
+    if (!ok) atomicExch(mm.abort, 1);
+    tc_fence_after();
+    return ok;
+}
+
+// Issue helpers (called by thread 0 after a CTA barrier).
+__device__ __forceinline__ void issue_l1(uint32_t d, uint32_t x_addr, uint32_t w1_addr) {
+    const uint32_t id = idesc_f16(128, 64);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks)
+        mma_f16_ss(d, sdesc(x_addr + ks * 4096, 2048, 128), sdesc(w1_addr + ks * 2048, 1024, 128), id, ks > 0);
+}
+__device__ __forceinline__ void issue_l2(uint32_t d, uint32_t h_addr, uint32_t w2_addr) {
+    const uint32_t id = idesc_f16(128, 64);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+        mma_f16_ss(d, sdesc(h_addr + ks * 4096, 2048, 128), sdesc(w2_addr + ks * 2048, 1024, 128), id, ks > 0);
+}
+__device__ __forceinline__ void issue_l3(uint32_t d, uint32_t h_addr, uint32_t w3_addr) {
+    const uint32_t id = idesc_f16(128, 16);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+        mma_f16_ss(d, sdesc(h_addr + ks * 4096, 2048, 128), sdesc(w3_addr + ks * 512, 256, 128), id, ks > 0);
+}
+
+// Reads 64 accumulator columns [col, col+64) of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_row64(uint32_t tmem, int col, float *y) {
+    uint32_t lane = (uint32_t)((threadIdx.x & ~31) << 16);
+    tmem_ld16(tmem + lane + col, y);
+    tmem_ld16(tmem + lane + col + 16, y + 16);
+    tmem_ld16(tmem + lane + col + 32, y + 32);
+    tmem_ld16(tmem + lane + col + 48, y + 48);
+    tmem_wait_ld();
+}
+
+// Forward MLP of the tile in `tile` (X already written, fence + barrier done by the caller).
+// Leaves h1/h2 in `tile` at the end (h2), returns y[0..3] (+ b3) for this thread's row.
+// If keep_d1/keep_d2 are non-null the Hardswish derivatives are stored there (f16 pairs).
+__device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char *h1_tile, char *h2_tile, Mma &mm,
+                                                 float *y4, __half2 *keep_d1, __half2 *keep_d2) {
+    const float *bias = reinterpret_cast<const float *>(smem + SM_BIAS);
+    const int r = threadIdx.x;
+    float y[64];
+    if (r == 0) {
+        tc_fence_after();
+        issue_l1(mm.tmem, smem_u32(x_tile), smem_u32(smem + SM_W1));
+        mma_commit(mm.mbar);
+    }
+    bool ok = mma_wait(mm);
+    tmem_row64(mm.tmem, 0, y);
+#pragma unroll
+    for (int o = 0; o < 64; ++o) {
+        float z = y[o] + bias[o];
+        if (keep_d1 && (o & 1)) keep_d1[o >> 1] = __floats2half2_rn(hswish_d(y[o - 1] + bias[o - 1]), hswish_d(z));
+        y[o] = hswish(z);
+    }
+    write_row64(h1_tile, r, y);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (r == 0) {
+        tc_fence_after();
+        issue_l2(mm.tmem, smem_u32(h1_tile), smem_u32(smem + SM_W2));
+        mma_commit(mm.mbar);
+    }
+    ok = mma_wait(mm) && ok;
+    tmem_row64(mm.tmem, 0, y);
+#pragma unroll
+    for (int o = 0; o < 64; ++o) {
+        float z = y[o] + bias[64 + o];
+        if (keep_d2 && (o & 1)) keep_d2[o >> 1] = __floats2half2_rn(hswish_d(y[o - 1] + bias[64 + o - 1]), hswish_d(z));
+        y[o] = hswish(z);
+    }
+    write_row64(h2_tile, r, y);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (r == 0) {
+        tc_fence_after();
+        issue_l3(mm.tmem, smem_u32(h2_tile), smem_u32(smem + SM_W3));
+        mma_commit(mm.mbar);
+    }
+    ok = mma_wait(mm) && ok;
+    {
+        float y16[16];
+        uint32_t lane = (uint32_t)((threadIdx.x & ~31) << 16);
+        tmem_ld16(mm.tmem + lane, y16);
+        tmem_wait_ld();
+#pragma unroll
+        for (int o = 0; o < 4; ++o) y4[o] = y16[o] + bias[128 + o];
+    }
+    tc_fence_before();
+    return ok;
+}
+
+__device__ __forceinline__ void append_active(bool active, int ray, int *list_out, int *count_out) {
+    unsigned mask = __ballot_sync(0xffffffffu, active);
+    if (mask == 0) return;
+    int lane = threadIdx.x & 31;
+    int leader = __ffs(mask) - 1;
+    int base = 0;
+    if (lane == leader) base = atomicAdd(count_out, __popc(mask));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (active) list_out[base + __popc(mask & ((1u << lane) - 1))] = ray;
+}
+
+// ================================================================================================
+// Forward
+// ================================================================================================
+template <bool DEC, int MODE>
+__global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, FwdOut fo) {
+    extern __shared__ __align__(1024) char smem[];
+    __shared__ int s_abort;
+    const int tid = threadIdx.x;
+    Mma mm{};
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SM_FWD_MISC + 8);
+    if (DEC) {
+        if (tid == 0) {
+            mbar_init(smem + SM_FWD_MISC, 1);
+            fence_mbar_init();
+            s_abort = 0;
+        }
+        if (tid < 32) tmem_alloc(tmem_slot, TM_FWD_COLS);
+        load_decoder(smem, sc, true);
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        mm.tmem = *tmem_slot;
+        mm.parity = 0;
+        mm.mbar = smem + SM_FWD_MISC;
+        mm.abort = &s_abort;
+    }
+    const float2 *lut2 = reinterpret_cast<const float2 *>(smem + SM_FWD_LUT);
+    char *tile = smem + SM_FWD_TILE;
+    unsigned long long nhits = 0;
+    const int nchunks = (pp.count + 127) / 128;
+    for (int chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+        const int slot = chunk * 128 + tid;
+        const bool have = slot < pp.count;
+        const int ray = have ? pp.list_in[slot] : -1;
+        float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+        float T = 0.0f;
+        float rgb[3] = {0, 0, 0}, dacc[4] = {0, 0, 0, 0}, nacc = 0.0f, nrm[3] = {0, 0, 0}, edn = 0.0f;
+        float Nm[3] = {0, 0, 0};
+        bool nvalid = false;
+        float med_t = 0.0f, med_i = 0.0f;
+        bool med_set = false;
+        if (have) {
+            O = make_float3(pp.O[3 * (size_t)ray], pp.O[3 * (size_t)ray + 1], pp.O[3 * (size_t)ray + 2]);
+            v = make_float3(pp.v[3 * (size_t)ray], pp.v[3 * (size_t)ray + 1], pp.v[3 * (size_t)ray + 2]);
+            T = pp.T[ray];
+            if (MODE != FLARE_FWD_MEDIAN)
+                for (int c = 0; c < 3; ++c) rgb[c] = fo.bitmap[3 * (size_t)ray + c];
+            if (MODE == FLARE_FWD_TRAINING) {
+                for (int c = 0; c < 4; ++c) dacc[c] = fo.dacc[4 * (size_t)ray + c];
+                nacc = fo.nacc[4 * (size_t)ray];
+                for (int c = 0; c < 3; ++c) Nm[c] = fo.surface_normal[3 * (size_t)ray + c];
+                nvalid = __fmaf_rn(Nm[0], Nm[0], __fmaf_rn(Nm[1], Nm[1], Nm[2] * Nm[2])) > 0.0f;
+            }
+            if (MODE == FLARE_FWD_INFERENCE_GEOMETRY) {
+                if (fo.normal)
+                    for (int c = 0; c < 3; ++c) nrm[c] = fo.normal[3 * (size_t)ray + c];
+                if (fo.edn) edn = fo.edn[ray];
+            }
+        }
+        int ind = -1;
+        float t_hit = 0.0f;
+        for (int h = 0; h < K_HITS; ++h) {
+            ind = have ? pp.hit_idx[(size_t)h * pp.count + slot] : -1;
+            t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
+            bool valid = ind >= 0 && T >= pp.T_thr;
+            if (MODE == FLARE_FWD_MEDIAN) valid = valid && (T > 0.5f);
+            const int idc = ind >= 0 ? ind : 0;
+            Geo g;
+            if (ind >= 0) geometry(sc, idc, t_hit, O, v, g);
+            else g = Geo{};
+            float y4[4] = {0, 0, 0, 0};
+            if (DEC) {
+                if (!__syncthreads_or(valid)) continue;  // uniform: no ray of this CTA needs slot h
+                write_x_row(tile, tid, lut2, sc, idc, g.u * LUT_SCALE, g.w * LUT_SCALE, v, !valid);
+                fence_async_smem();
+                tc_fence_before();
+                __syncthreads();
+                mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, nullptr);
+                __syncthreads();
+                if (s_abort) goto done;
+            }
+            if (!valid) continue;
+            {
+                float4 rgba = __ldg(reinterpret_cast<const float4 *>(sc.RGBA) + ind);
+                float sig_y = DEC ? sigm(y4[3]) : 1.0f;
+                float opa1 = sigm(rgba.w);
+                float alpha = opa1 * g.G * sig_y;
+                float o = T * alpha;
+                ++nhits;
+                if (MODE == FLARE_FWD_MEDIAN) {
+                    med_t = t_hit;
+                    med_i = __int_as_float(ind);
+                    med_set = true;
+                    T = T - o;
+                    continue;
+                }
+                float c0 = rgba.x, c1 = rgba.y, c2 = rgba.z;
+                if (DEC) {
+                    c0 *= fmaxf(y4[0], 0.0f);
+                    c1 *= fmaxf(y4[1], 0.0f);
+                    c2 *= fmaxf(y4[2], 0.0f);
+                }
+                if (MODE == FLARE_FWD_PCA && sc.override_colors) {
+                    c0 = sc.override_colors[3 * (size_t)ind];
+                    c1 = sc.override_colors[3 * (size_t)ind + 1];
+                    c2 = sc.override_colors[3 * (size_t)ind + 2];
+                }
+                rgb[0] = __fmaf_rn(c0, o, rgb[0]);
+                rgb[1] = __fmaf_rn(c1, o, rgb[1]);
+                rgb[2] = __fmaf_rn(c2, o, rgb[2]);
+                float sgn = (__fmaf_rn(g.N[0], v.x, __fmaf_rn(g.N[1], v.y, g.N[2] * v.z)) > 0.0f) ? -1.0f : 1.0f;
+                if (MODE == FLARE_FWD_INFERENCE_GEOMETRY) {
+                    nrm[0] = __fmaf_rn(sgn * g.N[0], o, nrm[0]);
+                    nrm[1] = __fmaf_rn(sgn * g.N[1], o, nrm[1]);
+                    nrm[2] = __fmaf_rn(sgn * g.N[2], o, nrm[2]);
+                    edn = __fmaf_rn(t_hit, o, edn);
+                }
+                T = T - o;
+                if (MODE == FLARE_FWD_TRAINING) {
+                    float tt = __saturatef(__fdividef(fo.reg_a, t_hit) + fo.reg_b);
+                    float oacc = dacc[1], toacc = dacc[2];
+                    float Ld = o * __fmaf_rn(tt, oacc, -toacc);
+                    dacc[0] = __fmaf_rn(4.0f, Ld, dacc[0]);
+                    dacc[1] = oacc + o;
+                    dacc[2] = __fmaf_rn(tt, o, toacc);
+                    dacc[3] = __fmaf_rn(t_hit, o, dacc[3]);
+                    float nd = sgn * __fmaf_rn(Nm[0], g.N[0], __fmaf_rn(Nm[1], g.N[1], Nm[2] * g.N[2]));
+                    if (nvalid) nacc += o * (1.0f - nd);
+                }
+            }
+        }
+        {
+            bool active = have && ind >= 0 && T >= pp.T_thr;
+            if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
+            if (have) {
+                if (MODE != FLARE_FWD_MEDIAN) {
+                    if (!active) {
+                        rgb[0] = __fmaf_rn(pp.bg0, T, rgb[0]);
+                        rgb[1] = __fmaf_rn(pp.bg1, T, rgb[1]);
+                        rgb[2] = __fmaf_rn(pp.bg2, T, rgb[2]);
+                    }
+                    for (int c = 0; c < 3; ++c) fo.bitmap[3 * (size_t)ray + c] = rgb[c];
+                }
+                if (MODE == FLARE_FWD_TRAINING) {
+                    for (int c = 0; c < 4; ++c) fo.dacc[4 * (size_t)ray + c] = dacc[c];
+                    fo.nacc[4 * (size_t)ray] = nacc;
+                }
+                if (MODE == FLARE_FWD_INFERENCE_GEOMETRY) {
+                    if (fo.normal)
+                        for (int c = 0; c < 3; ++c) fo.normal[3 * (size_t)ray + c] = nrm[c];
+                    if (fo.alpha) fo.alpha[ray] = 1.0f - T;
+                    if (fo.edn) fo.edn[ray] = edn;
+                }
+                if (MODE == FLARE_FWD_MEDIAN && med_set) {
+                    fo.med[2 * (size_t)ray] = med_t;
+                    fo.med[2 * (size_t)ray + 1] = med_i;
+                }
+                pp.t_min[ray] = ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY;
+                pp.T[ray] = T;
+            }
+            append_active(active, ray, pp.list_out, pp.count_out);
+        }
+    }
+done:
+    for (int o = 16; o > 0; o >>= 1) nhits += __shfl_xor_sync(0xffffffffu, nhits, o);
+    if ((tid & 31) == 0 && nhits) atomicAdd(pp.stats + ST_HITS, nhits);
+    if (DEC) {
+        if (s_abort && tid == 0) atomicOr(pp.status, ERR_MBAR);
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid < 32) tmem_dealloc(mm.tmem, TM_FWD_COLS);
+    }
+}
+
+// ================================================================================================
+// Backward
+// ================================================================================================
+// vector reduction into global memory (sm_90+)
+__device__ __forceinline__ void red_add_v4(float *addr, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+template <bool DEC>
+__global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, BwdIO bo) {
+    extern __shared__ __align__(1024) char smem[];
+    __shared__ int s_abort;
+    __shared__ int s_first;
+    const int tid = threadIdx.x;
+    Mma mm{};
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SM_BWD_MISC + 8);
+    float gscale = 1.0f, ginv = 1.0f;
+    if (DEC) {
+        if (tid == 0) {
+            mbar_init(smem + SM_BWD_MISC, 1);
+            fence_mbar_init();
+            s_abort = 0;
+            s_first = 1;
+        }
+        if (tid < 32) tmem_alloc(tmem_slot, TM_BWD_COLS);
+        load_decoder(smem, sc, false);
+        {   // ones column tile (128 rows x 8, element 0 = 1)
+            uint4 *ones = reinterpret_cast<uint4 *>(smem + SM_BWD_ONES);
+            __half2 h[4] = {__floats2half2_rn(1.0f, 0.0f), __floats2half2_rn(0.0f, 0.0f), __floats2half2_rn(0.0f, 0.0f),
+                            __floats2half2_rn(0.0f, 0.0f)};
+            ones[tid] = *reinterpret_cast<uint4 *>(h);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        mm.tmem = *tmem_slot;
+        mm.parity = 0;
+        mm.mbar = smem + SM_BWD_MISC;
+        mm.abort = &s_abort;
+        gscale = bo.gscale[0];
+        ginv = 1.0f / gscale;
+    }
+    const float2 *lut2 = reinterpret_cast<const float2 *>(sc.features);
+    char *xt = smem + SM_BWD_X, *d3t = smem + SM_BWD_D3, *h1t = smem + SM_BWD_H1, *h2t = smem + SM_BWD_H2;
+    const int nchunks = (pp.count + 127) / 128;
+    for (int chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+        const int slot = chunk * 128 + tid;
+        const bool have = slot < pp.count;
+        const int ray = have ? pp.list_in[slot] : -1;
+        float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+        float T = 0.0f;
+        float dLdI[3] = {0, 0, 0}, run[3] = {0, 0, 0};  // run = -(colour from this hit onwards, incl. bg)
+        float D[4] = {0, 0, 0, 0}, P[4] = {0, 0, 0, 0};
+        float Nm[3] = {0, 0, 0};
+        bool nvalid = false;
+        if (have) {
+            O = make_float3(pp.O[3 * (size_t)ray], pp.O[3 * (size_t)ray + 1], pp.O[3 * (size_t)ray + 2]);
+            v = make_float3(pp.v[3 * (size_t)ray], pp.v[3 * (size_t)ray + 1], pp.v[3 * (size_t)ray + 2]);
+            T = pp.T[ray];
+            for (int c = 0; c < 3; ++c) {
+                dLdI[c] = bo.dL_dI[3 * (size_t)ray + c];
+                run[c] = -bo.I[3 * (size_t)ray + c];
+            }
+            for (int c = 0; c < 4; ++c) {
+                D[c] = bo.dacc[4 * (size_t)ray + c];
+                P[c] = bo.prefix[4 * (size_t)ray + c];
+            }
+            for (int c = 0; c < 3; ++c) Nm[c] = bo.surface_normal[3 * (size_t)ray + c];
+            nvalid = __fmaf_rn(Nm[0], Nm[0], __fmaf_rn(Nm[1], Nm[1], Nm[2] * Nm[2])) > 0.0f;
+        }
+        int ind = -1;
+        float t_hit = 0.0f;
+        for (int h = 0; h < K_HITS; ++h) {
+            ind = have ? pp.hit_idx[(size_t)h * pp.count + slot] : -1;
+            t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
+            const bool valid = ind >= 0 && T >= pp.T_thr;
+            const int idc = ind >= 0 ? ind : 0;
+            Geo g;
+            if (ind >= 0) geometry(sc, idc, t_hit, O, v, g);
+            else g = Geo{};
+            const float cu = g.u * LUT_SCALE, cw = g.w * LUT_SCALE;
+            float y4[4] = {0, 0, 0, 0};
+            __half2 hd1[32], hd2[32];
+            if (DEC) {
+                if (!__syncthreads_or(valid)) continue;  // uniform
+                write_x_row(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
+                fence_async_smem();
+                tc_fence_before();
+                __syncthreads();
+                mlp_forward_tile(smem, xt, h1t, h2t, mm, y4, hd1, hd2);
+                __syncthreads();
+                if (s_abort) goto done;
+            }
+            // ---- compositing gradient (restates Backward.cu:1700-1900) ----
+            float gu = 0.0f, gw = 0.0f, dLdt_depth = 0.0f, ow = 0.0f, sgn = 1.0f;
+            float d3[4] = {0, 0, 0, 0};
+            if (valid) {
+                float4 rgba = __ldg(reinterpret_cast<const float4 *>(sc.RGBA) + ind);
+                float z3[3] = {1.0f, 1.0f, 1.0f}, sig_y = 1.0f, dz3[4] = {1.0f, 1.0f, 1.0f, 0.0f};
+                if (DEC) {
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        z3[c] = fmaxf(y4[c], 0.0f);
+                        dz3[c] = y4[c] >= 0.0f ? 1.0f : 0.0f;
+                    }
+                    sig_y = sigm(y4[3]);
+                    dz3[3] = sig_y * (1.0f - sig_y);
+                }
+                const float opa1 = sigm(rgba.w);
+                const float aG = opa1 * g.G;     // sigma(A) G
+                const float alpha = aG * sig_y;  // opacity of this hit
+                const float T_prev = T;
+                float a_eff = alpha;
+                T = T - T * alpha;
+                float tu = __fdividef(bo.reg_a, t_hit) + bo.reg_b;
+                float tt = __saturatef(tu);
+                float o = T_prev * alpha;
+                float oacc = P[1], toacc = P[2];
+                float dLdo = 2.0f * (__fmaf_rn(tt, __fmaf_rn(2.0f, oacc, -D[1]), -2.0f * toacc) + D[2]);
+                float dLdt = 2.0f * o * __fmaf_rn(2.0f, oacc, o - D[1]);
+                dLdt *= __fdividef(-bo.reg_a, t_hit * t_hit);
+                if (tt != tu) dLdt = 0.0f;
+                sgn = (__fmaf_rn(g.N[0], v.x, __fmaf_rn(g.N[1], v.y, g.N[2] * v.z)) > 0.0f) ? -1.0f : 1.0f;
+                float nd = sgn * __fmaf_rn(Nm[0], g.N[0], __fmaf_rn(Nm[1], g.N[1], Nm[2] * g.N[2]));
+                float dLn_do = nvalid ? 1.0f - nd : 0.0f;
+                P[0] = __fmaf_rn(o, dLdo, P[0]);
+                P[1] = oacc + o;
+                P[2] = __fmaf_rn(tt, o, toacc);
+                P[3] = __fmaf_rn(o, dLn_do, P[3]);
+                float dLdalpha = (T >= pp.T_thr) ? __fdividef(P[0] - D[0], 1.0f - alpha) : 0.0f;
+                dLdalpha = bo.lambda_depth * __fmaf_rn(dLdo, T_prev, dLdalpha);
+                dLdt_depth = dLdt * bo.lambda_depth;
+                if (T < pp.T_thr) {
+                    run[0] = -T_prev * pp.bg0;
+                    run[1] = -T_prev * pp.bg1;
+                    run[2] = -T_prev * pp.bg2;
+                    a_eff = 0.0f;
+                }
+                float cc0 = z3[0] * rgba.x, cc1 = z3[1] * rgba.y, cc2 = z3[2] * rgba.z;
+                float partial = __fdividef(
+                    __fmaf_rn(dLdI[0], __fmaf_rn(cc0, T_prev, run[0]),
+                              __fmaf_rn(dLdI[1], __fmaf_rn(cc1, T_prev, run[1]), dLdI[2] * __fmaf_rn(cc2, T_prev, run[2]))),
+                    1.0f - a_eff);
+                float gsum = partial + dLdalpha;  // dL/d(alpha) of this hit
+                float w_eff = a_eff * T_prev;
+                float dRGB0 = z3[0] * w_eff, dRGB1 = z3[1] * w_eff, dRGB2 = z3[2] * w_eff;
+                run[0] = __fmaf_rn(dRGB0, rgba.x, run[0]);
+                run[1] = __fmaf_rn(dRGB1, rgba.y, run[1]);
+                run[2] = __fmaf_rn(dRGB2, rgba.z, run[2]);
+                atomicAdd(bo.dRGB + 3 * (size_t)ind, dRGB0 * dLdI[0]);
+                atomicAdd(bo.dRGB + 3 * (size_t)ind + 1, dRGB1 * dLdI[1]);
+                atomicAdd(bo.dRGB + 3 * (size_t)ind + 2, dRGB2 * dLdI[2]);
+                atomicAdd(bo.dA + ind, alpha * (1.0f - opa1) * gsum);
+                // kappa = 1 + softplus(k): dG/dkappa (Backward.cu:1882-1894)
+                float dk = alpha * gsum * 0.5f * g.r2k * sigm(g.kraw) * g.kinv * (g.kinv - __logf(g.r2));
+                if (isnan(dk)) dk = 0.0f;
+                atomicAdd(bo.dk + ind, dk);
+                // delta3: gradients of the layer-3 pre-activations
+                d3[0] = dLdI[0] * rgba.x * alpha * T_prev * dz3[0];
+                d3[1] = dLdI[1] * rgba.y * alpha * T_prev * dz3[1];
+                d3[2] = dLdI[2] * rgba.z * alpha * T_prev * dz3[2];
+                d3[3] = aG * gsum * dz3[3];
+                // opacity path of dL/du, dL/dw: d alpha/du = -alpha (r^2)^(kappa-1) u
+                float apk = alpha * gsum * g.pk;
+                gu = -apk * g.u;
+                gw = -apk * g.w;
+                ow = o;
+            }
+            // ---- decoder backward on the tensor core ----
+            if (DEC) {
+                {   // delta3 tile row (scaled into the f16 range), zero for rows that do not contribute
+                    uint4 *T3 = reinterpret_cast<uint4 *>(d3t);
+                    __half2 hh[4] = {__floats2half2_rn(d3[0] * gscale, d3[1] * gscale),
+                                     __floats2half2_rn(d3[2] * gscale, d3[3] * gscale), __floats2half2_rn(0.f, 0.f),
+                                     __floats2half2_rn(0.f, 0.f)};
+                    T3[tid] = *reinterpret_cast<uint4 *>(hh);
+                    T3[128 + tid] = make_uint4(0, 0, 0, 0);
+                }
+                fence_async_smem();
+                tc_fence_before();
+                __syncthreads();
+                const uint32_t acc0 = s_first ? 0u : 1u;
+                const uint32_t dwreg = mm.tmem + TM_DW;
+                const uint32_t half1 = 16u << 16;
+                if (tid == 0) {
+                    tc_fence_after();
+                    // G2 = d3 W3 : M=128, N=64 (h2 features), K=16; B = W3 read MN-major
+                    mma_f16_ss(mm.tmem, sdesc(smem_u32(d3t), 2048, 128), sdesc(smem_u32(smem + SM_W3), 128, 256),
+                               idesc_f16(128, 64, 0, 1), 0);
+                    // dW3^T += H2^T d3 : M=64 (h2 features), N=8, K=128 hits; both operands MN-major
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg + half1 + 64, sdesc(smem_u32(h2t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(d3t) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
+                                   (ks > 0) | acc0);
+                    // db3 += d3^T 1 : M=64 (rows >= 16 are not used), N=8
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg + half1 + 80, sdesc(smem_u32(d3t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(smem + SM_BWD_ONES) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
+                                   (ks > 0) | acc0);
+                    mma_commit(mm.mbar);
+                }
+                mma_wait(mm);
+                float gy[64];
+                tmem_row64(mm.tmem, 0, gy);
+                // delta2 = G2 * hswish'(y2) -> H2 tile (H2 is free: dW3 completed with G2)
+#pragma unroll
+                for (int o = 0; o < 32; ++o) {
+                    float2 dd = __half22float2(hd2[o]);
+                    gy[2 * o] *= dd.x;
+                    gy[2 * o + 1] *= dd.y;
+                }
+                write_row64(h2t, tid, gy);
+                fence_async_smem();
+                tc_fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    tc_fence_after();
+                    // G1 = d2 W2 : M=128, N=64 (h1 features), K=64
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16_ss(mm.tmem, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
+                                   sdesc(smem_u32(smem + SM_W2) + ks * 256, 128, 1024), idesc_f16(128, 64, 0, 1),
+                                   ks > 0);
+                    // dW2 += d2^T H1 : M=64 (out), N=64 (h1 features), K=128 hits
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg + half1, sdesc(smem_u32(h2t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(h1t) + ks * 256, 128, 2048), idesc_f16(64, 64, 1, 1),
+                                   (ks > 0) | acc0);
+                    // db2 += d2^T 1
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg + half1 + 72, sdesc(smem_u32(h2t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(smem + SM_BWD_ONES) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
+                                   (ks > 0) | acc0);
+                    mma_commit(mm.mbar);
+                }
+                mma_wait(mm);
+                tmem_row64(mm.tmem, 0, gy);
+#pragma unroll
+                for (int o = 0; o < 32; ++o) {
+                    float2 dd = __half22float2(hd1[o]);
+                    gy[2 * o] *= dd.x;
+                    gy[2 * o + 1] *= dd.y;
+                }
+                write_row64(h1t, tid, gy);  // delta1 (H1 is free: dW2 completed with G1)
+                fence_async_smem();
+                tc_fence_before();
+                __syncthreads();
+                if (tid == 0) {
+                    tc_fence_after();
+                    // dX[:, 0:16) = d1 W1[:, 0:16) ; dX[:, 32:128) -> TMEM columns [16, 112)
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16_ss(mm.tmem, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
+                                   sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1),
+                                   ks > 0);
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16_ss(mm.tmem + 16, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
+                                   sdesc(smem_u32(smem + SM_W1) + 4 * 1024 + ks * 256, 128, 1024),
+                                   idesc_f16(128, 96, 0, 1), ks > 0);
+                    // dW1 += d1^T X : M=64, N=128, K=128 hits
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(xt) + ks * 256, 128, 2048), idesc_f16(64, 128, 1, 1),
+                                   (ks > 0) | acc0);
+                    // db1 += d1^T 1
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg + 128, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(smem + SM_BWD_ONES) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
+                                   (ks > 0) | acc0);
+                    mma_commit(mm.mbar);
+                }
+                mma_wait(mm);
+                const uint32_t lane = (uint32_t)((threadIdx.x & ~31) << 16);
+                float dx16[16];
+                tmem_ld16(mm.tmem + lane, dx16);
+                tmem_wait_ld();
+                float dxu = 0.0f, dxw = 0.0f;
+                if (valid) {
+                    // LUT: dX element 2l+f -> feature gradients of level l and the coordinate gradient
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) {
+                        LutCell c = lut_cell(l, cu, cw);
+                        float dx_ = dx16[2 * l] * ginv, dy_ = dx16[2 * l + 1] * ginv;
+                        float ux = c.fx, vx = 1.0f - ux, uy = c.fy, vy = 1.0f - uy;
+                        float2 f00 = __ldg(lut2 + c.i00), f10 = __ldg(lut2 + c.i00 + 1),
+                               f01 = __ldg(lut2 + c.i00 + c.R), f11 = __ldg(lut2 + c.i00 + c.R + 1);
+                        float dfx_x = __fmaf_rn(f10.x - f00.x, vy, (f11.x - f01.x) * uy);
+                        float dfx_y = __fmaf_rn(f10.y - f00.y, vy, (f11.y - f01.y) * uy);
+                        float dfy_x = __fmaf_rn(f01.x - f00.x, vx, (f11.x - f10.x) * ux);
+                        float dfy_y = __fmaf_rn(f01.y - f00.y, vx, (f11.y - f10.y) * ux);
+                        float sc_ = 0.5f * LUT_SCALE * ((float)c.R - 1.0f);
+                        dxu += sc_ * __fmaf_rn(dx_, dfx_x, dy_ * dfx_y);
+                        dxw += sc_ * __fmaf_rn(dx_, dfy_x, dy_ * dfy_y);
+                        float *F = bo.dfeat + 2 * (size_t)c.i00;
+                        atomicAdd(F, dx_ * vx * vy);
+                        atomicAdd(F + 1, dy_ * vx * vy);
+                        atomicAdd(F + 2, dx_ * ux * vy);
+                        atomicAdd(F + 3, dy_ * ux * vy);
+                        atomicAdd(F + 2 * c.R, dx_ * vx * uy);
+                        atomicAdd(F + 2 * c.R + 1, dy_ * vx * uy);
+                        atomicAdd(F + 2 * c.R + 2, dx_ * ux * uy);
+                        atomicAdd(F + 2 * c.R + 3, dy_ * ux * uy);
+                    }
+                }
+                gu += dxu;
+                gw += dxw;
+                // descriptor gradient: dX[32:128) at TMEM columns [16, 112)
+                float *dc = bo.dcond + (size_t)idc * 96;
+#pragma unroll
+                for (int b = 0; b < 6; ++b) {
+                    float v16[16];
+                    tmem_ld16(mm.tmem + lane + 16 + 16 * b, v16);
+                    tmem_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4)
+                            red_add_v4(dc + 16 * b + e, v16[e] * ginv, v16[e + 1] * ginv, v16[e + 2] * ginv,
+                                       v16[e + 3] * ginv);
+                    }
+                }
+                tc_fence_before();
+                __syncthreads();
+                if (tid == 0) s_first = 0;
+                if (s_abort) goto done;
+            }
+            if (valid) {
+                // ---- primitive geometry gradients from dL/du, dL/dw and dL/dt (depth) ----
+                float ndv = __fmaf_rn(g.N[0], v.x, __fmaf_rn(g.N[1], v.y, g.N[2] * v.z));
+                float inv_ndv = 1.0f / ndv;
+                float Uv = __fmaf_rn(g.U[0], v.x, __fmaf_rn(g.U[1], v.y, g.U[2] * v.z));
+                float Vv = __fmaf_rn(g.V[0], v.x, __fmaf_rn(g.V[1], v.y, g.V[2] * v.z));
+                // total dL/dt through u, w (P = O + t v) and the depth regulariser
+                float dLdt = __fmaf_rn(gu * g.sx, Uv, __fmaf_rn(gw * g.sy, Vv, dLdt_depth));
+                float kt = dLdt * inv_ndv;
+                // dL/dm = dL/dt N/(N.v) - (gu e^-sx U + gw e^-sy V)
+                float su = gu * g.sx, sw = gw * g.sy;
+                atomicAdd(bo.dm + 3 * (size_t)ind, kt * g.N[0] - (su * g.U[0] + sw * g.V[0]));
+                atomicAdd(bo.dm + 3 * (size_t)ind + 1, kt * g.N[1] - (su * g.U[1] + sw * g.V[1]));
+                atomicAdd(bo.dm + 3 * (size_t)ind + 2, kt * g.N[2] - (su * g.U[2] + sw * g.V[2]));
+                // dL/ds = -u dL/du (u = e^-s U.(P - m))
+                atomicAdd(bo.ds + 2 * (size_t)ind, -g.u * gu);
+                atomicAdd(bo.ds + 2 * (size_t)ind + 1, -g.w * gw);
+                // dL/dR for R = [U V N]: G_U = gu e^-sx (P-m), G_V = gw e^-sy (P-m),
+                // G_N = -dL/dt (P-m)/(N.v) - lambda_n o sgn N_target (the normal regulariser's opacity is held)
+                float ln = nvalid ? bo.lambda_normal * (-ow * sgn) : 0.0f;
+                float Gm[3][3];
+#pragma unroll
+                for (int i = 0; i < 3; ++i) {
+                    Gm[i][0] = su * g.d[i];
+                    Gm[i][1] = sw * g.d[i];
+                    Gm[i][2] = -kt * g.d[i] + ln * Nm[i];
+                }
+                // R = I + S M(q) with S = 2/|q|^2; dR/dq_k = S (dM/dq_k - S q_k M)
+                const float a = g.q[0], b = g.q[1], c = g.q[2], d = g.q[3], S = g.S;
+                float GM = Gm[0][0] * (-(c * c + d * d)) + Gm[0][1] * (b * c - a * d) + Gm[0][2] * (b * d + a * c) +
+                           Gm[1][0] * (b * c + a * d) + Gm[1][1] * (-(b * b + d * d)) + Gm[1][2] * (c * d - a * b) +
+                           Gm[2][0] * (b * d - a * c) + Gm[2][1] * (c * d + a * b) + Gm[2][2] * (-(b * b + c * c));
+                float dMa = -d * Gm[0][1] + c * Gm[0][2] + d * Gm[1][0] - b * Gm[1][2] - c * Gm[2][0] + b * Gm[2][1];
+                float dMb = c * Gm[0][1] + d * Gm[0][2] + c * Gm[1][0] - 2.0f * b * Gm[1][1] - a * Gm[1][2] +
+                            d * Gm[2][0] + a * Gm[2][1] - 2.0f * b * Gm[2][2];
+                float dMc = -2.0f * c * Gm[0][0] + b * Gm[0][1] + a * Gm[0][2] + b * Gm[1][0] + d * Gm[1][2] -
+                            a * Gm[2][0] + d * Gm[2][1] - 2.0f * c * Gm[2][2];
+                float dMd = -2.0f * d * Gm[0][0] - a * Gm[0][1] + b * Gm[0][2] + a * Gm[1][0] - 2.0f * d * Gm[1][1] +
+                            c * Gm[1][2] + b * Gm[2][0] + c * Gm[2][1];
+                red_add_v4(bo.dq + 4 * (size_t)ind, S * (dMa - S * a * GM), S * (dMb - S * b * GM),
+                           S * (dMc - S * c * GM), S * (dMd - S * d * GM));
+            }
+        }
+        {
+            const bool active = have && ind >= 0 && T >= pp.T_thr;
+            if (have) {
+                for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
+                for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
+                pp.t_min[ray] = ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY;
+                pp.T[ray] = T;
+            }
+            append_active(active, ray, pp.list_out, pp.count_out);
+        }
+    }
+done:
+    if (DEC) {
+        if (s_abort && tid == 0) atomicOr(pp.status, ERR_MBAR);
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        // flush this CTA's weight-gradient accumulators (all lanes load the same columns)
+        if (!s_first && !s_abort) {
+            const int w = tid >> 5, l = tid & 31;
+            const uint32_t lane = (uint32_t)((w * 32) << 16);
+            const int mrow = 16 * w + (l & 15);
+#pragma unroll 1
+            for (int b = 0; b < 9; ++b) {
+                float vals[16];
+                tmem_ld16(mm.tmem + lane + TM_DW + 16 * b, vals);
+                tmem_wait_ld();
+                for (int e = 0; e < 16; ++e) {
+                    const int col = 16 * b + e;
+                    const float x = vals[e] * ginv;
+                    if (l < 16) {  // half 0: dW1 row mrow, db1 at column 128
+                        if (col < 128) atomicAdd(bo.dw + DW_W1 + mrow * 128 + col, x);
+                        else if (col == 128) atomicAdd(bo.dw + DW_B1 + mrow, x);
+                    } else {       // half 1: dW2 row mrow | dW3^T row mrow | db2 | db3
+                        if (col < 64) atomicAdd(bo.dw + DW_W2 + mrow * 64 + col, x);
+                        else if (col < 68) atomicAdd(bo.dw + DW_W3 + (col - 64) * 64 + mrow, x);
+                        else if (col == 72) atomicAdd(bo.dw + DW_B2 + mrow, x);
+                        else if (col == 80 && mrow < 4) atomicAdd(bo.dw + DW_B3 + mrow, x);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid < 32) tmem_dealloc(mm.tmem, TM_BWD_COLS);
+    }
+}
+
+// ================================================================================================
+// helpers: init, gradient scale, dW packing into the reference fragment layout
+// ================================================================================================
+__global__ void init_rays_kernel(int R, float *T, float *t_min, int *list, float *med) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= R) return;
+    T[i] = 1.0f;
+    t_min[i] = 0.0f;
+    list[i] = i;
+    if (med) {
+        med[2 * (size_t)i] = INFINITY;
+        med[2 * (size_t)i + 1] = __int_as_float(-1);
+    }
+}
+
+__global__ void grad_scale_kernel(const float *dL_dI, int n3, float lambda_depth, float *scale_out) {
+    __shared__ float red[32];
+    float mx = fabsf(lambda_depth);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n3; i += gridDim.x * blockDim.x) mx = fmaxf(mx, fabsf(dL_dI[i]));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        mx = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (threadIdx.x == 0) atomicMax(reinterpret_cast<int *>(scale_out), __float_as_int(mx));
+    }
+}
+
+// max |dL/dI| (stored as float bits) -> power-of-two scale with max * scale ~ 2^4
+__global__ void grad_scale_finish_kernel(float *scale) {
+    float mx = scale[0];
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+        frexpf(mx, &e);
+        e = 4 - e;
+        e = max(-100, min(100, e));
+    }
+    scale[0] = ldexpf(1.0f, e);
+}
+
+// Adds the dense MLP gradients into row 0 of the reference's fragment-layout buffers
+// (layout decoded from train.py:754-790).
+__global__ void pack_dw_kernel(const float *dw, float *dw1, float *db1, float *dw2, float *db2, float *dw3,
+                               float *db3) {
+    int t = blockIdx.x * blockDim.x + threadIdx.x;
+    // dW1: flat[(i*16 + j)*64 + c*32 + lane] = W1g[8i + lane/4][8j + 2(lane%4) + c]
+    if (t < 8192) {
+        int lane = t & 31, c = (t >> 5) & 1, ij = t >> 6, i = ij >> 4, j = ij & 15;
+        int row = 8 * i + (lane >> 2), col = 8 * j + 2 * (lane & 3) + c;
+        if (dw1) dw1[t] += dw[DW_W1 + row * 128 + col];
+    }
+    if (t < 4096) {
+        int lane = t & 31, c = (t >> 5) & 1, ij = t >> 6, i = ij >> 3, j = ij & 7;
+        int row = 8 * i + (lane >> 2), col = 8 * j + 2 * (lane & 3) + c;
+        if (dw2) dw2[t] += dw[DW_W2 + row * 64 + col];
+    }
+    if (t < 512) {
+        int lane = t & 31, c = (t >> 5) & 1, j = t >> 6;
+        int row = lane >> 2, col = 8 * j + 2 * (lane & 3) + c;
+        if (dw3 && row < 4) dw3[t] += dw[DW_W3 + row * 64 + col];
+        // db1/db2: flat[j*64 + c*32 + lane] summed into b[8j + lane/4]; put it at c = 0, lane%4 = 0
+        if (c == 0 && (lane & 3) == 0) {
+            if (db1) db1[t] += dw[DW_B1 + 8 * j + (lane >> 2)];
+            if (db2) db2[t] += dw[DW_B2 + 8 * j + (lane >> 2)];
+        }
+    }
+    if (t < 64) {
+        int lane = t & 31, c = (t >> 5) & 1;
+        int row = lane >> 2;
+        if (db3 && c == 0 && (lane & 3) == 0 && row < 4) db3[t] += dw[DW_B3 + row];
+    }
+}
+
+// ================================================================================================
+// host drivers
+// ================================================================================================
+static SceneP scene_params(const flare_scene *sc, const float *override_colors) {
+    SceneP p;
+    p.m = sc->m; p.s = sc->s; p.q = sc->q; p.RGBA = sc->RGBA; p.k = sc->k;
+    p.cond = reinterpret_cast<const uint4 *>(sc->cond);
+    p.features = sc->features;
+    p.A1 = reinterpret_cast<const __half *>(sc->A1);
+    p.A2 = reinterpret_cast<const __half *>(sc->A2);
+    p.A3 = reinterpret_cast<const __half *>(sc->A3);
+    p.b1 = sc->b1; p.b2 = sc->b2; p.b3 = sc->b3;
+    p.override_colors = override_colors;
+    p.n = sc->n;
+    return p;
+}
+
+template <bool DEC, int MODE>
+static int launch_fwd(flare_renderer *r, const SceneP &sp, const PassP &pp, const FwdOut &fo, cudaStream_t st) {
+    auto kern = shade_fwd_kernel<DEC, MODE>;
+    int smem = DEC ? SM_FWD_BYTES : 0;
+    if (DEC) FLARE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int chunks = (pp.count + 127) / 128;
+    int grid = DEC ? std::min(chunks, r->num_sms * 2) : chunks;
+    kern<<<grid, 128, smem, st>>>(sp, pp, fo);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+template <bool DEC>
+static int launch_fwd_mode(flare_renderer *r, int mode, const SceneP &sp, const PassP &pp, const FwdOut &fo,
+                           cudaStream_t st) {
+    switch (mode) {
+        case FLARE_FWD_TRAINING: return launch_fwd<DEC, FLARE_FWD_TRAINING>(r, sp, pp, fo, st);
+        case FLARE_FWD_INFERENCE: return launch_fwd<DEC, FLARE_FWD_INFERENCE>(r, sp, pp, fo, st);
+        case FLARE_FWD_INFERENCE_GEOMETRY: return launch_fwd<DEC, FLARE_FWD_INFERENCE_GEOMETRY>(r, sp, pp, fo, st);
+        case FLARE_FWD_PCA: return launch_fwd<DEC, FLARE_FWD_PCA>(r, sp, pp, fo, st);
+        case FLARE_FWD_MEDIAN: return launch_fwd<DEC, FLARE_FWD_MEDIAN>(r, sp, pp, fo, st);
+    }
+    set_error("unknown forward mode %d", mode);
+    return FLARE_E_INVALID;
+}
+
+// Runs the pass loop: trace -> shade -> compaction, until no ray is active.
+template <typename ShadeFn>
+static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, cudaStream_t st, ShadeFn shade) {
+    int count = R;
+    int cur = 0;
+    long long passes = 0;
+    const long long max_passes = (long long)(r->n / K_HITS) + 4;
+    while (count > 0) {
+        if (passes > max_passes) {
+            set_error("pass loop did not terminate after %lld passes", passes);
+            return FLARE_E_DEVICE;
+        }
+        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, r->hit_t, r->hit_idx, count, st);
+        if (e) return e;
+        FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
+        e = shade(r->list[cur], count, r->list[cur ^ 1]);
+        if (e) return e;
+        FLARE_CUDA_TRY(cudaMemcpyAsync(r->h_count, r->counters, sizeof(int), cudaMemcpyDeviceToHost, st));
+        FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+        count = *r->h_count;
+        cur ^= 1;
+        ++passes;
+    }
+    unsigned long long p = (unsigned long long)passes;
+    FLARE_CUDA_TRY(cudaMemcpyAsync(r->dstats + ST_PASSES, &p, sizeof(p), cudaMemcpyHostToDevice, st));
+    FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+    return FLARE_OK;
+}
+
+static PassP make_pass(flare_renderer *r, const float *O, const float *v, float bg0, float bg1, float bg2,
+                       float T_thr) {
+    PassP pp{};
+    pp.O = O; pp.v = v;
+    pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
+    pp.T = r->T; pp.t_min = r->t_min;
+    pp.count_out = r->counters;
+    pp.status = r->dstatus;
+    pp.stats = r->dstats;
+    pp.bg0 = bg0; pp.bg1 = bg1; pp.bg2 = bg2;
+    pp.T_thr = T_thr;
+    return pp;
+}
+
+int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st) {
+    const int R = a->n_rays;
+    if (R <= 0) return FLARE_OK;
+    const bool dec = sc->cond != nullptr;
+    SceneP sp = scene_params(sc, a->override_colors);
+    FwdOut fo{};
+    fo.bitmap = a->bitmap; fo.dacc = a->depth_reg_accums; fo.nacc = a->normal_reg_accums;
+    fo.normal = a->normal; fo.alpha = a->alpha; fo.edn = a->expected_depth_numerator;
+    fo.med = a->depth_and_index; fo.surface_normal = a->surface_normal;
+    fo.reg_a = a->reg_a; fo.reg_b = a->reg_b;
+    init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0],
+                                                       a->mode == FLARE_FWD_MEDIAN ? a->depth_and_index : nullptr);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
+    return pass_loop(r, a->O, a->v, R, st, [&](const int *lin, int count, int *lout) -> int {
+        PassP pp = base;
+        pp.list_in = lin;
+        pp.count = count;
+        pp.list_out = lout;
+        return dec ? launch_fwd_mode<true>(r, a->mode, sp, pp, fo, st) : launch_fwd_mode<false>(r, a->mode, sp, pp, fo, st);
+    });
+}
+
+int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st) {
+    const int R = a->n_rays;
+    if (R <= 0) return FLARE_OK;
+    const bool dec = sc->cond != nullptr;
+    SceneP sp = scene_params(sc, nullptr);
+    BwdIO bo{};
+    bo.I = a->I; bo.dL_dI = a->dL_dI;
+    bo.dRGB = a->dL_dRGB; bo.dA = a->dL_dA; bo.dk = a->dL_dk; bo.dm = a->dL_dm; bo.ds = a->dL_ds; bo.dq = a->dL_dq;
+    bo.dcond = a->dL_dcond; bo.dfeat = a->dL_dfeatures;
+    bo.dw = r->dw;
+    bo.dacc = a->depth_reg_accums; bo.prefix = a->depth_normal_reg_prefix_sums;
+    bo.surface_normal = a->surface_normal;
+    bo.lambda_depth = a->lambda_depth; bo.reg_a = a->reg_a; bo.reg_b = a->reg_b; bo.lambda_normal = a->lambda_normal;
+    bo.gscale = r->gscale;
+    init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    if (dec) {
+        FLARE_CUDA_TRY(cudaMemsetAsync(r->dw, 0, DW_TOTAL * sizeof(float), st));
+        FLARE_CUDA_TRY(cudaMemsetAsync(r->gscale, 0, sizeof(float), st));
+        grad_scale_kernel<<<std::min((3 * R + 255) / 256, 1024), 256, 0, st>>>(a->dL_dI, 3 * R, a->lambda_depth,
+                                                                             r->gscale);
+        grad_scale_finish_kernel<<<1, 1, 0, st>>>(r->gscale);
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            SM_BWD_BYTES));
+    }
+    PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
+    int e = pass_loop(r, a->O, a->v, R, st, [&](const int *lin, int count, int *lout) -> int {
+        PassP pp = base;
+        pp.list_in = lin;
+        pp.count = count;
+        pp.list_out = lout;
+        int chunks = (count + 127) / 128;
+        if (dec) {
+            int grid = std::min(chunks, r->num_sms * 2);
+            shade_bwd_kernel<true><<<grid, 128, SM_BWD_BYTES, st>>>(sp, pp, bo);
+        } else {
+            shade_bwd_kernel<false><<<chunks, 128, 0, st>>>(sp, pp, bo);
+        }
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    });
+    if (e) return e;
+    if (dec) {
+        pack_dw_kernel<<<32, 256, 0, st>>>(r->dw, a->dL_dw1, a->dL_db1, a->dL_dw2, a->dL_db2, a->dL_dw3, a->dL_db3);
+        FLARE_CUDA_TRY(cudaGetLastError());
+    }
+    return FLARE_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// self-test: the forward MLP tile on caller-provided rows
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) selftest_mlp_kernel(const uint4 *X, int rows, SceneP sc, float *Y, int *status) {
+    extern __shared__ __align__(1024) char smem[];
+    __shared__ int s_abort;
+    const int tid = threadIdx.x;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SM_FWD_MISC + 8);
+    if (tid == 0) {
+        mbar_init(smem + SM_FWD_MISC, 1);
+        fence_mbar_init();
+        s_abort = 0;
+    }
+    if (tid < 32) tmem_alloc(tmem_slot, TM_FWD_COLS);
+    load_decoder(smem, sc, false);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    Mma mm{*tmem_slot, 0u, smem + SM_FWD_MISC, &s_abort};
+    char *tile = smem + SM_FWD_TILE;
+    for (int base = blockIdx.x * 128; base < rows; base += gridDim.x * 128) {
+        int row = base + tid;
+        uint4 *T = reinterpret_cast<uint4 *>(tile);
+        for (int kc = 0; kc < 16; ++kc) T[kc * 128 + tid] = row < rows ? X[(size_t)row * 16 + kc] : make_uint4(0, 0, 0, 0);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        float y4[4];
+        mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, nullptr);
+        __syncthreads();
+        if (s_abort) break;
+        if (row < rows)
+            for (int o = 0; o < 16; ++o) Y[(size_t)row * 16 + o] = o < 4 ? y4[o] : 0.0f;
+    }
+    if (s_abort && tid == 0) atomicOr(status, ERR_MBAR);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid < 32) tmem_dealloc(mm.tmem, TM_FWD_COLS);
+}
+
+int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
+                 const void *A3, const float *b3, float *Y, cudaStream_t st, int *status) {
+    if (rows <= 0) return FLARE_OK;
+    SceneP sp{};
+    sp.A1 = reinterpret_cast<const __half *>(A1);
+    sp.A2 = reinterpret_cast<const __half *>(A2);
+    sp.A3 = reinterpret_cast<const __half *>(A3);
+    sp.b1 = b1; sp.b2 = b2; sp.b3 = b3;
+    FLARE_CUDA_TRY(cudaFuncSetAttribute(selftest_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_FWD_BYTES));
+    int grid = std::max(1, std::min((rows + 127) / 128, 148));
+    selftest_mlp_kernel<<<grid, 128, SM_FWD_BYTES, st>>>(reinterpret_cast<const uint4 *>(X), rows, sp, Y, status);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+}  // namespace flare

@@ -1,0 +1,190 @@
+/*
+ * flare_b200.h -- C ABI of the B200-native FlaRe render path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream handle (cudaStream_t passed
+ * as void*; NULL means the legacy default stream), returns 0 on success and a non-zero FLARE_E_* code
+ * on failure, and leaves a human-readable message in a thread-local buffer read by
+ * flare_last_error().  No entry point synchronises the device except where stated; results are
+ * ready when the stream has drained.
+ *
+ * The entry points replace the methods of the reference PyTorch extension `PYOPTIXFLARERENDERER`
+ * (source/renderer/PyOptiXFLARERenderer.cpp:12-74 binds them, source/renderer/CPyOptiXFLARERenderer.h
+ * declares them).  Each declaration below names the reference method(s) it stands in for.
+ *
+ * Tensor layouts follow the reference exactly (all contiguous, row-major):
+ *   rays      O, v            (R,3)  f32      one origin / direction per ray
+ *   geometry  m (N,3) f32, s (N,2) f32 log-scale, q (N,4) f32 (w,x,y,z order as stored, unnormalised),
+ *             RGBA (N,4) f32 = [base RGB, opacity logit], k (N,1) f32 raw shape (kappa = 1 + softplus(k))
+ *   decoder   cond (N,96) f16, features (13154) f32 LUT, A1 (64,128) f16, b1 (64) f32,
+ *             A2 (64,64) f16, b2 (64) f32, A3 (16,64) f16, b3 (16) f32
+ * Outputs are accumulated (+=) into caller-zeroed buffers, as in the reference, except where stated.
+ */
+#ifndef FLARE_B200_H
+#define FLARE_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FLARE_OK 0
+#define FLARE_E_INVALID 1   /* bad argument (null pointer, size out of range) */
+#define FLARE_E_CUDA 2      /* a CUDA runtime call failed */
+#define FLARE_E_DEVICE 3    /* a kernel reported an error through the device status word */
+#define FLARE_E_STATE 4     /* call made in the wrong state (e.g. render before SetGeometry) */
+
+#define FLARE_HIT_BUFFER_SIZE 16 /* k of the k-nearest hit buffer (reference constants.h:2) */
+#define FLARE_LUT_SIZE 13154     /* 2 * (16^2 + 25^2 + 40^2 + 64^2), reference Forward_training.cu:608 */
+#define FLARE_COND_DIM 96        /* reference Forward_training.cu:32 */
+
+typedef struct flare_renderer flare_renderer;
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char *flare_last_error(void);
+
+/* Library version string. */
+const char *flare_version(void);
+
+/*
+ * Replaces CPyOptiXFLARERenderer::CPyOptiXFLARERenderer(number_of_sides, chi_square_squared_radius,
+ * max_batch_size) (CPyOptiXFLARERenderer.cpp:10-15 -> CPyOptiXFLARERenderer_CUDA_Core.cu:43-526).
+ * Scratch for max_batch_size rays is allocated here, on `device`.  number_of_sides in [3, 64].
+ * chi_square_squared_radius is stored but, as in the reference (Core.cu:583), the proxy radius uses
+ * the constant 11.3449.
+ */
+int flare_create(int number_of_sides, float chi_square_squared_radius, int max_batch_size, int device,
+                 flare_renderer **out);
+
+/* Frees everything the renderer owns.  Accepts NULL. */
+int flare_destroy(flare_renderer *r);
+
+/*
+ * Replaces CPyOptiXFLARERenderer::SetGeometry(m, scale, q, opacity, kappa)
+ * (CPyOptiXFLARERenderer.cpp:19-30 -> Core.cu:687-816).  Inputs are the ACTIVATED parameters, as the
+ * reference callers pass them (train.py:449): scale = exp(s) (N,2), opacity = sigmoid(A) (N),
+ * kappa = 1 + softplus(k) (N).  Builds the polygon frames and the LBVH on `stream`.
+ */
+int flare_set_geometry(flare_renderer *r, const float *m, const float *scale, const float *q,
+                       const float *opacity, const float *kappa, int n, void *stream);
+
+/*
+ * Replaces CPyOptiXFLARERenderer::Render(O, v, t_min, size) (CPyOptiXFLARERenderer.cpp:34-61 ->
+ * Core.cu:820-858 -> shaders.cu:19-77): for each ray, the 16 nearest proxy hits with t >= t_min[ray],
+ * ascending by (t, primitive index).  t_out and idx_out are (16, n_rays) slot-major; unused slots
+ * hold t = +inf, idx = -1.
+ */
+int flare_render_hits(flare_renderer *r, const float *O, const float *v, const float *t_min, int n_rays,
+                      float *t_out, int *idx_out, void *stream);
+
+/*
+ * Replaces the module function GenerateRays(R, D, F, width, height, fov_x, fov_y)
+ * (GenerateRays.cpp:6-28 -> GenerateRays.cu:6-72): out (H*W, 3) f32, v = R*dx + D*dy + F, not
+ * normalised.
+ */
+int flare_generate_rays(const float *R, const float *D, const float *F, int width, int height, float fov_x,
+                        float fov_y, float *out, void *stream);
+
+/* Which forward product a flare_forward call computes. */
+enum flare_forward_mode {
+    FLARE_FWD_TRAINING = 0,           /* Forward_training(_base): RGB + depth/normal-reg accumulators */
+    FLARE_FWD_INFERENCE = 1,          /* Forward_inference(_base): RGB */
+    FLARE_FWD_INFERENCE_GEOMETRY = 2, /* Forward_inference(_base)_with_geometry: RGB, normal, alpha, E[t] numerator */
+    FLARE_FWD_PCA = 3,                /* Forward_pca: RGB from override colours */
+    FLARE_FWD_MEDIAN = 4              /* GetMedianDepth(_base): (t, idx) of the last hit with T > 0.5 */
+};
+
+/* Scene parameters shared by forward and backward.  Decoder pointers are NULL for the base model. */
+typedef struct flare_scene {
+    const float *m, *s, *q, *RGBA, *k;       /* (N,3) (N,2) (N,4) (N,4) (N,1) raw parameters */
+    int n;                                   /* N; must equal the N of the last flare_set_geometry */
+    const void *cond;                        /* (N,96) f16 or NULL (base model) */
+    const float *features;                   /* (13154) f32 LUT */
+    const void *A1, *A2, *A3;                /* f16 weights (64,128) (64,64) (16,64) */
+    const float *b1, *b2, *b3;               /* f32 biases (64) (64) (16) */
+} flare_scene;
+
+typedef struct flare_forward_args {
+    int mode;                                /* enum flare_forward_mode */
+    const float *O, *v;                      /* (R,3) */
+    int n_rays;
+    float bg[3];
+    float T_threshold;
+    float *bitmap;                           /* (R,3) accumulated; not used by MEDIAN */
+    /* TRAINING */
+    float *depth_reg_accums;                 /* (R,4) (L_d, sum w, sum w t~, sum w t) accumulated */
+    float reg_a, reg_b;
+    float *depth_and_index;                  /* (R,2): MEDIAN output; unused by TRAINING (as in reference) */
+    const float *surface_normal;             /* (R,3) normal-reg target, zero vector = no target */
+    float *normal_reg_accums;                /* (R,4) .x accumulated */
+    /* INFERENCE_GEOMETRY (each may be NULL) */
+    float *normal;                           /* (R,3) accumulated */
+    float *alpha;                            /* (R) written: 1 - T */
+    float *expected_depth_numerator;         /* (R) accumulated */
+    /* PCA */
+    const float *override_colors;            /* (N,3) */
+} flare_forward_args;
+
+/*
+ * Replaces CPyOptiXFLARERenderer::{Forward_training, Forward_inference, Forward_pca,
+ * Forward_inference_with_geometry, GetMedianDepth} (CPyOptiXFLARERenderer.cpp:451-720 ->
+ * *_Forward_training.cu:949-1132, *_Forward_inference.cu:932-1104, *_GetMedianDepth.cu:882-1046) when
+ * scene->cond != NULL, and their _base twins (CPyOptiXFLARERenderer.cpp:66-450 ->
+ * *_Forward_training_base.cu, *_Forward_inference_base.cu, *_GetMedianDepth_base.cu) when it is NULL.
+ */
+int flare_forward(flare_renderer *r, const flare_scene *scene, const flare_forward_args *a, void *stream);
+
+typedef struct flare_backward_args {
+    const float *O, *v;                      /* (R,3) */
+    int n_rays;
+    float bg[3];
+    float T_threshold;
+    float *I;                                /* (R,3) final (clamped) image; OVERWRITTEN, as in reference */
+    const float *dL_dI;                      /* (R,3) */
+    /* gradients, accumulated (+=) into caller-zeroed buffers */
+    float *dL_dRGB, *dL_dA, *dL_dk, *dL_dm, *dL_ds, *dL_dq;   /* (N,3) (N,1) (N,1) (N,3) (N,2) (N,4) */
+    float *dL_dcond;                         /* (N,96) f32 (decoder only) */
+    float *dL_dfeatures;                     /* (13154) f32 (decoder only) */
+    /* MLP weight gradients in the reference's per-warp fragment layout (train.py:704-790); the fully
+       reduced gradient is added into row 0, other rows are untouched.  Sizes in floats per row:
+       dw1 8192, db1 512, dw2 4096, db2 512, dw3 512, db3 64. */
+    float *dL_dw1, *dL_db1, *dL_dw2, *dL_db2, *dL_dw3, *dL_db3;
+    /* regularisers (reference Backward.cu:1753-1817) */
+    const float *depth_reg_accums;           /* (R,4) from the forward */
+    float *depth_normal_reg_prefix_sums;     /* (R,4) caller-zeroed scratch (written) */
+    float lambda_depth, reg_a, reg_b;
+    const float *surface_normal;             /* (R,3) */
+    float lambda_normal;
+} flare_backward_args;
+
+/*
+ * Replaces CPyOptiXFLARERenderer::Backward (CPyOptiXFLARERenderer.cpp:722-873 ->
+ * *_Backward.cu:2238-2453) when scene->cond != NULL and Backward_base
+ * (CPyOptiXFLARERenderer.cpp:345-450 -> *_Backward_base.cu:641-804) when it is NULL.
+ */
+int flare_backward(flare_renderer *r, const flare_scene *scene, const flare_backward_args *a, void *stream);
+
+/* Statistics of the last forward/backward call (counted on the device; reading them synchronises the
+   stream of that call): rays, passes, composited hits, primitive tests, BVH node visits. */
+typedef struct flare_stats {
+    long long rays, passes, hits_composited, prim_tests, node_visits;
+} flare_stats;
+int flare_get_stats(flare_renderer *r, flare_stats *out);
+
+/*
+ * Exposes the per-primitive polygon frames built by the last flare_set_geometry, for the bit-exact
+ * hit-list test: frames (N,12) f32 = [m.xyz, N.xyz, U/(e^sx rho).xyz, V/(e^sy rho).xyz] in primitive
+ * order.  Device pointer to caller storage; synchronous on `stream`.
+ */
+int flare_get_frames(flare_renderer *r, float *frames_out, void *stream);
+
+/*
+ * Decoder self-test: runs the renderer's tensor-core MLP on `rows` fp16 input rows X (rows,128) and
+ * writes the 16 fp32 layer-3 outputs per row to Y (rows,16).  Used by the tests to check the MLP
+ * tiles against a host reference independently of tracing.
+ */
+int flare_selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2,
+                       const float *b2, const void *A3, const float *b3, float *Y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLARE_B200_H */

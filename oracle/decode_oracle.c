@@ -1,0 +1,269 @@
+/*
+ * decode_oracle.c -- CPU restatement of FlaRe's per-hit decode and front-to-back compositing.
+ *
+ * TEST INFRASTRUCTURE ONLY (checker and timed CPU baseline).  The product never links or calls it.
+ *
+ * Restates, per composited hit (reference paths relative to the FlaRe repository,
+ * source/renderer/CPyOptiXFLARERenderer_CUDA_*.cu):
+ *   - local coordinates (u, w) = e^-s * [U; V] . (O + t v - m)            Forward_training.cu:719-777
+ *   - 4-level dense LUT encoding of 0.2968928 * (u, w), res {16,25,40,64}  Forward_training.cu:114-194,240-263
+ *   - sin/cos view-direction encoding, 4 octaves                           Forward_training.cu:198-209,266-280
+ *   - decoder input order [LUT 8 | PE 24 | descriptor 96], fp16            Forward_training.cu:213-292
+ *   - MLP 128->64->64->16, Hardswish, fp16 activations, fp32 accumulate     Forward_training.cu:296-493
+ *   - colour = RGB_base * relu(y[0:3]); alpha = sigma(A) G(r) sigmoid(y3)   Forward_training.cu:846-878
+ *   - compositing while T >= T_thr, background at termination               Forward_training.cu:854-928
+ *   - depth / normal regulariser accumulators                              Forward_training.cu:884-908
+ *   - inference geometry outputs and override colours                      Forward_inference.cu:866-917
+ *   - median depth (last hit while T > 0.5)                                GetMedianDepth.cu:852-867
+ *   - base model (constant colour, alpha = sigma(A) G(r))                  Forward_training_base.cu:21-257
+ * Transcendentals use libm (expf, logf, powf, sinf, cosf); the reference's fast intrinsics differ by a
+ * few ulp, far inside the 1e-3 parity tolerance.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#define K_HITS 16
+#define LUT_SCALE 0.29689279887990428378374198030042f
+
+enum { M_TRAIN = 0, M_INFER = 1, M_GEOM = 2, M_PCA = 3, M_MEDIAN = 4 };
+
+typedef struct {
+    const float *m, *s, *q, *RGBA, *k;
+    const _Float16 *cond; /* NULL = base model */
+    const float *features;
+    const _Float16 *A1, *A2, *A3;
+    const float *b1, *b2, *b3;
+    const float *override_colors;
+} oscene;
+
+typedef struct {
+    int mode;
+    float bg[3];
+    float T_thr, reg_a, reg_b;
+} oparams;
+
+/* Per-ray state carried across passes (the reference keeps these in the output buffers). */
+typedef struct {
+    float T;
+    float rgb[3];
+    float dacc[4];     /* depth_reg_accums */
+    float nacc[4];     /* normal_reg_accums */
+    float normal[3];
+    float edn;         /* expected depth numerator */
+    float med_t;
+    int med_idx;
+    int hits;          /* composited hits (statistics) */
+} oray;
+
+static inline float sat(float x) { return x < 0.0f ? 0.0f : (x > 1.0f ? 1.0f : x); }
+static inline float hswish(float y) {
+    float c = y + 3.0f;
+    c = c < 0.0f ? 0.0f : (c > 6.0f ? 6.0f : c);
+    return (y * c) * (1.0f / 6.0f);
+}
+
+static const int lut_res[4] = {16, 25, 40, 64};
+static const int lut_off[4] = {0, 256, 881, 2481}; /* in float2 units */
+
+static void lut_encode(const float *features, float cu, float cw, float *out8) {
+    for (int l = 0; l < 4; ++l) {
+        int R = lut_res[l];
+        float xs = sat((cu + 1.0f) * 0.5f), ys = sat((cw + 1.0f) * 0.5f);
+        float scale = (float)R - 1.0f;
+        float px = xs * scale, py = ys * scale;
+        int ix = (int)floorf(px), iy = (int)floorf(py);
+        if (ix > R - 2) ix = R - 2;
+        if (iy > R - 2) iy = R - 2;
+        float fx = px - (float)ix, fy = py - (float)iy;
+        const float *F = features + 2 * lut_off[l];
+        for (int f = 0; f < 2; ++f) {
+            float f00 = F[2 * (iy * R + ix) + f], f10 = F[2 * (iy * R + ix + 1) + f];
+            float f01 = F[2 * ((iy + 1) * R + ix) + f], f11 = F[2 * ((iy + 1) * R + ix + 1) + f];
+            float r0 = fmaf(f00, 1.0f - fx, f10 * fx);
+            float r1 = fmaf(f01, 1.0f - fx, f11 * fx);
+            out8[2 * l + f] = fmaf(r0, 1.0f - fy, r1 * fy);
+        }
+    }
+}
+
+/* Decoder: returns y[0..3] (pre-activation outputs 0..3 of layer 3). */
+static void decode(const oscene *S, int idx, float cu, float cw, const float *v, float *y4) {
+    float x[128];
+    float lut[8];
+    lut_encode(S->features, cu, cw, lut);
+    for (int i = 0; i < 8; ++i) x[i] = (float)(_Float16)lut[i];
+    for (int a = 0; a < 3; ++a)
+        for (int f = 0; f < 4; ++f) {
+            float arg = (float)M_PI * (float)(1 << f) * v[a];
+            x[8 + 8 * a + 2 * f] = (float)(_Float16)sinf(arg);
+            x[9 + 8 * a + 2 * f] = (float)(_Float16)cosf(arg);
+        }
+    for (int j = 0; j < 96; ++j) x[32 + j] = (float)S->cond[(long)idx * 96 + j];
+    float h1[64], h2[64];
+    for (int o = 0; o < 64; ++o) {
+        float acc = S->b1[o];
+        for (int kk = 0; kk < 128; ++kk) acc = fmaf((float)S->A1[o * 128 + kk], x[kk], acc);
+        h1[o] = (float)(_Float16)hswish(acc);
+    }
+    for (int o = 0; o < 64; ++o) {
+        float acc = S->b2[o];
+        for (int kk = 0; kk < 64; ++kk) acc = fmaf((float)S->A2[o * 64 + kk], h1[kk], acc);
+        h2[o] = (float)(_Float16)hswish(acc);
+    }
+    for (int o = 0; o < 4; ++o) {
+        float acc = S->b3[o];
+        for (int kk = 0; kk < 64; ++kk) acc = fmaf((float)S->A3[o * 64 + kk], h2[kk], acc);
+        y4[o] = acc;
+    }
+}
+
+/* Shades one pass (up to 16 hits, ascending t) of one ray.  Returns 1 if the ray stays active.
+   `last_valid` is whether slot 16 held a hit (reference: is_active = ind16 != -1 && T >= thr). */
+static int shade_pass(const oscene *S, const oparams *P, const float *O, const float *v, const float *ts,
+                      const int *ids, int nh, const float *surface_normal, oray *st, int *count) {
+    float T = st->T;
+    int last_valid = (nh == K_HITS) && ids[K_HITS - 1] >= 0;
+    float Nm[3] = {0, 0, 0};
+    int nvalid = 0;
+    if (surface_normal) {
+        Nm[0] = surface_normal[0]; Nm[1] = surface_normal[1]; Nm[2] = surface_normal[2];
+        nvalid = fmaf(Nm[0], Nm[0], fmaf(Nm[1], Nm[1], Nm[2] * Nm[2])) > 0.0f;
+    }
+    for (int h = 0; h < nh; ++h) {
+        int idx = ids[h];
+        if (idx < 0) break;
+        int median = P->mode == M_MEDIAN;
+        if (!(T >= P->T_thr) || (median && !(T > 0.5f))) break;
+        float t = ts[h];
+        const float *q = S->q + 4 * idx;
+        float sx = expf(-S->s[2 * idx]), sy = expf(-S->s[2 * idx + 1]);
+        float aa = q[0] * q[0], bb = q[1] * q[1], cc = q[2] * q[2], dd = q[3] * q[3];
+        float Sq = 2.0f / (aa + bb + cc + dd);
+        float bs = q[1] * Sq, cs = q[2] * Sq, ds = q[3] * Sq;
+        float ab = q[0] * bs, ac = q[0] * cs, ad = q[0] * ds;
+        bb = bb * Sq;
+        float bc = q[1] * cs, bd = q[1] * ds;
+        cc = cc * Sq;
+        float cd = q[2] * ds;
+        dd = dd * Sq;
+        float Q11 = sx * (1.0f - cc - dd), Q12 = sx * (bc + ad), Q13 = sx * (bd - ac);
+        float Q21 = sy * (bc - ad), Q22 = sy * (1.0f - bb - dd), Q23 = sy * (cd + ab);
+        float N1 = bd + ac, N2 = cd - ab, N3 = 1.0f - bb - cc;
+        float kap = 1.0f + logf(1.0f + expf(S->k[idx]));
+        float kinv = 1.0f / kap;
+        const float *m = S->m + 3 * idx;
+        float dx = fmaf(v[0], t, O[0]) - m[0], dy = fmaf(v[1], t, O[1]) - m[1], dz = fmaf(v[2], t, O[2]) - m[2];
+        float u = fmaf(Q11, dx, fmaf(Q12, dy, Q13 * dz));
+        float w = fmaf(Q21, dx, fmaf(Q22, dy, Q23 * dz));
+        const float *rgba = S->RGBA + 4 * idx;
+        float sig_y = 1.0f, crgb[3] = {rgba[0], rgba[1], rgba[2]};
+        if (S->cond) {
+            float y[4];
+            decode(S, idx, u * LUT_SCALE, w * LUT_SCALE, v, y);
+            sig_y = 1.0f / (1.0f + expf(-y[3]));
+            for (int c = 0; c < 3; ++c) crgb[c] = rgba[c] * (y[c] > 0.0f ? y[c] : 0.0f);
+        }
+        if (P->mode == M_PCA && S->override_colors)
+            for (int c = 0; c < 3; ++c) crgb[c] = S->override_colors[3 * idx + c];
+        float opa1 = 1.0f / (1.0f + expf(-rgba[3]));
+        float r2 = fmaf(u, u, w * w);
+        float pk = powf(r2, kap - 1.0f);
+        if (isnan(pk)) pk = 0.0f;
+        float r2k = r2 * pk;
+        float alpha = opa1 * expf(-0.5f * kinv * r2k) * sig_y;
+        float o = T * alpha;
+        (*count)++;
+        st->hits++;
+        if (median) {
+            st->med_t = t;
+            st->med_idx = idx;
+            T = T - o;
+            continue;
+        }
+        for (int c = 0; c < 3; ++c) st->rgb[c] = fmaf(crgb[c], o, st->rgb[c]);
+        float sgn = (fmaf(N1, v[0], fmaf(N2, v[1], N3 * v[2])) > 0.0f) ? -1.0f : 1.0f;
+        if (P->mode == M_GEOM) {
+            st->normal[0] = fmaf(sgn * N1, o, st->normal[0]);
+            st->normal[1] = fmaf(sgn * N2, o, st->normal[1]);
+            st->normal[2] = fmaf(sgn * N3, o, st->normal[2]);
+            st->edn = fmaf(t, o, st->edn);
+        }
+        T = T - o;
+        if (P->mode == M_TRAIN) {
+            float tt = sat(P->reg_a / t + P->reg_b);
+            float oacc = st->dacc[1], toacc = st->dacc[2];
+            float Ld = o * fmaf(tt, oacc, -toacc);
+            st->dacc[0] = fmaf(4.0f, Ld, st->dacc[0]);
+            st->dacc[1] = oacc + o;
+            st->dacc[2] = fmaf(tt, o, toacc);
+            st->dacc[3] = fmaf(t, o, st->dacc[3]);
+            float nd = sgn * fmaf(Nm[0], N1, fmaf(Nm[1], N2, Nm[2] * N3));
+            if (nvalid) st->nacc[0] += o * (1.0f - nd);
+        }
+    }
+    st->T = T;
+    int active = last_valid && (T >= P->T_thr);
+    if (P->mode == M_MEDIAN) active = active && (T > 0.5f);
+    return active;
+}
+
+static void finish_ray(const oparams *P, oray *st) {
+    if (P->mode == M_MEDIAN) return;
+    for (int c = 0; c < 3; ++c) st->rgb[c] = fmaf(P->bg[c], st->T, st->rgb[c]);
+}
+
+/*
+ * Forward over per-ray hit lists in CSR form: ray r's hits, ascending in t, are hit_t/hit_idx
+ * [off[r], off[r+1]), grouped in passes of 16 (a pass that ends with fewer than 16 entries, or a
+ * trailing -1, ends the ray).  Outputs (all may be NULL except rgb):
+ *   rgb (R,3), dacc (R,4), nacc (R,4), normal (R,3), alpha (R), edn (R), med (R,2 floats: t, idx bits),
+ *   Tout (R), nhits (R).
+ * Returns the total number of composited hits.
+ */
+long oracle_shade_csr(const float *m, const float *s, const float *q, const float *RGBA, const float *k,
+                      const void *cond, const float *features, const void *A1, const float *b1, const void *A2,
+                      const float *b2, const void *A3, const float *b3, const float *override_colors, int mode,
+                      const float *bg, float T_thr, float reg_a, float reg_b, const float *O, const float *v,
+                      const float *surface_normal, int R, const long *off, const float *hit_t,
+                      const int *hit_idx, float *rgb, float *dacc, float *nacc, float *normal, float *alpha,
+                      float *edn, float *med, float *Tout, int *nhits) {
+    oscene S = {m, s, q, RGBA, k, (const _Float16 *)cond, features, (const _Float16 *)A1, (const _Float16 *)A2,
+                (const _Float16 *)A3, b1, b2, b3, override_colors};
+    oparams P;
+    P.mode = mode;
+    P.bg[0] = bg[0]; P.bg[1] = bg[1]; P.bg[2] = bg[2];
+    P.T_thr = T_thr; P.reg_a = reg_a; P.reg_b = reg_b;
+    long total = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : total)
+    for (int r = 0; r < R; ++r) {
+        oray st;
+        memset(&st, 0, sizeof(st));
+        st.T = 1.0f;
+        st.med_t = INFINITY;
+        st.med_idx = -1;
+        int cnt = 0;
+        long b = off[r], e = off[r + 1];
+        for (long p = b; p < e; p += K_HITS) {
+            int nh = (int)((e - p) < K_HITS ? (e - p) : K_HITS);
+            int act = shade_pass(&S, &P, O + 3 * r, v + 3 * r, hit_t + p, hit_idx + p, nh,
+                                 surface_normal ? surface_normal + 3 * r : NULL, &st, &cnt);
+            if (!act) break;
+        }
+        finish_ray(&P, &st);
+        total += cnt;
+        for (int c = 0; c < 3; ++c) rgb[3 * r + c] = st.rgb[c];
+        if (dacc) for (int c = 0; c < 4; ++c) dacc[4 * r + c] = st.dacc[c];
+        if (nacc) for (int c = 0; c < 4; ++c) nacc[4 * r + c] = st.nacc[c];
+        if (normal) for (int c = 0; c < 3; ++c) normal[3 * r + c] = st.normal[c];
+        if (alpha) alpha[r] = 1.0f - st.T;
+        if (edn) edn[r] = st.edn;
+        if (med) {
+            med[2 * r] = st.med_t;
+            memcpy(&med[2 * r + 1], &st.med_idx, 4);
+        }
+        if (Tout) Tout[r] = st.T;
+        if (nhits) nhits[r] = st.hits;
+    }
+    return total;
+}

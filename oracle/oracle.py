@@ -1,0 +1,161 @@
+"""CPU oracle for the FlaRe render path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs import this module,
+and only as the checker or the timed CPU baseline.  The product package (flare_b200/) never imports it.
+
+Pieces (see the headers of trace_oracle.c and decode_oracle.c for the reference lines restated):
+  prep_frames      proxy frames from SetGeometry inputs          (Core.cu:553-622)
+  hits             16-nearest hits beyond t_min, brute force     (shaders.cu:145-189)
+  hit_lists        the multi-pass restart loop -> per-ray CSR    (Forward_training.cu:1004-1131)
+  forward          decode + composite over CSR hit lists         (Forward_*.cu, GetMedianDepth*.cu)
+Gradients are in grad_oracle.py (torch autograd in float64).
+
+Parity status: the reference needs the closed OptiX SDK and a GPU, so it cannot be run here; the hit
+test (octagon proxy) is pinned by analytic known-answer scenes and the LUT by the reference's own
+Python LUT level (scripts/encoding_2d_benchmark.py:107-163), see tests/golden/make_golden.py.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+K = 16
+MODES = {"training": 0, "inference": 1, "geometry": 2, "pca": 3, "median": 4}
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB):
+            build()
+        _lib = ctypes.CDLL(_LIB)
+        _lib.oracle_shade_csr.restype = ctypes.c_long
+        _lib.oracle_next_tmin.restype = ctypes.c_float
+        _lib.oracle_next_tmin.argtypes = [ctypes.c_float]
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _f32(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def _np(t, dtype=None):
+    """torch tensor or array -> contiguous numpy (float32 unless dtype given)."""
+    if hasattr(t, "detach"):
+        t = t.detach().cpu().numpy()
+    return np.ascontiguousarray(t if dtype is None else np.asarray(t, dtype=dtype))
+
+
+def polygon_constants(nsides=8):
+    c = np.zeros(nsides, np.float32)
+    s = np.zeros(nsides, np.float32)
+    lib().oracle_polygon_constants(ctypes.c_int(nsides), _p(c), _p(s))
+    return c, s
+
+
+def prep_frames(m, scale, q, opacity, kappa):
+    m, scale, q, opacity, kappa = (_f32(_np(x)) for x in (m, scale, q, opacity, kappa))
+    n = m.shape[0]
+    out = np.zeros((n, 12), np.float32)
+    lib().oracle_prep_frames(_p(m), _p(scale), _p(q), _p(opacity), _p(kappa), ctypes.c_int(n), _p(out))
+    return out
+
+
+def hits(frames, O, v, t_min, nsides=8):
+    frames, O, v, t_min = (_f32(_np(x)) for x in (frames, O, v, t_min))
+    R = O.shape[0]
+    t = np.zeros((K, R), np.float32)
+    idx = np.zeros((K, R), np.int32)
+    lib().oracle_hits(_p(frames), ctypes.c_int(frames.shape[0]), _p(O), _p(v), _p(t_min), ctypes.c_int(R),
+                      ctypes.c_int(nsides), _p(t), _p(idx))
+    return t, idx
+
+
+def next_tmin(t16):
+    return np.nextafter(np.float32(t16), np.float32(np.inf), dtype=np.float32)
+
+
+def hit_lists(frames, O, v, nsides=8, max_passes=100000):
+    """Runs the multi-pass restart loop to exhaustion: every hit of every ray in ascending (t, idx)
+    order, with the reference's restart t_min = nextafter(t_16) (ties at t_16 with a larger index are
+    dropped, as the reference's k-buffer drops them).  Returns CSR (off (R+1) int64, t, idx)."""
+    O, v = _f32(_np(O)), _f32(_np(v))
+    R = O.shape[0]
+    t_min = np.zeros(R, np.float32)
+    per_ray_t = [[] for _ in range(R)]
+    per_ray_i = [[] for _ in range(R)]
+    active = np.arange(R)
+    passes = 0
+    while active.size and passes < max_passes:
+        t, idx = hits(frames, O[active], v[active], t_min[active], nsides)
+        for j, r in enumerate(active):
+            valid = idx[:, j] >= 0
+            per_ray_t[r].extend(t[valid, j].tolist())
+            per_ray_i[r].extend(idx[valid, j].tolist())
+        full = idx[K - 1] >= 0
+        t_min[active[full]] = np.nextafter(t[K - 1, full], np.float32(np.inf), dtype=np.float32)
+        active = active[full]
+        passes += 1
+    off = np.zeros(R + 1, np.int64)
+    off[1:] = np.cumsum([len(x) for x in per_ray_i])
+    tt = np.array([x for r in per_ray_t for x in r], np.float32)
+    ii = np.array([x for r in per_ray_i for x in r], np.int32)
+    return off, tt, ii
+
+
+def scene_arrays(scene):
+    """numpy views of a flare_b200.scene.Scene (or dict) in the oracle's dtypes."""
+    g = scene if isinstance(scene, dict) else scene.__dict__
+    out = {}
+    for k_, x in g.items():
+        if k_ in ("cond", "A1", "A2", "A3"):
+            out[k_] = _np(x, np.float16)
+        else:
+            out[k_] = _f32(_np(x))
+    return out
+
+
+def forward(scene, O, v, csr, mode="training", base=False, bg=(0.0, 0.0, 0.0), T_thr=1e-4, reg_a=0.0,
+            reg_b=0.0, surface_normal=None, override_colors=None):
+    """Forward over CSR hit lists.  Returns a dict of numpy outputs (rgb, dacc, nacc, normal, alpha,
+    edn, med (R,2) with the index as float bits, T, nhits) and the composited-hit total."""
+    S = scene_arrays(scene)
+    O, v = _f32(_np(O)), _f32(_np(v))
+    R = O.shape[0]
+    off, tt, ii = csr
+    off = np.ascontiguousarray(off, np.int64)
+    tt = _f32(tt)
+    ii = np.ascontiguousarray(ii, np.int32)
+    out = {
+        "rgb": np.zeros((R, 3), np.float32), "dacc": np.zeros((R, 4), np.float32),
+        "nacc": np.zeros((R, 4), np.float32), "normal": np.zeros((R, 3), np.float32),
+        "alpha": np.zeros(R, np.float32), "edn": np.zeros(R, np.float32), "med": np.zeros((R, 2), np.float32),
+        "T": np.zeros(R, np.float32), "nhits": np.zeros(R, np.int32),
+    }
+    sn = None if surface_normal is None else _f32(_np(surface_normal))
+    oc = None if override_colors is None else _f32(_np(override_colors))
+    bgv = _f32(bg)
+    total = lib().oracle_shade_csr(
+        _p(S["m"]), _p(S["s"]), _p(S["q"]), _p(S["RGBA"]), _p(S["k"]),
+        None if base else _p(S["cond"]), _p(S["features"]), _p(S["A1"]), _p(S["b1"]), _p(S["A2"]),
+        _p(S["b2"]), _p(S["A3"]), _p(S["b3"]), _p(oc), ctypes.c_int(MODES[mode]), _p(bgv),
+        ctypes.c_float(T_thr), ctypes.c_float(reg_a), ctypes.c_float(reg_b), _p(O), _p(v), _p(sn),
+        ctypes.c_int(R), _p(off), _p(tt), _p(ii), _p(out["rgb"]), _p(out["dacc"]), _p(out["nacc"]),
+        _p(out["normal"]), _p(out["alpha"]), _p(out["edn"]), _p(out["med"]), _p(out["T"]), _p(out["nhits"]))
+    out["total_hits"] = int(total)
+    return out
