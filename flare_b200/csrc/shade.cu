@@ -52,7 +52,10 @@ constexpr int SM_BWD_BYTES = SM_BWD_MISC + 64;
 
 constexpr int TM_FWD_COLS = 128;
 constexpr int TM_BWD_COLS = 256;
-constexpr int TM_DW = 112;  // backward: weight-gradient region starts at this column
+constexpr int TM_DW = 128;  // backward: weight-gradient region starts at this column
+// backward TMEM map: transients [0,128): Y1 [0,64), Y2 [64,128) kept until delta2 is formed, Y3 / G2 / G1
+// at [0,64), dX at [0,112).  Weight gradients [128,256): lanes 0-15 of each warp (half 0) dW1 (64x128);
+// lanes 16-31 (half 1) dW2 [0,64), dW3^T hi|lo [64,72), db2 [72], db3 hi|lo rows [80], db1 [88].
 
 // dense weight-gradient accumulator layout in renderer->dw (floats)
 constexpr int DW_W1 = 0, DW_B1 = 8192, DW_W2 = 8256, DW_B2 = 12352, DW_W3 = 12416, DW_B3 = 13440;
@@ -118,11 +121,13 @@ struct Geo {
 __device__ __forceinline__ void geometry(const SceneP &sc, int idx, float t, float3 O, float3 v, Geo &g) {
     float2 s = __ldg(reinterpret_cast<const float2 *>(sc.s) + idx);
     float4 q = __ldg(reinterpret_cast<const float4 *>(sc.q) + idx);
-    g.sx = __expf(-s.x);
-    g.sy = __expf(-s.y);
+    // accurate exp / division: the LUT interpolation has cell boundaries, so the local coordinates are
+    // kept within an ulp or two of the exact value (fast-math intrinsics drift several ulp)
+    g.sx = expf(-s.x);
+    g.sy = expf(-s.y);
     g.q[0] = q.x; g.q[1] = q.y; g.q[2] = q.z; g.q[3] = q.w;
     float aa = q.x * q.x, bb = q.y * q.y, cc = q.z * q.z, dd = q.w * q.w;
-    float S = __fdividef(2.0f, aa + bb + cc + dd);
+    float S = __fdiv_rn(2.0f, aa + bb + cc + dd);
     g.S = S;
     float bs = q.y * S, cs = q.z * S, ds = q.w * S;
     float ab = q.x * bs, ac = q.x * cs, ad = q.x * ds;
@@ -135,7 +140,7 @@ __device__ __forceinline__ void geometry(const SceneP &sc, int idx, float t, flo
     g.V[0] = bc - ad; g.V[1] = 1.0f - bb - dd; g.V[2] = cd + ab;
     g.N[0] = bd + ac; g.N[1] = cd - ab; g.N[2] = 1.0f - bb - cc;
     g.kraw = __ldg(sc.k + idx);
-    g.kappa = 1.0f + __logf(1.0f + __expf(g.kraw));
+    g.kappa = 1.0f + log1pf(expf(g.kraw));
     g.kinv = 1.0f / g.kappa;
     const float *m = sc.m + 3 * (size_t)idx;
     g.d[0] = __fmaf_rn(v.x, t, O.x) - __ldg(m);
@@ -235,8 +240,39 @@ __device__ __forceinline__ void write_row64(char *tile, int r, const float *x) {
     }
 }
 
+// Writes 16 values as K chunks kc0, kc0+1 of row r of a K-major interleaved 128-row tile.
+__device__ __forceinline__ void write_row16(char *tile, int r, int kc0, const float *x) {
+    uint4 *T = reinterpret_cast<uint4 *>(tile);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        __half2 h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(x[8 * c + 2 * e], x[8 * c + 2 * e + 1]);
+        T[(kc0 + c) * 128 + r] = *reinterpret_cast<uint4 *>(h);
+    }
+}
+
+// As write_row16, split into f16 hi = rn(x) (tile_hi) and lo = rn(x - hi) (tile_lo).
+__device__ __forceinline__ void write_row16_split(char *tile_hi, char *tile_lo, int r, int kc0, const float *x) {
+    uint4 *H = reinterpret_cast<uint4 *>(tile_hi);
+    uint4 *L = reinterpret_cast<uint4 *>(tile_lo);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        __half2 h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float a0 = x[8 * c + 2 * e], a1 = x[8 * c + 2 * e + 1];
+            h[e] = __floats2half2_rn(a0, a1);
+            const float2 hf = __half22float2(h[e]);
+            l[e] = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+        }
+        H[(kc0 + c) * 128 + r] = *reinterpret_cast<uint4 *>(h);
+        L[(kc0 + c) * 128 + r] = *reinterpret_cast<uint4 *>(l);
+    }
+}
+
 // Loads the decoder weights, biases (and optionally the LUT) into shared memory.
-__device__ void load_decoder(char *smem, const SceneP &sc, bool with_lut) {
+__device__ void load_decoder(char *smem, const SceneP &sc, bool with_lut, bool dup_w3 = false) {
     const int tid = threadIdx.x, nt = blockDim.x;
     const uint4 *A1 = reinterpret_cast<const uint4 *>(sc.A1);
     const uint4 *A2 = reinterpret_cast<const uint4 *>(sc.A2);
@@ -251,7 +287,10 @@ __device__ void load_decoder(char *smem, const SceneP &sc, bool with_lut) {
     }
     for (int c = tid; c < 16 * 8; c += nt) {
         int o = c >> 3, kc = c & 7;
-        *reinterpret_cast<uint4 *>(smem + SM_W3 + kc * 256 + o * 16) = __ldg(A3 + c);
+        // rows 4..15 of A3 are padding (only outputs 0..3 are used); the backward stores a copy of rows
+        // 0..3 in rows 4..7 so a delta3 split into f16 hi (K 0..3) + lo (K 4..7) parts multiplies W3 twice
+        int src = (dup_w3 && o >= 4 && o < 8) ? c - 32 : c;
+        *reinterpret_cast<uint4 *>(smem + SM_W3 + kc * 256 + o * 16) = __ldg(A3 + src);
     }
     float *bias = reinterpret_cast<float *>(smem + SM_BIAS);
     for (int i = tid; i < 144; i += nt) bias[i] = i < 64 ? __ldg(sc.b1 + i) : (i < 128 ? __ldg(sc.b2 + i - 64) : __ldg(sc.b3 + i - 128));
@@ -310,9 +349,10 @@ __device__ __forceinline__ void tmem_row64(uint32_t tmem, int col, float *y) {
 
 // Forward MLP of the tile in `tile` (X already written, fence + barrier done by the caller).
 // Leaves h1/h2 in `tile` at the end (h2), returns y[0..3] (+ b3) for this thread's row.
-// If keep_d1/keep_d2 are non-null the Hardswish derivatives are stored there (f16 pairs).
+// If keep_d1 is non-null the layer-1 Hardswish derivatives are stored there (fp32).  Layer 2 accumulates
+// into TMEM columns [y2col, y2col+64): the backward keeps them there to form delta2 exactly.
 __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char *h1_tile, char *h2_tile, Mma &mm,
-                                                 float *y4, __half2 *keep_d1, __half2 *keep_d2) {
+                                                 float *y4, float *keep_d1, int y2col) {
     const float *bias = reinterpret_cast<const float *>(smem + SM_BIAS);
     const int r = threadIdx.x;
     float y[64];
@@ -324,10 +364,14 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
     bool ok = mma_wait(mm);
     tmem_row64(mm.tmem, 0, y);
 #pragma unroll
-    for (int o = 0; o < 64; ++o) {
-        float z = y[o] + bias[o];
-        if (keep_d1 && (o & 1)) keep_d1[o >> 1] = __floats2half2_rn(hswish_d(y[o - 1] + bias[o - 1]), hswish_d(z));
-        y[o] = hswish(z);
+    for (int o = 0; o < 64; o += 2) {
+        const float z0 = y[o] + bias[o], z1 = y[o + 1] + bias[o + 1];
+        if (keep_d1) {
+            keep_d1[o] = hswish_d(z0);
+            keep_d1[o + 1] = hswish_d(z1);
+        }
+        y[o] = hswish(z0);
+        y[o + 1] = hswish(z1);
     }
     write_row64(h1_tile, r, y);
     fence_async_smem();
@@ -335,16 +379,16 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
     __syncthreads();
     if (r == 0) {
         tc_fence_after();
-        issue_l2(mm.tmem, smem_u32(h1_tile), smem_u32(smem + SM_W2));
+        issue_l2(mm.tmem + y2col, smem_u32(h1_tile), smem_u32(smem + SM_W2));
         mma_commit(mm.mbar);
     }
     ok = mma_wait(mm) && ok;
-    tmem_row64(mm.tmem, 0, y);
+    tmem_row64(mm.tmem, y2col, y);
 #pragma unroll
-    for (int o = 0; o < 64; ++o) {
-        float z = y[o] + bias[64 + o];
-        if (keep_d2 && (o & 1)) keep_d2[o >> 1] = __floats2half2_rn(hswish_d(y[o - 1] + bias[64 + o - 1]), hswish_d(z));
-        y[o] = hswish(z);
+    for (int o = 0; o < 64; o += 2) {
+        const float z0 = y[o] + bias[64 + o], z1 = y[o + 1] + bias[64 + o + 1];
+        y[o] = hswish(z0);
+        y[o + 1] = hswish(z1);
     }
     write_row64(h2_tile, r, y);
     fence_async_smem();
@@ -456,7 +500,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
-                mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, nullptr);
+                mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, 0);
                 __syncthreads();
                 if (s_abort) goto done;
             }
@@ -580,7 +624,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             s_first = 1;
         }
         if (tid < 32) tmem_alloc(tmem_slot, TM_BWD_COLS);
-        load_decoder(smem, sc, false);
+        load_decoder(smem, sc, false, true);
         {   // ones column tile (128 rows x 8, element 0 = 1)
             uint4 *ones = reinterpret_cast<uint4 *>(smem + SM_BWD_ONES);
             __half2 h[4] = {__floats2half2_rn(1.0f, 0.0f), __floats2half2_rn(0.0f, 0.0f), __floats2half2_rn(0.0f, 0.0f),
@@ -638,14 +682,14 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             else g = Geo{};
             const float cu = g.u * LUT_SCALE, cw = g.w * LUT_SCALE;
             float y4[4] = {0, 0, 0, 0};
-            __half2 hd1[32], hd2[32];
+            float hd1[64];
             if (DEC) {
                 if (!__syncthreads_or(valid)) continue;  // uniform
                 write_x_row(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
-                mlp_forward_tile(smem, xt, h1t, h2t, mm, y4, hd1, hd2);
+                mlp_forward_tile(smem, xt, h1t, h2t, mm, y4, hd1, 64);
                 __syncthreads();
                 if (s_abort) goto done;
             }
@@ -726,11 +770,17 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             }
             // ---- decoder backward on the tensor core ----
             if (DEC) {
-                {   // delta3 tile row (scaled into the f16 range), zero for rows that do not contribute
+                {   // delta3 tile row, scaled into the f16 range and split into hi (columns 0..3) and
+                    // lo = delta3 - hi (columns 4..7); zero for rows that do not contribute
                     uint4 *T3 = reinterpret_cast<uint4 *>(d3t);
-                    __half2 hh[4] = {__floats2half2_rn(d3[0] * gscale, d3[1] * gscale),
-                                     __floats2half2_rn(d3[2] * gscale, d3[3] * gscale), __floats2half2_rn(0.f, 0.f),
-                                     __floats2half2_rn(0.f, 0.f)};
+                    __half2 hh[4];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float a0 = d3[2 * e] * gscale, a1 = d3[2 * e + 1] * gscale;
+                        hh[e] = __floats2half2_rn(a0, a1);
+                        const float2 hf = __half22float2(hh[e]);
+                        hh[2 + e] = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+                    }
                     T3[tid] = *reinterpret_cast<uint4 *>(hh);
                     T3[128 + tid] = make_uint4(0, 0, 0, 0);
                 }
@@ -758,16 +808,20 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     mma_commit(mm.mbar);
                 }
                 mma_wait(mm);
-                float gy[64];
-                tmem_row64(mm.tmem, 0, gy);
-                // delta2 = G2 * hswish'(y2) -> H2 tile (H2 is free: dW3 completed with G2)
+                const uint32_t lane = (uint32_t)((threadIdx.x & ~31) << 16);
+                {   // delta2 = G2 * hswish'(y2 + b2), y2 re-read in fp32 from TMEM -> H2 tile (free: dW3 done)
+                    const float *b2s = reinterpret_cast<const float *>(smem + SM_BIAS) + 64;
 #pragma unroll
-                for (int o = 0; o < 32; ++o) {
-                    float2 dd = __half22float2(hd2[o]);
-                    gy[2 * o] *= dd.x;
-                    gy[2 * o + 1] *= dd.y;
+                    for (int cb = 0; cb < 4; ++cb) {
+                        float gv[16], yv[16];
+                        tmem_ld16(mm.tmem + lane + 16 * cb, gv);
+                        tmem_ld16(mm.tmem + lane + 64 + 16 * cb, yv);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) gv[e] *= hswish_d(yv[e] + b2s[16 * cb + e]);
+                        write_row16(h2t, tid, 2 * cb, gv);
+                    }
                 }
-                write_row64(h2t, tid, gy);
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
@@ -791,14 +845,16 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     mma_commit(mm.mbar);
                 }
                 mma_wait(mm);
-                tmem_row64(mm.tmem, 0, gy);
+                // delta1 = G1 * hswish'(y1): hi -> H1 tile, lo -> H2 tile (both free now)
 #pragma unroll
-                for (int o = 0; o < 32; ++o) {
-                    float2 dd = __half22float2(hd1[o]);
-                    gy[2 * o] *= dd.x;
-                    gy[2 * o + 1] *= dd.y;
+                for (int cb = 0; cb < 4; ++cb) {
+                    float gv[16];
+                    tmem_ld16(mm.tmem + lane + 16 * cb, gv);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) gv[e] *= hd1[16 * cb + e];
+                    write_row16_split(h1t, h2t, tid, 2 * cb, gv);
                 }
-                write_row64(h1t, tid, gy);  // delta1 (H1 is free: dW2 completed with G1)
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
@@ -813,20 +869,34 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                         mma_f16_ss(mm.tmem + 16, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
                                    sdesc(smem_u32(smem + SM_W1) + 4 * 1024 + ks * 256, 128, 1024),
                                    idesc_f16(128, 96, 0, 1), ks > 0);
-                    // dW1 += d1^T X : M=64, N=128, K=128 hits
+                    // + the lo part of delta1
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16_ss(mm.tmem, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
+                                   sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1), 1);
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_f16_ss(mm.tmem + 16, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
+                                   sdesc(smem_u32(smem + SM_W1) + 4 * 1024 + ks * 256, 128, 1024),
+                                   idesc_f16(128, 96, 0, 1), 1);
+                    // dW1 += d1^T X : M=64, N=128, K=128 hits (hi and lo parts of d1)
                     for (int ks = 0; ks < 8; ++ks)
                         mma_f16_ss(dwreg, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
                                    sdesc(smem_u32(xt) + ks * 256, 128, 2048), idesc_f16(64, 128, 1, 1),
                                    (ks > 0) | acc0);
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg, sdesc(smem_u32(h2t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(xt) + ks * 256, 128, 2048), idesc_f16(64, 128, 1, 1), 1);
                     // db1 += d1^T 1
                     for (int ks = 0; ks < 8; ++ks)
-                        mma_f16_ss(dwreg + 128, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
+                        mma_f16_ss(dwreg + half1 + 88, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
                                    sdesc(smem_u32(smem + SM_BWD_ONES) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
                                    (ks > 0) | acc0);
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16_ss(dwreg + half1 + 88, sdesc(smem_u32(h2t) + ks * 256, 128, 2048),
+                                   sdesc(smem_u32(smem + SM_BWD_ONES) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
+                                   1);
                     mma_commit(mm.mbar);
                 }
                 mma_wait(mm);
-                const uint32_t lane = (uint32_t)((threadIdx.x & ~31) << 16);
                 float dx16[16];
                 tmem_ld16(mm.tmem + lane, dx16);
                 tmem_wait_ld();
@@ -945,21 +1015,21 @@ done:
             const uint32_t lane = (uint32_t)((w * 32) << 16);
             const int mrow = 16 * w + (l & 15);
 #pragma unroll 1
-            for (int b = 0; b < 9; ++b) {
+            for (int b = 0; b < 8; ++b) {
                 float vals[16];
                 tmem_ld16(mm.tmem + lane + TM_DW + 16 * b, vals);
                 tmem_wait_ld();
                 for (int e = 0; e < 16; ++e) {
                     const int col = 16 * b + e;
                     const float x = vals[e] * ginv;
-                    if (l < 16) {  // half 0: dW1 row mrow, db1 at column 128
-                        if (col < 128) atomicAdd(bo.dw + DW_W1 + mrow * 128 + col, x);
-                        else if (col == 128) atomicAdd(bo.dw + DW_B1 + mrow, x);
-                    } else {       // half 1: dW2 row mrow | dW3^T row mrow | db2 | db3
+                    if (l < 16) {  // half 0: dW1 row mrow
+                        atomicAdd(bo.dw + DW_W1 + mrow * 128 + col, x);
+                    } else {       // half 1: dW2 row mrow | dW3^T row mrow | db2 | db3 | db1
                         if (col < 64) atomicAdd(bo.dw + DW_W2 + mrow * 64 + col, x);
-                        else if (col < 68) atomicAdd(bo.dw + DW_W3 + (col - 64) * 64 + mrow, x);
+                        else if (col < 72) atomicAdd(bo.dw + DW_W3 + ((col - 64) & 3) * 64 + mrow, x);
                         else if (col == 72) atomicAdd(bo.dw + DW_B2 + mrow, x);
-                        else if (col == 80 && mrow < 4) atomicAdd(bo.dw + DW_B3 + mrow, x);
+                        else if (col == 80 && mrow < 8) atomicAdd(bo.dw + DW_B3 + (mrow & 3), x);
+                        else if (col == 88) atomicAdd(bo.dw + DW_B1 + mrow, x);
                     }
                 }
             }
@@ -1231,7 +1301,7 @@ __global__ void __launch_bounds__(128) selftest_mlp_kernel(const uint4 *X, int r
         tc_fence_before();
         __syncthreads();
         float y4[4];
-        mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, nullptr);
+        mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, 0);
         __syncthreads();
         if (s_abort) break;
         if (row < rows)

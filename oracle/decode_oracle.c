@@ -267,3 +267,8 @@ long oracle_shade_csr(const float *m, const float *s, const float *q, const floa
     }
     return total;
 }
+
+/* The LUT encoding alone, for the golden-vector test: out (n, 8) for coordinates (cu, cw). */
+void oracle_lut(const float *features, const float *cu, const float *cw, int n, float *out) {
+    for (int i = 0; i < n; ++i) lut_encode(features, cu[i], cw[i], out + 8 * i);
+}

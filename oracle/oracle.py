@@ -150,12 +150,20 @@ def forward(scene, O, v, csr, mode="training", base=False, bg=(0.0, 0.0, 0.0), T
     sn = None if surface_normal is None else _f32(_np(surface_normal))
     oc = None if override_colors is None else _f32(_np(override_colors))
     bgv = _f32(bg)
+    G = lambda k_: _p(S.get(k_)) if not base else None  # noqa: E731
     total = lib().oracle_shade_csr(
         _p(S["m"]), _p(S["s"]), _p(S["q"]), _p(S["RGBA"]), _p(S["k"]),
-        None if base else _p(S["cond"]), _p(S["features"]), _p(S["A1"]), _p(S["b1"]), _p(S["A2"]),
-        _p(S["b2"]), _p(S["A3"]), _p(S["b3"]), _p(oc), ctypes.c_int(MODES[mode]), _p(bgv),
+        G("cond"), G("features"), G("A1"), G("b1"), G("A2"), G("b2"), G("A3"), G("b3"), _p(oc), ctypes.c_int(MODES[mode]), _p(bgv),
         ctypes.c_float(T_thr), ctypes.c_float(reg_a), ctypes.c_float(reg_b), _p(O), _p(v), _p(sn),
         ctypes.c_int(R), _p(off), _p(tt), _p(ii), _p(out["rgb"]), _p(out["dacc"]), _p(out["nacc"]),
         _p(out["normal"]), _p(out["alpha"]), _p(out["edn"]), _p(out["med"]), _p(out["T"]), _p(out["nhits"]))
     out["total_hits"] = int(total)
+    return out
+
+
+def lut(features, cu, cw):
+    """The 4-level LUT encoding of coordinates (cu, cw) (already scaled by 1/sqrt(11.3449)) -> (n, 8)."""
+    features, cu, cw = _f32(_np(features)), _f32(_np(cu)), _f32(_np(cw))
+    out = np.zeros((cu.shape[0], 8), np.float32)
+    lib().oracle_lut(_p(features), _p(cu), _p(cw), ctypes.c_int(cu.shape[0]), _p(out))
     return out

@@ -1,0 +1,337 @@
+"""GPU parity of the CUDA path (through the C ABI / drop-in host layer) against the CPU oracle.
+
+Bars (from the task): hit indices bit-exact; rendered RGB / opacity / accumulators within 1e-3 max
+absolute error; gradients within 1e-3 relative L2 (fp32 and the decoder's f16 tensor-core operands).
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from flare_b200.scene import camera_rays, make_scene
+from oracle import grad_oracle, oracle
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+RGB_TOL = 1e-3
+GRAD_TOL = 1e-3
+T_NEAR, T_FAR = 0.1, 1000.0
+REG_A = -(T_NEAR * T_FAR) / (T_FAR - T_NEAR)
+REG_B = T_FAR / (T_FAR - T_NEAR)
+
+
+def _renderer(n_rays, sides=8):
+    from flare_b200.renderer import CPyOptiXFLARERenderer
+    return CPyOptiXFLARERenderer(sides, 11.3449, n_rays)
+
+
+class Case:
+    """Config-0 style workload: seeded scene, one camera, oracle hit lists."""
+
+    def __init__(self, n, width, seed=0, eye=(0.0, 0.0, 3.0), fov=60.0):
+        self.sc = make_scene(n, seed)
+        self.O, self.v = camera_rays(width, width, fov, eye=eye)
+        self.R = width * width
+        self.g = self.sc.to("cuda")
+        self.Og, self.vg = self.O.cuda(), self.v.cuda()
+        self.r = _renderer(self.R)
+        self.r.SetGeometry(*[t.contiguous() for t in self.g.activated()])
+        self.frames = self.r.frames().cpu().numpy()
+        self.csr = oracle.hit_lists(self.frames, self.O, self.v)
+
+    def dec(self):
+        g = self.g
+        return (g.cond, g.features, g.A1, g.b1, g.A2, g.b2, g.A3, g.b3)
+
+    def geo(self):
+        g = self.g
+        return (g.m, g.s, g.q, g.RGBA, g.k)
+
+
+@pytest.fixture(scope="module")
+def case0():
+    return Case(10000, 64, seed=0)
+
+
+@pytest.fixture(scope="module")
+def case_dense():
+    # denser view: more hits per ray, several passes
+    return Case(200000, 32, seed=1, eye=(0.0, 0.0, 1.8), fov=40.0)
+
+
+def z(*s):
+    return torch.zeros(*s, device="cuda")
+
+
+# ---------------------------------------------------------------------------------------------- MLP
+def test_mlp_tile_matches_torch():
+    from flare_b200.renderer import selftest_mlp
+    sc = make_scene(10, 3)
+    g = torch.Generator().manual_seed(5)
+    X = (torch.randn(1000, 128, generator=g) * 0.5).half()
+    Y = selftest_mlp(X.cuda(), sc.A1.cuda(), sc.b1.cuda() + 0.1, sc.A2.cuda(), sc.b2.cuda() - 0.05, sc.A3.cuda(),
+                     sc.b3.cuda() + 0.2).cpu()
+
+    def hs(y):
+        return y * torch.clamp(y + 3, 0, 6) / 6
+
+    h1 = hs(X.float() @ sc.A1.float().T + sc.b1 + 0.1).half().float()
+    h2 = hs(h1 @ sc.A2.float().T + sc.b2 - 0.05).half().float()
+    y = h2 @ sc.A3.float().T + sc.b3 + 0.2
+    assert (Y[:, :4] - y[:, :4]).abs().max().item() < 1e-3
+
+
+# --------------------------------------------------------------------------------------------- hits
+def test_frames_match_oracle(case0):
+    fo = oracle.prep_frames(*case0.sc.activated())
+    np.testing.assert_allclose(case0.frames, fo, rtol=2e-6, atol=1e-6)
+
+
+def test_hits_bit_exact_first_pass(case0):
+    c = case0
+    t, idx = c.r.Render(c.Og, c.vg, z(c.R), c.R)
+    to, io = oracle.hits(c.frames, c.O, c.v, np.zeros(c.R, np.float32))
+    assert np.array_equal(idx.cpu().numpy(), io)
+    assert np.array_equal(t.cpu().numpy(), to)
+    assert (io >= 0).sum() > 1000
+
+
+def test_hits_bit_exact_every_pass(case_dense):
+    c = case_dense
+    tmin = np.zeros(c.R, np.float32)
+    passes = 0
+    while True:
+        t, idx = c.r.Render(c.Og, c.vg, torch.from_numpy(tmin).cuda(), c.R)
+        to, io = oracle.hits(c.frames, c.O, c.v, tmin)
+        assert np.array_equal(idx.cpu().numpy(), io), f"pass {passes}"
+        assert np.array_equal(t.cpu().numpy(), to), f"pass {passes}"
+        full = io[15] >= 0
+        if not full.any():
+            break
+        tmin = np.where(full, np.nextafter(to[15], np.float32(np.inf), dtype=np.float32), np.float32(np.inf))
+        passes += 1
+    assert passes >= 2
+
+
+def test_hits_random_tmin(case0):
+    c = case0
+    tm = (np.random.RandomState(3).rand(c.R) * 3.5).astype(np.float32)
+    t, idx = c.r.Render(c.Og, c.vg, torch.from_numpy(tm).cuda(), c.R)
+    to, io = oracle.hits(c.frames, c.O, c.v, tm)
+    assert np.array_equal(idx.cpu().numpy(), io)
+
+
+def test_hits_edge_cases():
+    r = _renderer(64)
+    O = torch.zeros(64, 3, device="cuda")
+    v = torch.nn.functional.normalize(torch.randn(64, 3, device="cuda"), dim=1)
+    # no primitives: every slot empty
+    e = torch.zeros(0, device="cuda")
+    r.SetGeometry(e.view(0, 3), e.view(0, 2), e.view(0, 4), e, e)
+    t, idx = r.Render(O, v, z(64), 64)
+    assert (idx == -1).all() and torch.isinf(t).all()
+    # one primitive straight ahead
+    m = torch.tensor([[0.0, 0.0, 2.0]], device="cuda")
+    r.SetGeometry(m, torch.full((1, 2), 0.5, device="cuda"), torch.tensor([[1.0, 0, 0, 0]], device="cuda"),
+                  torch.full((1,), 0.9, device="cuda"), torch.full((1,), 2.0, device="cuda"))
+    vv = torch.tensor([[0.0, 0.0, 1.0]], device="cuda").repeat(64, 1)
+    t, idx = r.Render(O, vv, z(64), 64)
+    assert (idx[0] == 0).all() and torch.allclose(t[0], torch.full((64,), 2.0, device="cuda"))
+    assert (idx[1:] == -1).all()
+    # t_min beyond the hit: nothing
+    t, idx = r.Render(O, vv, torch.full((64,), 2.5, device="cuda"), 64)
+    assert (idx == -1).all()
+    # zero rays is a no-op
+    r.Render(O, vv, z(64), 0)
+
+
+# ------------------------------------------------------------------------------------------ forward
+def _fwd_oracle(c, mode, base, bg=(0.1, 0.2, 0.3), sn=None, oc=None):
+    return oracle.forward(c.sc, c.O, c.v, c.csr, mode, base=base, bg=bg, T_thr=1e-4, reg_a=REG_A, reg_b=REG_B,
+                          surface_normal=sn, override_colors=oc)
+
+
+def _surface_normals(R, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    sn = torch.nn.functional.normalize(torch.randn(R, 3, generator=g), dim=1)
+    sn[::2] = 0.0  # half the rays carry no normal target
+    return sn
+
+
+@pytest.mark.parametrize("base", [True, False])
+def test_forward_training(case_dense, base):
+    c = case_dense
+    R = c.R
+    bg = (0.1, 0.2, 0.3)
+    sn = _surface_normals(R)
+    ref = _fwd_oracle(c, "training", base, bg, sn=sn.numpy())
+    bitmap, dacc, nacc, dai = z(R, 3), z(R, 4), z(R, 4), z(R, 2)
+    args = (c.Og, c.vg, bitmap, *bg, *c.geo(), 1e-4, dacc, REG_A, REG_B, dai, sn.cuda(), nacc)
+    if base:
+        c.r.Forward_training_base(*args)
+    else:
+        c.r.Forward_training(*c.dec(), *args)
+    st = c.r.stats()
+    assert st["hits_composited"] == ref["total_hits"]
+    assert st["passes"] >= 2
+    assert np.abs(bitmap.cpu().numpy() - ref["rgb"]).max() < RGB_TOL
+    assert np.abs(dacc.cpu().numpy() - ref["dacc"]).max() < RGB_TOL * max(1.0, np.abs(ref["dacc"]).max())
+    assert np.abs(nacc.cpu().numpy() - ref["nacc"]).max() < RGB_TOL
+
+
+@pytest.mark.parametrize("base", [True, False])
+def test_forward_inference_and_geometry(case_dense, base):
+    c = case_dense
+    R = c.R
+    bg = (0.3, 0.1, 0.0)
+    ref = _fwd_oracle(c, "geometry", base, bg)
+    bitmap, normal, alpha, edn = z(R, 3), z(R, 3), z(R), z(R)
+    if base:
+        c.r.Forward_inference_base_with_geometry(c.Og, c.vg, bitmap, normal, alpha, edn, *bg, *c.geo(), 1e-4)
+    else:
+        c.r.Forward_inference_with_geometry(*c.dec(), c.Og, c.vg, bitmap, normal, alpha, edn, *bg, *c.geo(), 1e-4)
+    assert np.abs(bitmap.cpu().numpy() - ref["rgb"]).max() < RGB_TOL
+    assert np.abs(alpha.cpu().numpy() - ref["alpha"]).max() < RGB_TOL
+    assert np.abs(normal.cpu().numpy() - ref["normal"]).max() < RGB_TOL
+    assert np.abs(edn.cpu().numpy() - ref["edn"]).max() < RGB_TOL * max(1.0, np.abs(ref["edn"]).max())
+    # plain inference gives the same image
+    b2 = z(R, 3)
+    if base:
+        c.r.Forward_inference_base(c.Og, c.vg, b2, *bg, *c.geo(), 1e-4)
+    else:
+        c.r.Forward_inference(*c.dec(), c.Og, c.vg, b2, *bg, *c.geo(), 1e-4)
+    assert torch.equal(b2, bitmap)
+
+
+def test_forward_pca(case0):
+    c = case0
+    R = c.R
+    oc = torch.rand(c.sc.n, 3, generator=torch.Generator().manual_seed(9))
+    ref = _fwd_oracle(c, "pca", False, oc=oc.numpy())
+    bitmap = z(R, 3)
+    c.r.Forward_pca(*c.dec(), oc.cuda(), c.Og, c.vg, bitmap, 0.1, 0.2, 0.3, *c.geo(), 1e-4)
+    assert np.abs(bitmap.cpu().numpy() - ref["rgb"]).max() < RGB_TOL
+
+
+@pytest.mark.parametrize("base", [True, False])
+def test_median_depth(case_dense, base):
+    c = case_dense
+    R = c.R
+    ref = _fwd_oracle(c, "median", base)
+    dai = z(R, 2)
+    if base:
+        c.r.GetMedianDepth_base(c.Og, c.vg, *c.geo(), 1e-4, dai)
+    else:
+        c.r.GetMedianDepth(*c.dec(), c.Og, c.vg, *c.geo(), 1e-4, dai)
+    got = dai.cpu().numpy()
+    gi = got[:, 1].view(np.int32)
+    ri = ref["med"][:, 1].view(np.int32)
+    agree = gi == ri
+    # the last hit with T > 0.5 can flip only where T crosses 0.5 within rounding
+    assert agree.mean() > 0.995
+    np.testing.assert_array_equal(got[agree, 0], ref["med"][agree, 0])
+
+
+def test_forward_is_deterministic(case0):
+    c = case0
+    outs = []
+    for _ in range(2):
+        b = z(c.R, 3)
+        c.r.Forward_inference(*c.dec(), c.Og, c.vg, b, 0.0, 0.0, 0.0, *c.geo(), 1e-4)
+        outs.append(b)
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_smoke_scene_on_gpu():
+    from test_oracle import _smoke, _smoke_rays, analytic_smoke_image
+    zz = _smoke()
+    O, v = _smoke_rays(zz)
+    r = _renderer(64)
+    m, s, q, RGBA, k = (torch.from_numpy(zz[n]).cuda() for n in ("m", "s", "q", "RGBA", "k"))
+    r.SetGeometry(m, torch.exp(s), q, torch.sigmoid(RGBA[:, 3]).contiguous(),
+                  (1 + torch.nn.functional.softplus(k[:, 0])).contiguous())
+    img = z(64, 3)
+    r.Forward_inference_base(torch.from_numpy(O).cuda(), torch.from_numpy(v).cuda(), img, *zz["bg"].tolist(), m, s, q,
+                             RGBA, k, 1e-4)
+    exp, hit = analytic_smoke_image(zz, O, v)
+    assert np.abs(img.cpu().numpy() - exp).max() < 1e-5
+
+
+def test_generate_rays_formula():
+    from flare_b200.renderer import GenerateRays
+    Rv = torch.tensor([1.0, 0, 0], device="cuda")
+    D = torch.tensor([0, 1.0, 0], device="cuda")
+    F = torch.tensor([0, 0, 1.0], device="cuda")
+    out = GenerateRays(Rv, D, F, 7, 5, 1.0, 0.8).cpu().double()
+    ttx, tty = 2 * math.tan(0.5), 2 * math.tan(0.4)
+    ys, xs = torch.meshgrid(torch.arange(5.0), torch.arange(7.0), indexing="ij")
+    dx = (-0.5 + (xs + 0.5) / 7) * ttx
+    dy = (-0.5 + (ys + 0.5) / 5) * tty
+    assert out.shape == (5, 7, 3)
+    assert torch.allclose(out[..., 0], dx.double(), atol=1e-6)
+    assert torch.allclose(out[..., 1], dy.double(), atol=1e-6)
+    assert torch.allclose(out[..., 2], torch.ones(5, 7, dtype=torch.float64))
+
+
+# ----------------------------------------------------------------------------------------- backward
+def unpack_weight_grads(dw1, db1, dw2, db2, dw3, db3):
+    """The reference caller's reduction of the per-warp fragment layout (train.py:754-790), restated."""
+    w3 = dw3.sum(0).reshape(8, 2, 32).transpose(1, 2).reshape(8, 8, -1).transpose(0, 1).flatten(1, 2)
+    b3 = db3.sum(0).reshape(2, 32).transpose(0, 1).reshape(8, 8).sum(1)
+    w2 = dw2.sum(0).reshape(64, 2, 32).transpose(1, 2).reshape(8, 8, 8, -1).transpose(1, 2).flatten(0, 1).flatten(1, 2)
+    b2 = db2.sum(0).reshape(8, 2, 32).transpose(1, 2).reshape(8, 8, -1).sum(2).flatten(0, 1)
+    w1 = dw1.sum(0).reshape(128, 2, 32).transpose(1, 2).reshape(8, 16, 8, -1).transpose(1, 2).flatten(0, 1).flatten(1, 2)
+    b1 = db1.sum(0).reshape(8, 2, 32).transpose(1, 2).reshape(8, 8, -1).sum(2).flatten(0, 1)
+    return w1, b1, w2, b2, w3, b3
+
+
+def _run_backward(c, base, lam_d, lam_n, seed):
+    R, n = c.R, c.sc.n
+    bg = (0.1, 0.2, 0.3)
+    sn = _surface_normals(R, seed)
+    ref = _fwd_oracle(c, "training", base, bg, sn=sn.numpy())
+    bitmap, dacc, nacc, dai = z(R, 3), z(R, 4), z(R, 4), z(R, 2)
+    args = (c.Og, c.vg, bitmap, *bg, *c.geo(), 1e-4, dacc, REG_A, REG_B, dai, sn.cuda(), nacc)
+    if base:
+        c.r.Forward_training_base(*args)
+    else:
+        c.r.Forward_training(*c.dec(), *args)
+    g = torch.Generator().manual_seed(seed)
+    dLdI = (torch.randn(R, 3, generator=g) / R).float()
+    I = bitmap.clone()
+    G = dict(RGB=z(n, 3), A=z(n, 1), k=z(n, 1), m=z(n, 3), s=z(n, 2), q=z(n, 4))
+    prefix = z(R, 4)
+    if base:
+        c.r.Backward_base(c.Og, c.vg, *bg, *c.geo(), I, dLdI.cuda(), G["RGB"], G["A"], G["k"], G["m"], G["s"], G["q"],
+                          1e-4, dacc, prefix, lam_d, REG_A, REG_B, dai, sn.cuda(), nacc, lam_n)
+    else:
+        W = dict(w3=z(3, 512), b3=z(3, 64), w2=z(3, 4096), b2=z(3, 512), w1=z(3, 8192), b1=z(3, 512))
+        G["cond"], G["features"] = z(n, 96), z(13154)
+        c.r.Backward(*c.dec(), c.Og, c.vg, *bg, *c.geo(), I, dLdI.cuda(), G["RGB"], G["A"], G["k"], W["w3"], W["b3"],
+                     W["w2"], W["b2"], W["w1"], W["b1"], G["cond"], G["features"], G["m"], G["s"], G["q"], 1e-4, dacc,
+                     prefix, lam_d, REG_A, REG_B, dai, sn.cuda(), nacc, lam_n)
+        assert torch.count_nonzero(W["w1"][1:]) == 0  # only row 0 is written
+        w1, b1, w2, b2, w3, b3 = unpack_weight_grads(*(W[k].cpu() for k in ("w1", "b1", "w2", "b2", "w3", "b3")))
+        G.update(A1=w1, b1=b1, A2=w2, b2=b2, A3=w3[:4], b3=b3[:4])
+    gr = grad_oracle.gradients(c.sc, c.O, c.v, c.csr, ref["nhits"], dLdI.numpy(), base=base, bg=bg, reg_a=REG_A,
+                               reg_b=REG_B, lambda_depth=lam_d, lambda_normal=lam_n, surface_normal=sn.numpy())
+    if not base:
+        gr["A3"] = gr["A3"][:4]
+        gr["b3"] = gr["b3"][:4]
+    return G, gr
+
+
+@pytest.mark.parametrize("base", [True, False])
+@pytest.mark.parametrize("reg", [(0.0, 0.0), (1e-3, 1e-3)])
+def test_backward_matches_autograd(case_dense, base, reg):
+    G, gr = _run_backward(case_dense, base, reg[0], reg[1], seed=11)
+    keys = ["RGB", "A", "k", "m", "s", "q"] + ([] if base else ["cond", "features", "A1", "b1", "A2", "b2", "A3", "b3"])
+    bad = {}
+    for k in keys:
+        got = G[k].cpu().numpy() if torch.is_tensor(G[k]) else G[k]
+        e = grad_oracle.rel_l2(got, gr[k].numpy())
+        if not e < GRAD_TOL:
+            bad[k] = e
+    assert not bad, f"relative L2 above {GRAD_TOL}: {bad}"

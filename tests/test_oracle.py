@@ -1,0 +1,161 @@
+"""CPU tests of the oracle (the checker): golden vectors, known-answer scenes, internal consistency."""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from flare_b200.scene import camera_rays, make_scene
+from oracle import grad_oracle, oracle
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def test_lut_matches_reference_gridlevel():
+    """The oracle LUT equals the reference's own Python LUT level (encoding_2d_benchmark.GridLevel)."""
+    g = np.load(os.path.join(GOLD, "lut_gridlevel.npz"))
+    out = oracle.lut(g["features"], g["cu"], g["cw"])
+    # GridLevel runs in float64, the oracle in float32: the coordinate (c+1)/2*(R-1) carries ~6e-8 * 63
+    # of rounding, times a table slope <= 0.2 per cell -> < 1e-6
+    np.testing.assert_allclose(out, g["expected"], atol=1e-6, rtol=0)
+
+
+def test_polygon_constants_octagon():
+    c, s = oracle.polygon_constants(8)
+    # vertices on the unit circle are exactly on the boundary: max_j (c_j x + s_j y) == 1
+    for j in range(8):
+        th = 2 * math.pi * j / 8
+        x, y = math.cos(th), math.sin(th)
+        assert max(c * x + s * y) == pytest.approx(1.0, abs=1e-6)
+    # the centre of every edge as well, and the inscribed circle is inside
+    assert max(c * math.cos(math.pi / 8) * math.cos(math.pi / 8) + s * math.cos(math.pi / 8) * math.sin(math.pi / 8)) == pytest.approx(1.0, abs=1e-6)
+
+
+def _smoke():
+    z = np.load(os.path.join(GOLD, "smoke_scene.npz"))
+    return z
+
+
+def _smoke_rays(z):
+    W, H, fov = int(z["width"]), int(z["height"]), float(z["fov"])
+    tt = 2 * math.tan(0.5 * fov)
+    ys, xs = np.meshgrid(np.arange(H), np.arange(W), indexing="ij")
+    dx = (tt / W) * xs.ravel() + 0.5 * tt * (1.0 / W - 1.0)
+    dy = (tt / H) * ys.ravel() + 0.5 * tt * (1.0 / H - 1.0)
+    v = np.stack([dx, dy, np.ones_like(dx)], 1)
+    v = (v / np.linalg.norm(v, axis=1, keepdims=True)).astype(np.float32)
+    return np.zeros_like(v), v
+
+
+def analytic_smoke_image(z, O, v):
+    """Single primitive at (0,0,3) facing the camera: closed form in float64."""
+    sx = 0.75
+    sig = 0.9
+    kappa = 2.0
+    rho = (kappa * (11.3449 + 2 * math.log(sig))) ** (1 / (2 * kappa))
+    out = np.zeros((v.shape[0], 3))
+    hit = np.zeros(v.shape[0], bool)
+    for i in range(v.shape[0]):
+        t = 3.0 / v[i, 2]
+        x, y = t * v[i, 0], t * v[i, 1]
+        u, w = x / sx, y / sx
+        a, b = u / rho, w / rho
+        inside = all(math.cos((2 * j + 1) * math.pi / 8) * a + math.sin((2 * j + 1) * math.pi / 8) * b
+                     <= math.cos(math.pi / 8) for j in range(8))
+        T = 1.0
+        c = np.zeros(3)
+        if inside:
+            G = math.exp(-0.5 * (u * u + w * w) ** kappa / kappa)
+            al = sig * G
+            c += al * np.array([1.0, 0.0, 0.0])
+            T = 1 - al
+            hit[i] = True
+        out[i] = c + T * z["bg"]
+    return out, hit
+
+
+def test_smoke_scene_known_answer():
+    z = _smoke()
+    O, v = _smoke_rays(z)
+    fr = oracle.prep_frames(z["m"], np.exp(z["s"]), z["q"], 1 / (1 + np.exp(-z["RGBA"][:, 3])),
+                            1 + np.log1p(np.exp(z["k"][:, 0])))
+    csr = oracle.hit_lists(fr, O, v)
+    scene = {"m": z["m"], "s": z["s"], "q": z["q"], "RGBA": z["RGBA"], "k": z["k"]}
+    out = oracle.forward(scene, O, v, csr, "inference", base=True, bg=z["bg"])
+    exp, hit = analytic_smoke_image(z, O, v)
+    assert hit.any() and not hit.all()
+    assert (np.diff(csr[0]) == hit).all()
+    np.testing.assert_allclose(out["rgb"], exp, atol=2e-6)
+    # the centre-most pixels are red-dominated, the corners show the background
+    assert out["rgb"][hit, 0].min() > z["bg"].max()
+
+
+def test_hit_lists_sorted_and_beyond_tmin():
+    sc = make_scene(2000, 3)
+    O, v = camera_rays(16, 16, 60.0, eye=(0.0, 0.0, 3.0))
+    fr = oracle.prep_frames(*sc.activated())
+    t, idx = oracle.hits(fr, O, v, np.full(256, 2.5, np.float32))
+    valid = idx >= 0
+    assert (t[valid] >= 2.5).all()
+    # ascending by (t, idx), padding at the end
+    for r in range(256):
+        k = valid[:, r].sum()
+        assert valid[:k, r].all() and not valid[k:, r].any()
+        tt, ii = t[:k, r], idx[:k, r]
+        assert all((tt[j] < tt[j + 1]) or (tt[j] == tt[j + 1] and ii[j] < ii[j + 1]) for j in range(k - 1))
+    assert np.isinf(t[~valid]).all() and (idx[~valid] == -1).all()
+
+
+def test_multipass_restart_is_nextafter():
+    sc = make_scene(3000, 5)
+    O, v = camera_rays(8, 8, 30.0, eye=(0.0, 0.0, 3.0))
+    fr = oracle.prep_frames(*sc.activated())
+    off, tt, ii = oracle.hit_lists(fr, O, v)
+    for r in range(64):
+        seg_t = tt[off[r]:off[r + 1]]
+        assert (np.diff(seg_t) >= 0).all()
+
+
+def test_empty_scene_and_ray_misses():
+    O = np.zeros((4, 3), np.float32)
+    v = np.tile(np.array([[0, 0, 1]], np.float32), (4, 1))
+    t, idx = oracle.hits(np.zeros((0, 12), np.float32), O, v, np.zeros(4, np.float32))
+    assert (idx == -1).all() and np.isinf(t).all()
+
+
+@pytest.mark.parametrize("base", [True, False])
+def test_grad_oracle_forward_matches_c_oracle(base):
+    sc = make_scene(3000, 1)
+    O, v = camera_rays(24, 24, 60.0, eye=(0.0, 0.0, 3.0))
+    fr = oracle.prep_frames(*sc.activated())
+    csr = oracle.hit_lists(fr, O, v)
+    ref = oracle.forward(sc, O, v, csr, "training", base=base)
+    d = np.zeros((576, 3), np.float32)
+    gr = grad_oracle.gradients(sc, O, v, csr, ref["nhits"], d, base=base)
+    np.testing.assert_allclose(gr["C"].numpy(), ref["rgb"], atol=2e-4)
+
+
+def test_grad_oracle_finite_difference():
+    """The autograd oracle against central differences of its own float64 forward (tiny scene)."""
+    sc = make_scene(200, 2)
+    O, v = camera_rays(8, 8, 40.0, eye=(0.0, 0.0, 3.0))
+    fr = oracle.prep_frames(*sc.activated())
+    csr = oracle.hit_lists(fr, O, v)
+    ref = oracle.forward(sc, O, v, csr, "training", base=True)
+    if ref["total_hits"] == 0:
+        pytest.skip("no hits")
+    dLdI = np.random.RandomState(0).randn(64, 3).astype(np.float32)
+    gr = grad_oracle.gradients(sc, O, v, csr, ref["nhits"], dLdI, base=True, exact_t=True)
+    hit_prims = np.unique(csr[2][:ref["total_hits"]])
+    p = int(hit_prims[0])
+    eps = 1e-6
+
+    def loss(delta_m):
+        sc2 = {k: (x.clone().double() if k != "m" else x.clone().double()) for k, x in sc.__dict__.items()}
+        sc2["m"][p, 0] += delta_m
+        g2 = grad_oracle.gradients(sc2, O, v, csr, ref["nhits"], np.zeros_like(dLdI), base=True, exact_t=True)
+        return float((torch.as_tensor(dLdI, dtype=torch.float64) * g2["C"]).sum())
+
+    fd = (loss(eps) - loss(-eps)) / (2 * eps)
+    assert fd == pytest.approx(float(gr["m"][p, 0]), rel=2e-3, abs=1e-7)
