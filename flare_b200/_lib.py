@@ -47,6 +47,12 @@ class Stats(ctypes.Structure):
                 ("prim_tests", ctypes.c_longlong), ("node_visits", ctypes.c_longlong)]
 
 
+class KernelTimes(ctypes.Structure):
+    _fields_ = [("ms", ctypes.c_double * 4), ("launches", ctypes.c_longlong * 4)]
+
+
+KERNEL_NAMES = ("build", "trace", "shade_forward", "shade_backward")
+
 # every entry point declared in include/flare_b200.h
 EXPORTS = {
     "flare_last_error": (ctypes.c_char_p, []),
@@ -61,6 +67,8 @@ EXPORTS = {
     "flare_backward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(BackwardArgs), vp]),
     "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
     "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
+    "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),
+    "flare_get_kernel_times": (ctypes.c_int, [vp, ctypes.POINTER(KernelTimes)]),
     "flare_selftest_mlp": (ctypes.c_int, [vp, ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp]),
 }
 

@@ -31,6 +31,34 @@ int check_status(flare_renderer *r, cudaStream_t st, const char *what) {
     return FLARE_OK;
 }
 
+int prof_begin(flare_renderer *r, int kind, cudaStream_t st) {
+    if (!r->prof_on) return -1;
+    if (r->prof_n >= flare_renderer::PROF_SLOTS) {
+        cudaStreamSynchronize(st);
+        prof_collect(r);
+    }
+    int slot = r->prof_n++;
+    r->prof_kind[slot] = kind;
+    cudaEventRecord(r->prof_ev[2 * slot], st);
+    return slot;
+}
+
+void prof_end(flare_renderer *r, int slot, cudaStream_t st) {
+    if (slot < 0) return;
+    cudaEventRecord(r->prof_ev[2 * slot + 1], st);
+}
+
+void prof_collect(flare_renderer *r) {
+    for (int i = 0; i < r->prof_n; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, r->prof_ev[2 * i], r->prof_ev[2 * i + 1]) == cudaSuccess) {
+            r->prof_ms[r->prof_kind[i]] += ms;
+            r->prof_launches[r->prof_kind[i]] += 1;
+        }
+    }
+    r->prof_n = 0;
+}
+
 int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
                  const void *A3, const float *b3, float *Y, cudaStream_t st, int *status);
 
@@ -140,6 +168,8 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
 int flare_destroy(flare_renderer *r) {
     if (!r) return FLARE_OK;
     DeviceGuard dg(r->device);
+    for (int i = 0; i < 2 * flare_renderer::PROF_SLOTS; ++i)
+        if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
                     r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dw, r->gscale, r->dstatus, r->dstats};
@@ -156,10 +186,16 @@ int flare_set_geometry(flare_renderer *r, const float *m, const float *scale, co
     CHECK_ARG(r, "flare_set_geometry: renderer is NULL");
     CHECK_ARG(n >= 0, "flare_set_geometry: n = %d < 0", n);
     CHECK_ARG(n == 0 || (m && scale && q && opacity && kappa), "flare_set_geometry: NULL tensor");
+    CHECK_ARG(((reinterpret_cast<uintptr_t>(q) & 15) | (reinterpret_cast<uintptr_t>(scale) & 7)) == 0,
+              "flare_set_geometry: q must be 16-byte aligned and scale 8-byte aligned");
     DeviceGuard dg(r->device);
+    int slot = prof_begin(r, PK_BUILD, S(stream));
     int e = build_geometry(r, m, scale, q, opacity, kappa, n, S(stream));
+    prof_end(r, slot, S(stream));
     if (e) return e;
-    return check_status(r, S(stream), "flare_set_geometry");
+    e = check_status(r, S(stream), "flare_set_geometry");
+    prof_collect(r);
+    return e;
 }
 
 int flare_render_hits(flare_renderer *r, const float *O, const float *v, const float *t_min, int n_rays, float *t_out,
@@ -194,6 +230,14 @@ static int check_scene(flare_renderer *r, const flare_scene *sc, const char *who
     if (sc->cond)
         CHECK_ARG(sc->features && sc->A1 && sc->A2 && sc->A3 && sc->b1 && sc->b2 && sc->b3,
                   "%s: decoder tensors missing", who);
+    // the kernels read q and RGBA as float4, s and the LUT as float2, the descriptor and weights in
+    // 16-byte chunks (as the reference's casts do)
+    auto al = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
+    CHECK_ARG(al(sc->q, 16) && al(sc->RGBA, 16) && al(sc->s, 8), "%s: q and RGBA must be 16-byte aligned, s 8-byte",
+              who);
+    if (sc->cond)
+        CHECK_ARG(al(sc->cond, 16) && al(sc->A1, 16) && al(sc->A2, 16) && al(sc->A3, 16) && al(sc->features, 8),
+                  "%s: descriptor and weights must be 16-byte aligned, features 8-byte", who);
     return FLARE_OK;
 }
 
@@ -255,6 +299,38 @@ int flare_get_stats(flare_renderer *r, flare_stats *out) {
     out->prim_tests = (long long)h[ST_PRIM_TESTS];
     out->node_visits = (long long)h[ST_NODES];
     out->rays = 0;
+    return FLARE_OK;
+}
+
+int flare_profile(flare_renderer *r, int enable) {
+    g_err[0] = 0;
+    CHECK_ARG(r, "flare_profile: renderer is NULL");
+    DeviceGuard dg(r->device);
+    if (enable && !r->prof_ev[0]) {
+        for (int i = 0; i < 2 * flare_renderer::PROF_SLOTS; ++i)
+            FLARE_CUDA_TRY(cudaEventCreate(&r->prof_ev[i]));
+    }
+    r->prof_on = enable != 0;
+    r->prof_n = 0;
+    for (int k = 0; k < 4; ++k) {
+        r->prof_ms[k] = 0.0;
+        r->prof_launches[k] = 0;
+    }
+    return FLARE_OK;
+}
+
+int flare_get_kernel_times(flare_renderer *r, flare_kernel_times *out) {
+    g_err[0] = 0;
+    CHECK_ARG(r && out, "flare_get_kernel_times: NULL argument");
+    DeviceGuard dg(r->device);
+    if (r->prof_n) {
+        FLARE_CUDA_TRY(cudaDeviceSynchronize());
+        prof_collect(r);
+    }
+    for (int k = 0; k < 4; ++k) {
+        out->ms[k] = r->prof_ms[k];
+        out->launches[k] = r->prof_launches[k];
+    }
     return FLARE_OK;
 }
 

@@ -39,6 +39,15 @@ struct flare_renderer {
     float *dw = nullptr;      // dense weight-gradient accumulators (see shade.cu)
     float *gscale = nullptr;  // backward gradient scale (1 float)
 
+    // ---- optional per-kernel timing (CUDA events on the launching stream) ----
+    bool prof_on = false;
+    static constexpr int PROF_SLOTS = 256;
+    cudaEvent_t prof_ev[2 * PROF_SLOTS] = {};
+    int prof_kind[PROF_SLOTS] = {};
+    int prof_n = 0;
+    double prof_ms[4] = {0, 0, 0, 0};
+    long long prof_launches[4] = {0, 0, 0, 0};
+
     // ---- status / statistics ----
     int *dstatus = nullptr;               // device status bits
     unsigned long long *dstats = nullptr; // flare::ST_* counters
@@ -62,6 +71,13 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
 int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
                  const void *A3, const float *b3, float *Y, cudaStream_t st);
+
+// api.cu: per-kernel timing; begin returns a slot (or -1 when profiling is off), collect needs the
+// stream synchronised.
+enum { PK_BUILD = 0, PK_TRACE = 1, PK_SHADE_FWD = 2, PK_SHADE_BWD = 3 };
+int prof_begin(flare_renderer *r, int kind, cudaStream_t st);
+void prof_end(flare_renderer *r, int slot, cudaStream_t st);
+void prof_collect(flare_renderer *r);
 
 // api.cu: reads the device status word after a call and turns set bits into an error.
 int check_status(flare_renderer *r, cudaStream_t st, const char *what);

@@ -102,7 +102,11 @@ struct BwdIO {
     const float *surface_normal;
     float lambda_depth, reg_a, reg_b, lambda_normal;
     const float *gscale;  // [0] = scale applied to delta3 operands
+    int vec4;             // dq and dcond are 16-byte aligned: use vector reductions
 };
+
+// dst[0..3] += (a, b, c, d): one vector reduction when 16-byte aligned, else four scalar atomics.
+__device__ __forceinline__ void red_add4(float *dst, bool vec, float a, float b, float c, float d);
 
 // ------------------------------------------------------------------------------------------------
 // per-hit geometry (reference Forward_training.cu:719-783 and Backward.cu:1527-1608)
@@ -607,6 +611,17 @@ __device__ __forceinline__ void red_add_v4(float *addr, float a, float b, float 
                  : "memory");
 }
 
+__device__ __forceinline__ void red_add4(float *dst, bool vec, float a, float b, float c, float d) {
+    if (vec) {
+        red_add_v4(dst, a, b, c, d);
+    } else {
+        atomicAdd(dst, a);
+        atomicAdd(dst + 1, b);
+        atomicAdd(dst + 2, c);
+        atomicAdd(dst + 3, d);
+    }
+}
+
 template <bool DEC>
 __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, BwdIO bo) {
     extern __shared__ __align__(1024) char smem[];
@@ -940,8 +955,8 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     if (valid) {
 #pragma unroll
                         for (int e = 0; e < 16; e += 4)
-                            red_add_v4(dc + 16 * b + e, v16[e] * ginv, v16[e + 1] * ginv, v16[e + 2] * ginv,
-                                       v16[e + 3] * ginv);
+                            red_add4(dc + 16 * b + e, bo.vec4, v16[e] * ginv, v16[e + 1] * ginv,
+                                     v16[e + 2] * ginv, v16[e + 3] * ginv);
                     }
                 }
                 tc_fence_before();
@@ -988,8 +1003,8 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                             a * Gm[2][0] + d * Gm[2][1] - 2.0f * c * Gm[2][2];
                 float dMd = -2.0f * d * Gm[0][0] - a * Gm[0][1] + b * Gm[0][2] + a * Gm[1][0] - 2.0f * d * Gm[1][1] +
                             c * Gm[1][2] + b * Gm[2][0] + c * Gm[2][1];
-                red_add_v4(bo.dq + 4 * (size_t)ind, S * (dMa - S * a * GM), S * (dMb - S * b * GM),
-                           S * (dMc - S * c * GM), S * (dMd - S * d * GM));
+                red_add4(bo.dq + 4 * (size_t)ind, bo.vec4, S * (dMa - S * a * GM), S * (dMb - S * b * GM),
+                         S * (dMc - S * c * GM), S * (dMd - S * d * GM));
             }
         }
         {
@@ -1160,7 +1175,8 @@ static int launch_fwd_mode(flare_renderer *r, int mode, const SceneP &sp, const 
 
 // Runs the pass loop: trace -> shade -> compaction, until no ray is active.
 template <typename ShadeFn>
-static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, cudaStream_t st, ShadeFn shade) {
+static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, cudaStream_t st, int shade_kind,
+                     ShadeFn shade) {
     int count = R;
     int cur = 0;
     long long passes = 0;
@@ -1170,13 +1186,18 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
             set_error("pass loop did not terminate after %lld passes", passes);
             return FLARE_E_DEVICE;
         }
+        int slot = prof_begin(r, PK_TRACE, st);
         int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, r->hit_t, r->hit_idx, count, st);
+        prof_end(r, slot, st);
         if (e) return e;
         FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
+        slot = prof_begin(r, shade_kind, st);
         e = shade(r->list[cur], count, r->list[cur ^ 1]);
+        prof_end(r, slot, st);
         if (e) return e;
         FLARE_CUDA_TRY(cudaMemcpyAsync(r->h_count, r->counters, sizeof(int), cudaMemcpyDeviceToHost, st));
         FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+        prof_collect(r);
         count = *r->h_count;
         cur ^= 1;
         ++passes;
@@ -1215,7 +1236,7 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
                                                        a->mode == FLARE_FWD_MEDIAN ? a->depth_and_index : nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
     PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
-    return pass_loop(r, a->O, a->v, R, st, [&](const int *lin, int count, int *lout) -> int {
+    return pass_loop(r, a->O, a->v, R, st, PK_SHADE_FWD, [&](const int *lin, int count, int *lout) -> int {
         PassP pp = base;
         pp.list_in = lin;
         pp.count = count;
@@ -1238,6 +1259,7 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     bo.surface_normal = a->surface_normal;
     bo.lambda_depth = a->lambda_depth; bo.reg_a = a->reg_a; bo.reg_b = a->reg_b; bo.lambda_normal = a->lambda_normal;
     bo.gscale = r->gscale;
+    bo.vec4 = ((reinterpret_cast<uintptr_t>(a->dL_dq) | reinterpret_cast<uintptr_t>(dec ? a->dL_dcond : a->dL_dq)) & 15) == 0;
     init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
     if (dec) {
@@ -1250,7 +1272,7 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
                                             SM_BWD_BYTES));
     }
     PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
-    int e = pass_loop(r, a->O, a->v, R, st, [&](const int *lin, int count, int *lout) -> int {
+    int e = pass_loop(r, a->O, a->v, R, st, PK_SHADE_BWD, [&](const int *lin, int count, int *lout) -> int {
         PassP pp = base;
         pp.list_in = lin;
         pp.count = count;

@@ -1,0 +1,157 @@
+"""Data-parallel FlaRe training step over one process per GPU.
+
+The reference trains on one GPU (CPyOptiXFLARERenderer_CUDA_Core.cu:52 fixes device 0); its step is
+train.py:449-858: SetGeometry on the activated parameters, Forward_training over a ray batch, an image
+loss and its gradient in torch, Backward into zeroed gradient buffers.  Here the same step runs on N
+ranks: the scene is replicated, the rays of the step's views are sharded by view (and by row band when
+there are more ranks than views), each rank renders and back-propagates its shard into one flat fp32
+gradient buffer, and a single all-reduce (NCCL over NVLink) sums that buffer once per step.  The loss is
+normalised by the global ray count, so the summed gradient equals the single-GPU gradient of the whole
+batch.
+
+Loss: L1 against a target image, on the image clamped to [0, 1] with the gradient masked where the
+clamp is active (the reference clamps before its loss, train.py:688-702).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from .scene import Scene
+
+T_NEAR, T_FAR = 0.1, 1000.0
+REG_A = -(T_NEAR * T_FAR) / (T_FAR - T_NEAR)
+REG_B = T_FAR / (T_FAR - T_NEAR)
+T_THRESHOLD_TRAINING = 1e-4  # arguments/__init__.py:129
+
+
+def shard_rays(n_views: int, rays_per_view: int, world: int, rank: int):
+    """This rank's (view, first ray, ray count) pieces.  Views are dealt round-robin; with more ranks
+    than views every view is cut into contiguous row bands, one per rank that shares it."""
+    if world <= n_views:
+        return [(v, 0, rays_per_view) for v in range(rank, n_views, world)]
+    per_view = world // n_views
+    if world % n_views:
+        raise ValueError(f"{world} ranks do not divide evenly over {n_views} views")
+    v = rank // per_view
+    b = rank % per_view
+    lo = rays_per_view * b // per_view
+    hi = rays_per_view * (b + 1) // per_view
+    return [(v, lo, hi - lo)]
+
+
+# gradient tensors of one step, in the order they sit in the flat buffer: name -> shape (N = primitives)
+def grad_layout(n: int, decoder: bool):
+    lay = [("loss", (1,)), ("RGB", (n, 3)), ("A", (n, 1)), ("k", (n, 1)), ("m", (n, 3)), ("s", (n, 2)), ("q", (n, 4))]
+    if decoder:
+        lay += [("cond", (n, 96)), ("features", (13154,)), ("w3", (1, 512)), ("b3", (1, 64)), ("w2", (1, 4096)),
+                ("b2", (1, 512)), ("w1", (1, 8192)), ("b1", (1, 512))]
+    return lay
+
+
+class GradBuffer:
+    """All gradients of a step as views into one contiguous fp32 buffer (one all-reduce per step)."""
+
+    ALIGN = 16  # floats: every segment starts on a 64-byte boundary (the kernels use vector reductions)
+
+    def __init__(self, n: int, decoder: bool, device):
+        self.layout = grad_layout(n, decoder)
+        offs, off = [], 0
+        for _, shape in self.layout:
+            offs.append(off)
+            cnt = int(torch.tensor(shape).prod())
+            off += (cnt + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+        self.flat = torch.zeros(off, dtype=torch.float32, device=device)
+        self.views = {}
+        for (name, shape), o in zip(self.layout, offs):
+            cnt = int(torch.tensor(shape).prod())
+            self.views[name] = self.flat[o:o + cnt].view(*shape)
+
+    def __getitem__(self, k):
+        return self.views[k]
+
+    def zero_(self):
+        self.flat.zero_()
+
+    def allreduce_(self, group=None):
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+            dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
+
+    @property
+    def nbytes(self):
+        return self.flat.numel() * 4
+
+
+@dataclass
+class Shard:
+    O: torch.Tensor
+    v: torch.Tensor
+    target: torch.Tensor
+
+
+class TrainStep:
+    """Runs SetGeometry + per-shard Forward_training / L1 loss / Backward + one all-reduce."""
+
+    def __init__(self, renderer, scene: Scene, shards, total_rays: int, decoder: bool = True, bg=(0.0, 0.0, 0.0),
+                 lambda_depth: float = 0.0, lambda_normal: float = 0.0, group=None):
+        self.r = renderer
+        self.sc = scene
+        self.decoder = decoder
+        self.shards = shards
+        self.total_rays = total_rays
+        self.bg = bg
+        self.lambda_depth = lambda_depth
+        self.lambda_normal = lambda_normal
+        self.group = group
+        dev = scene.m.device
+        self.grads = GradBuffer(scene.n, decoder, dev)
+        self.buf = []
+        for sh in shards:
+            R = sh.O.shape[0]
+            z = lambda *s: torch.zeros(*s, device=dev)  # noqa: E731
+            self.buf.append(dict(bitmap=z(R, 3), dacc=z(R, 4), nacc=z(R, 4), dai=z(R, 2), sn=z(R, 3), prefix=z(R, 4),
+                                 dLdI=z(R, 3)))
+        self.loss = self.grads["loss"]  # summed by the same all-reduce as the gradients
+        self.collect_stats = False
+        self.hits = 0
+
+    def geometry(self):
+        sc = self.sc
+        self.r.SetGeometry(sc.m, torch.exp(sc.s), sc.q, torch.sigmoid(sc.RGBA[:, 3]).contiguous(),
+                           (1.0 + torch.nn.functional.softplus(sc.k[:, 0])).contiguous())
+
+    def __call__(self):
+        sc, r, G = self.sc, self.r, self.grads
+        self.geometry()
+        G.zero_()
+        inv = 1.0 / (3.0 * self.total_rays)
+        for sh, b in zip(self.shards, self.buf):
+            for k in ("bitmap", "dacc", "nacc", "prefix"):
+                b[k].zero_()
+            fargs = (sh.O, sh.v, b["bitmap"], *self.bg, sc.m, sc.s, sc.q, sc.RGBA, sc.k, T_THRESHOLD_TRAINING, b["dacc"],
+                     REG_A, REG_B, b["dai"], b["sn"], b["nacc"])
+            if self.decoder:
+                dec = (sc.cond, sc.features, sc.A1, sc.b1, sc.A2, sc.b2, sc.A3, sc.b3)
+                r.Forward_training(*dec, *fargs)
+            else:
+                r.Forward_training_base(*fargs)
+            if self.collect_stats:
+                self.hits += r.stats()["hits_composited"]
+            img = b["bitmap"].clamp(0.0, 1.0)
+            diff = img - sh.target
+            self.loss += diff.abs().sum() * inv
+            torch.mul(torch.sign(diff), inv * (img == b["bitmap"]).float(), out=b["dLdI"])
+            I = img.contiguous()
+            if self.decoder:
+                r.Backward(*dec, sh.O, sh.v, *self.bg, sc.m, sc.s, sc.q, sc.RGBA, sc.k, I, b["dLdI"], G["RGB"], G["A"],
+                           G["k"], G["w3"], G["b3"], G["w2"], G["b2"], G["w1"], G["b1"], G["cond"], G["features"],
+                           G["m"], G["s"], G["q"], T_THRESHOLD_TRAINING, b["dacc"], b["prefix"],
+                           self.lambda_depth, REG_A, REG_B, b["dai"], b["sn"], b["nacc"], self.lambda_normal)
+            else:
+                r.Backward_base(sh.O, sh.v, *self.bg, sc.m, sc.s, sc.q, sc.RGBA, sc.k, I, b["dLdI"], G["RGB"], G["A"],
+                                G["k"], G["m"], G["s"], G["q"], T_THRESHOLD_TRAINING, b["dacc"], b["prefix"],
+                                self.lambda_depth, REG_A, REG_B, b["dai"], b["sn"], b["nacc"], self.lambda_normal)
+        G.allreduce_(self.group)
+        return self.loss

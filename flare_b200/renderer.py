@@ -281,6 +281,16 @@ class CPyOptiXFLARERenderer:
         _lib.check(self._lib.flare_get_stats(self._h, ctypes.byref(st)), "stats")
         return {k: getattr(st, k) for k, _ in _lib.Stats._fields_}
 
+    def profile(self, enable: bool = True):
+        """Enables (and zeroes) or disables per-kernel CUDA-event timing."""
+        _lib.check(self._lib.flare_profile(self._h, 1 if enable else 0), "profile")
+
+    def kernel_times(self):
+        """{kernel: (total ms, launches)} accumulated since profile(True)."""
+        kt = _lib.KernelTimes()
+        _lib.check(self._lib.flare_get_kernel_times(self._h, ctypes.byref(kt)), "kernel_times")
+        return {n: (kt.ms[i], kt.launches[i]) for i, n in enumerate(_lib.KERNEL_NAMES)}
+
     def frames(self):
         """Per-primitive proxy frames (N,12) of the last SetGeometry (used by the hit-list parity test)."""
         out = torch.empty((self._n, 12), dtype=F32, device=f"cuda:{self.device}")

@@ -170,6 +170,19 @@ typedef struct flare_stats {
 int flare_get_stats(flare_renderer *r, flare_stats *out);
 
 /*
+ * Per-kernel device time, measured with CUDA events recorded on the caller's stream around every
+ * launch while profiling is enabled (flare_profile(r, 1) enables and zeroes the counters).  Index 0
+ * LBVH build (whole flare_set_geometry), 1 traversal, 2 forward shading, 3 backward shading.  No
+ * reference counterpart (the reference logs wall-clock FPS only, train.py:1459-1491).
+ */
+typedef struct flare_kernel_times {
+    double ms[4];
+    long long launches[4];
+} flare_kernel_times;
+int flare_profile(flare_renderer *r, int enable);
+int flare_get_kernel_times(flare_renderer *r, flare_kernel_times *out);
+
+/*
  * Exposes the per-primitive polygon frames built by the last flare_set_geometry, for the bit-exact
  * hit-list test: frames (N,12) f32 = [m.xyz, N.xyz, U/(e^sx rho).xyz, V/(e^sy rho).xyz] in primitive
  * order.  Device pointer to caller storage; synchronous on `stream`.
