@@ -75,11 +75,13 @@ EXPORTS = {
 _lib = None
 
 
-def load(path: str = LIB_PATH):
-    """Loads libflare_b200.so and declares every exported signature.  Raises if it is missing."""
+def load(path: str = None):
+    """Loads libflare_b200.so (or the file named by $FLARE_B200_LIB) and declares every exported
+    signature.  Raises if it is missing."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("FLARE_B200_LIB") or LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(f"flare_b200: native library not found at {path}; run `python -m flare_b200.build`")
     lib = ctypes.CDLL(path)

@@ -135,6 +135,12 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
             r->poly.c[j] = (float)(std::cos(phi) / ap);
             r->poly.s[j] = (float)(std::sin(phi) / ap);
         }
+        // fmaf(-c, a, (-s) * b) == -fmaf(c, a, s * b) exactly, so opposite edges fold into one |.| test
+        // whenever the rounded constants are exactly antisymmetric
+        bool sym = number_of_sides % 2 == 0;
+        for (int j = 0; sym && j < number_of_sides / 2; ++j)
+            sym = r->poly.c[j + number_of_sides / 2] == -r->poly.c[j] && r->poly.s[j + number_of_sides / 2] == -r->poly.s[j];
+        r->poly.half = sym ? number_of_sides / 2 : 0;
     }
     size_t R = (size_t)(max_batch_size > 0 ? max_batch_size : 1);
     cudaError_t e = cudaSuccess;
@@ -149,7 +155,14 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
     ALLOC(r->counters, 64 * sizeof(int));
     ALLOC(r->dw, 16384 * sizeof(float));
     ALLOC(r->gscale, 64);
-    ALLOC(r->bounds, 64);
+    ALLOC(r->dfeat_priv, (size_t)r->num_sms * 2 * 13184 * sizeof(float));
+    ALLOC(r->bounds, 128);
+    ALLOC(r->ray_keys, 2 * R * sizeof(unsigned long long));
+    ALLOC(r->ray_ids_tmp, R * sizeof(int));
+    if (e == cudaSuccess) {
+        r->ray_sort_tmp_bytes = ray_sort_temp_bytes((int)R);
+        e = cudaMalloc(&r->ray_sort_tmp, r->ray_sort_tmp_bytes);
+    }
     ALLOC(r->dstatus, 64);
     ALLOC(r->dstats, ST_NSTATS * sizeof(unsigned long long));
 #undef ALLOC
@@ -172,7 +185,7 @@ int flare_destroy(flare_renderer *r) {
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
-                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dw, r->gscale, r->dstatus, r->dstats};
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->dw, r->gscale, r->dstatus, r->dstats};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (r->h_count) cudaFreeHost(r->h_count);

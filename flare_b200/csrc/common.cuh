@@ -36,6 +36,7 @@ struct __align__(16) Node {
 // Polygon edge constants for the hit test (host computes them once per renderer).
 struct PolyConst {
     int n;
+    int half;  // n even and edge j+n/2 == -(edge j) exactly: test |c a + s b| <= 1 for j < n/2 only
     float c[MAX_SIDES];
     float s[MAX_SIDES];
 };

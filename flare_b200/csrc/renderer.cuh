@@ -33,11 +33,16 @@ struct flare_renderer {
     int *hit_idx = nullptr;   // (16, max_rays)
     float *ray_aux = nullptr; // (max_rays, 4) per-ray carried state (backward running colour, median)
     int *counters = nullptr;  // [0] next active count, [1..] scratch
+    unsigned long long *ray_keys = nullptr;  // (2, max_rays) ray-ordering keys (trace.cu)
+    int *ray_ids_tmp = nullptr;              // (max_rays)
+    void *ray_sort_tmp = nullptr;
+    size_t ray_sort_tmp_bytes = 0;
     int *h_count = nullptr;   // pinned host mirror of counters[0]
 
     // ---- decoder scratch ----
     float *dw = nullptr;      // dense weight-gradient accumulators (see shade.cu)
     float *gscale = nullptr;  // backward gradient scale (1 float)
+    float *dfeat_priv = nullptr;  // per-CTA LUT gradient copies (2 * num_sms * 13184 floats)
 
     // ---- optional per-kernel timing (CUDA events on the launching stream) ----
     bool prof_on = false;
@@ -65,8 +70,11 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
                  int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st);
 
+// trace.cu: writes the coherence order of R rays into list_out
+int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st);
+size_t ray_sort_temp_bytes(int max_rays);
+
 // shade.cu
-struct ShadeArgs;  // defined in shade.cu
 int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st);
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
 int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,

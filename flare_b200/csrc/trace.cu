@@ -10,6 +10,8 @@
 //
 // The hit test is exact fp32 with explicit rounding intrinsics; oracle/trace_oracle.c executes the
 // identical sequence, which is what makes hit lists bit-comparable.
+#include <cub/device/device_radix_sort.cuh>
+
 #include "renderer.cuh"
 
 namespace flare {
@@ -36,22 +38,26 @@ __device__ __forceinline__ void kbuf_insert(KBuf &b, float t, int id) {
 
 // Exact hit test on the record of sorted primitive p (same operation order as the oracle).
 __device__ __forceinline__ bool hit_prim(const float4 *__restrict__ rec, int p, float3 O, float3 v, float t_min,
-                                         const PolyConst &c_poly, float &t_out) {
+                                         const PolyConst &c_poly, float &t_out, float t_max = INFINITY) {
     float4 r0 = __ldg(rec + 3 * (size_t)p), r1 = __ldg(rec + 3 * (size_t)p + 1), r2 = __ldg(rec + 3 * (size_t)p + 2);
     // r0 = m.xyz N.x, r1 = N.yz Ua.xy, r2 = Ua.z Va.xyz
     float dx = __fsub_rn(r0.x, O.x), dy = __fsub_rn(r0.y, O.y), dz = __fsub_rn(r0.z, O.z);
     float num = __fmaf_rn(r0.w, dx, __fmaf_rn(r1.x, dy, __fmul_rn(r1.y, dz)));
     float den = __fmaf_rn(r0.w, v.x, __fmaf_rn(r1.x, v.y, __fmul_rn(r1.y, v.z)));
     float t = __fdiv_rn(num, den);
-    if (!(t >= t_min)) return false;
+    if (!(t >= t_min) || t > t_max) return false;  // beyond the 16th hit: cannot enter the buffer
     float ex = __fsub_rn(__fmaf_rn(v.x, t, O.x), r0.x);
     float ey = __fsub_rn(__fmaf_rn(v.y, t, O.y), r0.y);
     float ez = __fsub_rn(__fmaf_rn(v.z, t, O.z), r0.z);
     float a = __fmaf_rn(r1.z, ex, __fmaf_rn(r1.w, ey, __fmul_rn(r2.x, ez)));
     float b = __fmaf_rn(r2.y, ex, __fmaf_rn(r2.z, ey, __fmul_rn(r2.w, ez)));
-    const int ns = c_poly.n;
-    for (int j = 0; j < ns; ++j)
-        if (!(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b)) <= 1.0f)) return false;
+    if (c_poly.half) {
+        for (int j = 0; j < c_poly.half; ++j)
+            if (!(fabsf(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b))) <= 1.0f)) return false;
+    } else {
+        for (int j = 0; j < c_poly.n; ++j)
+            if (!(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b)) <= 1.0f)) return false;
+    }
     t_out = t;
     return true;
 }
@@ -182,11 +188,238 @@ __global__ void __launch_bounds__(128) trace_kernel(const float *__restrict__ O_
     }
 }
 
+// Warp-packet variant: the 32 rays of a warp share one traversal stack (in shared memory) and every node
+// fetch; each lane keeps its own k-buffer and interval [t_min, t_16], and a child is entered when any
+// lane's interval overlaps its box (lane masks ride on the stack).  Control flow is warp-uniform, so
+// the per-ray divergence of the one-thread-per-ray walk disappears; coherent rays (sorted by origin and
+// direction before the first pass) share most of their node visits.  The hit set is the same exact
+// k-nearest set as any other traversal order.
+template <bool STATS>
+__global__ void __launch_bounds__(128, 6) trace_packet_kernel(
+    const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
+    const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
+    const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats) {
+    __shared__ int s_node[4][TRACE_STACK];
+    __shared__ unsigned s_mask[4][TRACE_STACK];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = j < count;
+    unsigned long long nprim = 0, nnode = 0;
+    int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
+    float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+    float t_min = INFINITY;
+    if (live) {
+        O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
+        v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
+        t_min = tmin_[ray];
+    }
+    KBuf kb;
+#pragma unroll
+    for (int k = 0; k < K_HITS; ++k) {
+        kb.t[k] = INFINITY;
+        kb.i[k] = 0x7fffffff;
+    }
+    const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
+                                  1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
+                                  1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
+    const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);
+    const bool want = live && t_min < INFINITY;
+    if (n == 1) {
+        float t;
+        if (want) {
+            ++nprim;
+            if (hit_prim(rec, 0, O, v, t_min, poly, t)) kbuf_insert(kb, t, ids[0]);
+        }
+    } else if (n > 1) {
+        unsigned mask = __ballot_sync(0xffffffffu, want);
+        int node = 0, sp = 0;
+        const unsigned long long max_visits = 2ull * (unsigned long long)n + 64ull;
+        while (mask) {
+            if (++nnode > max_visits) {
+                if (lane == 0) atomicOr(status, ERR_INDEX);
+                break;
+            }
+            const bool in = (mask >> lane) & 1u;
+            const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
+            const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
+            const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
+            const float thi = __fmaf_rn(fabsf(kb.t[K_HITS - 1]), 1e-5f, kb.t[K_HITS - 1]);
+            float t0 = 0.0f, t1 = 0.0f;
+            bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
+            bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
+            if (d.x < 0) {  // warp-uniform: leaf child 0
+                if (h0) {
+                    float t;
+                    ++nprim;
+                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, kb.t[K_HITS - 1])) {
+                        const int pid = __ldg(ids + ~d.x);
+                        if (t < kb.t[K_HITS - 1] || (t == kb.t[K_HITS - 1] && pid < kb.i[K_HITS - 1]))
+                            kbuf_insert(kb, t, pid);
+                    }
+                }
+                h0 = false;
+            }
+            if (d.y < 0) {
+                if (h1) {
+                    float t;
+                    ++nprim;
+                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, kb.t[K_HITS - 1])) {
+                        const int pid = __ldg(ids + ~d.y);
+                        if (t < kb.t[K_HITS - 1] || (t == kb.t[K_HITS - 1] && pid < kb.i[K_HITS - 1]))
+                            kbuf_insert(kb, t, pid);
+                    }
+                }
+                h1 = false;
+            }
+            const unsigned m0 = __ballot_sync(0xffffffffu, h0), m1 = __ballot_sync(0xffffffffu, h1);
+            if (m0 && m1) {
+                // nearer child first by lane vote (lanes that hit only one child vote for it)
+                const unsigned v0 = __ballot_sync(0xffffffffu, h0 && (!h1 || t0 <= t1));
+                const bool first0 = __popc(v0) * 2 >= __popc(m0 | m1);
+                if (sp < TRACE_STACK) {
+                    if (lane == 0) {
+                        s_node[wib][sp] = first0 ? d.y : d.x;
+                        s_mask[wib][sp] = first0 ? m1 : m0;
+                    }
+                    ++sp;
+                } else if (lane == 0) {
+                    atomicOr(status, ERR_STACK);
+                }
+                node = first0 ? d.x : d.y;
+                mask = first0 ? m0 : m1;
+                __syncwarp();
+                continue;
+            }
+            if (m0) { node = d.x; mask = m0; continue; }
+            if (m1) { node = d.y; mask = m1; continue; }
+            __syncwarp();
+            if (sp == 0) break;
+            --sp;
+            node = s_node[wib][sp];
+            mask = s_mask[wib][sp];
+        }
+    }
+    if (live) {
+#pragma unroll
+        for (int k = 0; k < K_HITS; ++k) {
+            const bool valid = kb.i[k] != 0x7fffffff;
+            t_out[(size_t)k * stride + j] = valid ? kb.t[k] : INFINITY;
+            idx_out[(size_t)k * stride + j] = valid ? kb.i[k] : -1;
+        }
+    }
+    if (STATS) {
+        for (int o = 16; o > 0; o >>= 1) nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
+        if (lane == 0 && (nprim | nnode)) {
+            atomicAdd(stats + ST_PRIM_TESTS, nprim);
+            atomicAdd(stats + ST_NODES, nnode);
+        }
+    }
+}
+
+
+// ------------------------------------------------------------------------------------------------
+// Ray ordering: rays are visited in the order of a 64-bit key, origin Morton code (30 bits, within the
+// batch's origin bounds) above the Morton code of the octahedral direction (2 x 16 bits), so the 32 rays
+// of a packet are neighbours in origin and direction whatever order the caller passed them in.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ int ord_f(float f) {
+    int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float ord_inv(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7FFFFFFF); }
+
+__global__ void origin_bounds_kernel(const float *__restrict__ O, int R, int *__restrict__ bounds) {
+    float lo[3] = {INFINITY, INFINITY, INFINITY}, hi[3] = {-INFINITY, -INFINITY, -INFINITY};
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < R; i += gridDim.x * blockDim.x)
+        for (int a = 0; a < 3; ++a) {
+            float x = O[3 * (size_t)i + a];
+            lo[a] = fminf(lo[a], x);
+            hi[a] = fmaxf(hi[a], x);
+        }
+    for (int a = 0; a < 3; ++a)
+        for (int o = 16; o > 0; o >>= 1) {
+            lo[a] = fminf(lo[a], __shfl_xor_sync(0xffffffffu, lo[a], o));
+            hi[a] = fmaxf(hi[a], __shfl_xor_sync(0xffffffffu, hi[a], o));
+        }
+    if ((threadIdx.x & 31) == 0 && lo[0] <= hi[0])
+        for (int a = 0; a < 3; ++a) {
+            atomicMin(bounds + a, ord_f(lo[a]));
+            atomicMax(bounds + 3 + a, ord_f(hi[a]));
+        }
+}
+
+__device__ __forceinline__ unsigned long long spread16(unsigned x) {
+    unsigned long long v = x & 0xFFFFu;
+    v = (v | (v << 8)) & 0x00FF00FFull;
+    v = (v | (v << 4)) & 0x0F0F0F0Full;
+    v = (v | (v << 2)) & 0x33333333ull;
+    v = (v | (v << 1)) & 0x55555555ull;
+    return v;
+}
+__device__ __forceinline__ unsigned spread10(unsigned v) {
+    v = (v * 0x00010001u) & 0xFF0000FFu;
+    v = (v * 0x00000101u) & 0x0F00F00Fu;
+    v = (v * 0x00000011u) & 0xC30C30C3u;
+    v = (v * 0x00000005u) & 0x49249249u;
+    return v;
+}
+
+__global__ void ray_key_kernel(const float *__restrict__ O, const float *__restrict__ v, int R,
+                               const int *__restrict__ bounds, unsigned long long *__restrict__ keys,
+                               int *__restrict__ ids) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= R) return;
+    unsigned oc = 0;
+    for (int a = 0; a < 3; ++a) {
+        float lo = ord_inv(bounds[a]), hi = ord_inv(bounds[3 + a]);
+        float x = hi > lo ? (O[3 * (size_t)i + a] - lo) / (hi - lo) : 0.5f;
+        oc |= spread10((unsigned)fminf(fmaxf(x * 1024.0f, 0.0f), 1023.0f)) << (2 - a);
+    }
+    float dx = v[3 * (size_t)i], dy = v[3 * (size_t)i + 1], dz = v[3 * (size_t)i + 2];
+    float l1 = fabsf(dx) + fabsf(dy) + fabsf(dz);
+    float px = l1 > 0.0f ? dx / l1 : 0.0f, py = l1 > 0.0f ? dy / l1 : 0.0f;
+    if (dz < 0.0f) {  // octahedral fold of the lower hemisphere
+        float qx = (1.0f - fabsf(py)) * copysignf(1.0f, px), qy = (1.0f - fabsf(px)) * copysignf(1.0f, py);
+        px = qx;
+        py = qy;
+    }
+    unsigned ux = (unsigned)fminf(fmaxf((px * 0.5f + 0.5f) * 65536.0f, 0.0f), 65535.0f);
+    unsigned uy = (unsigned)fminf(fmaxf((py * 0.5f + 0.5f) * 65536.0f, 0.0f), 65535.0f);
+    keys[i] = ((unsigned long long)oc << 32) | (spread16(ux) << 1) | spread16(uy);
+    ids[i] = i;
+}
+
+__global__ void init_bounds6_kernel(int *b) {
+    if (threadIdx.x < 3) b[threadIdx.x] = 0x7FFFFFFF;
+    else if (threadIdx.x < 6) b[threadIdx.x] = (int)0x80000000;
+}
+
+int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st) {
+    if (R <= 1) return FLARE_OK;
+    int *bounds = reinterpret_cast<int *>(r->bounds) + 8;
+    init_bounds6_kernel<<<1, 32, 0, st>>>(bounds);
+    origin_bounds_kernel<<<std::min((R + 255) / 256, 1184), 256, 0, st>>>(O, R, bounds);
+    ray_key_kernel<<<(R + 255) / 256, 256, 0, st>>>(O, v, R, bounds, r->ray_keys, r->ray_ids_tmp);
+    size_t tmp = r->ray_sort_tmp_bytes;
+    FLARE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(r->ray_sort_tmp, tmp, r->ray_keys, r->ray_keys + r->max_rays,
+                                                   r->ray_ids_tmp, list_out, R, 0, 64, st));
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+size_t ray_sort_temp_bytes(int max_rays) {
+    size_t tmp = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, tmp, (unsigned long long *)nullptr, (unsigned long long *)nullptr,
+                                    (int *)nullptr, (int *)nullptr, max_rays, 0, 64, (cudaStream_t)0);
+    return tmp;
+}
+
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
                  int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st) {
     if (count <= 0) return FLARE_OK;
     const int B = 128;
-    trace_kernel<true><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes, r->rec,
+    trace_packet_kernel<true><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes, r->rec,
                                                            r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
                                                            r->dstatus, r->dstats);
     FLARE_CUDA_TRY(cudaGetLastError());
