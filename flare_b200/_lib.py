@@ -70,6 +70,8 @@ EXPORTS = {
     "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),
     "flare_get_kernel_times": (ctypes.c_int, [vp, ctypes.POINTER(KernelTimes)]),
     "flare_selftest_mlp": (ctypes.c_int, [vp, ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "flare_render_hits_noalloc": (ctypes.c_int, [ctypes.c_int, vp, vp, vp, vp, vp, ctypes.c_int, vp, vp, vp,
+                                                 ctypes.c_int, vp, vp, vp]),
 }
 
 _lib = None

@@ -254,4 +254,33 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
     return FLARE_OK;
 }
 
+// The same build over an explicit buffer set (used by the allocation-free entry point in noalloc.cu).
+int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, const float *q, const float *opacity,
+                        const float *kappa, int n, cudaStream_t st) {
+    if (n == 0) return FLARE_OK;
+    const int B = 256;
+    int G = (n + B - 1) / B;
+    init_bounds_kernel<<<1, 32, 0, st>>>(reinterpret_cast<int *>(g.bounds));
+    prep_kernel<<<G, B, 0, st>>>(m, scale, q, opacity, kappa, n, g.frames, g.aabb, reinterpret_cast<int *>(g.bounds));
+    morton_kernel<<<G, B, 0, st>>>(m, n, reinterpret_cast<int *>(g.bounds), g.morton, g.ids);
+    size_t tmp = g.sort_tmp_bytes;
+    FLARE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(g.sort_tmp, tmp, g.morton, g.morton_sorted, g.ids, g.ids_sorted, n,
+                                                   0, 30, st));
+    if (n > 1) {
+        FLARE_CUDA_TRY(cudaMemsetAsync(g.refit_flag, 0, (size_t)(n - 1) * sizeof(unsigned), st));
+        karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(g.morton_sorted, n, g.nodes, g.parent);
+    }
+    refit_kernel<<<G, B, 0, st>>>(n, g.ids_sorted, g.aabb, g.nodes, g.parent, g.refit_flag, g.rec, g.frames, g.status);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+size_t geometry_sort_temp_bytes(int n) {
+    size_t tmp = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, tmp, (unsigned *)nullptr, (unsigned *)nullptr, (int *)nullptr,
+                                    (int *)nullptr, n, 0, 30, (cudaStream_t)0);
+    return tmp;
+}
+
 }  // namespace flare
+

@@ -61,6 +61,27 @@ struct flare_renderer {
 
 namespace flare {
 
+// bvh.cu: the geometry buffers of one build over caller-chosen memory (allocation-free entry point)
+struct GeomBufs {
+    float *frames;
+    float4 *rec;
+    float *aabb;
+    unsigned *morton, *morton_sorted;
+    int *ids, *ids_sorted;
+    Node *nodes;
+    int *parent;
+    unsigned *refit_flag;
+    float *bounds;
+    void *sort_tmp;
+    size_t sort_tmp_bytes;
+    int *status;
+};
+int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, const float *q, const float *opacity,
+                        const float *kappa, int n, cudaStream_t st);
+size_t geometry_sort_temp_bytes(int n);
+int launch_trace_geom(const Node *nodes, const float4 *rec, const int *ids_sorted, int n, const PolyConst &poly,
+                      const float *O, const float *v, const float *t_min, int count, float *t_out, int *idx_out,
+                      int *status, cudaStream_t st);
 // bvh.cu
 int build_geometry(flare_renderer *r, const float *m, const float *scale, const float *q, const float *opacity,
                    const float *kappa, int n, cudaStream_t st);

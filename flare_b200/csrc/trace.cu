@@ -426,4 +426,17 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
     return FLARE_OK;
 }
 
+// The same traversal over explicit geometry (used by the allocation-free entry point in noalloc.cu).
+int launch_trace_geom(const Node *nodes, const float4 *rec, const int *ids_sorted, int n, const PolyConst &poly,
+                      const float *O, const float *v, const float *t_min, int count, float *t_out, int *idx_out,
+                      int *status, cudaStream_t st) {
+    if (count <= 0) return FLARE_OK;
+    const int B = 128;
+    trace_packet_kernel<false><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, nullptr, count, nodes, rec, ids_sorted,
+                                                                   n, t_out, idx_out, count, poly, status, nullptr);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
 }  // namespace flare
+

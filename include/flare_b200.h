@@ -190,6 +190,23 @@ int flare_get_kernel_times(flare_renderer *r, flare_kernel_times *out);
 int flare_get_frames(flare_renderer *r, float *frames_out, void *stream);
 
 /*
+ * Allocation-free 16-nearest-hit query.  No counterpart in the reference, whose renderer allocates its
+ * scratch in the constructor and in SetGeometry.  For callers that cannot allocate device memory when
+ * they call (during a CUDA stream capture, under a fixed device-memory budget, or as a plugin in a
+ * process whose allocator owns the device): builds the proxy hierarchy for n_prims <=
+ * FLARE_NOALLOC_MAX_PRIMS primitives from SetGeometry's activated inputs and writes the same (16, n_rays)
+ * t / idx as flare_set_geometry + flare_render_hits, with all scratch (about 11 MB) in a static device
+ * array that every GPU loading the library holds until exit.  Larger scenes return FLARE_E_INVALID.
+ * The first call on a device resolves the array's address; make it before any stream capture.  Calls
+ * share the array, so calls that overlap on the GPU race and must be serialised by the caller.  The
+ * call synchronises `stream` to read its status word.
+ */
+#define FLARE_NOALLOC_MAX_PRIMS 32768
+int flare_render_hits_noalloc(int number_of_sides, const float *m, const float *scale, const float *q,
+                              const float *opacity, const float *kappa, int n_prims, const float *O, const float *v,
+                              const float *t_min, int n_rays, float *t_out, int *idx_out, void *stream);
+
+/*
  * Decoder self-test: runs the renderer's tensor-core MLP on `rows` fp16 input rows X (rows,128) and
  * writes the 16 fp32 layer-3 outputs per row to Y (rows,16).  Used by the tests to check the MLP
  * tiles against a host reference independently of tracing.
