@@ -155,6 +155,7 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
     ALLOC(r->counters, 64 * sizeof(int));
     ALLOC(r->dw, 16384 * sizeof(float));
     ALLOC(r->gscale, 64);
+    ALLOC(r->hc_sum, 64);
     ALLOC(r->dfeat_priv, (size_t)r->num_sms * 2 * 13184 * sizeof(float));
     ALLOC(r->bounds, 128);
     ALLOC(r->ray_keys, 2 * R * sizeof(unsigned long long));
@@ -185,7 +186,7 @@ int flare_destroy(flare_renderer *r) {
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
-                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->dw, r->gscale, r->dstatus, r->dstats};
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (r->h_count) cudaFreeHost(r->h_count);
@@ -203,6 +204,8 @@ int flare_set_geometry(flare_renderer *r, const float *m, const float *scale, co
               "flare_set_geometry: q must be 16-byte aligned and scale 8-byte aligned");
     DeviceGuard dg(r->device);
     int slot = prof_begin(r, PK_BUILD, S(stream));
+    ++r->geom_version;
+    r->hc_valid = false;
     int e = build_geometry(r, m, scale, q, opacity, kappa, n, S(stream));
     prof_end(r, slot, S(stream));
     if (e) return e;

@@ -44,6 +44,21 @@ struct flare_renderer {
     float *gscale = nullptr;  // backward gradient scale (1 float)
     float *dfeat_priv = nullptr;  // per-CTA LUT gradient copies (2 * num_sms * 13184 floats)
 
+    // ---- hit cache: the passes of the last Forward_training, replayed by a matching Backward ----
+    unsigned long long geom_version = 0;  // bumped by every flare_set_geometry
+    int *hc_list = nullptr;               // per pass: the active ray ids
+    float *hc_t = nullptr;                // per pass: (16, count) slot-major hits
+    int *hc_idx = nullptr;
+    size_t hc_cap = 0;                    // capacity in ray-passes
+    size_t hc_need = 0;                   // ray-passes the last uncached forward needed
+    bool hc_valid = false;
+    int hc_npass = 0;
+    static constexpr int HC_MAX_PASSES = 4096;
+    size_t hc_off[HC_MAX_PASSES] = {};
+    int hc_cnt[HC_MAX_PASSES] = {};
+    unsigned long long hc_key[16] = {};    // pointer / size signature of the cached forward
+    unsigned long long *hc_sum = nullptr; // device: [0] forward input checksum, [1] backward input checksum
+
     // ---- optional per-kernel timing (CUDA events on the launching stream) ----
     bool prof_on = false;
     static constexpr int PROF_SLOTS = 256;

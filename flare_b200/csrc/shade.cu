@@ -25,6 +25,9 @@
 // (from max |dL/dI|) so small image gradients do not underflow.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+#include <cstring>
+
 #include "renderer.cuh"
 #include "umma.cuh"
 
@@ -1209,26 +1212,149 @@ static int launch_fwd_mode(flare_renderer *r, int mode, const SceneP &sp, const 
     return FLARE_E_INVALID;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Hit cache.  A Backward re-walks exactly the passes of the Forward_training that produced its image
+// (same rays, geometry and parameters give the same active rays and the same 16-hit lists per pass), so
+// the forward keeps each pass's active-ray list and hit lists and a matching backward replays them
+// instead of tracing again.  "Matching" is checked by a pointer/size signature and by a checksum of the
+// contents of every input the pass sequence depends on (rays, primitive parameters, decoder).
+// ------------------------------------------------------------------------------------------------
+struct HashBufs {
+    const unsigned *p[16];
+    unsigned long long n[16];
+    int count;
+};
+
+__global__ void checksum_kernel(HashBufs hb, unsigned long long *out) {
+    unsigned long long acc = 0;
+    for (int b = 0; b < hb.count; ++b) {
+        const unsigned *p = hb.p[b];
+        const unsigned long long n = hb.n[b];
+        for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+             i += (unsigned long long)gridDim.x * blockDim.x) {
+            unsigned long long x = ((unsigned long long)__ldg(p + i) << 32) ^ (i * 0x9E3779B97F4A7C15ull) ^ (unsigned long long)b;
+            x ^= x >> 33;
+            x *= 0xff51afd7ed558ccdull;
+            x ^= x >> 33;
+            acc += x;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(out, acc);
+}
+
+static int input_checksum(flare_renderer *r, const flare_scene *sc, const float *O, const float *v, int R,
+                          unsigned long long *out, cudaStream_t st) {
+    HashBufs hb{};
+    auto add = [&](const void *p, size_t bytes) {
+        if (p && bytes >= 4 && hb.count < 16) {
+            hb.p[hb.count] = static_cast<const unsigned *>(p);
+            hb.n[hb.count] = bytes / 4;
+            ++hb.count;
+        }
+    };
+    const size_t n = (size_t)sc->n;
+    add(O, (size_t)R * 12);
+    add(v, (size_t)R * 12);
+    add(sc->m, n * 12);
+    add(sc->s, n * 8);
+    add(sc->q, n * 16);
+    add(sc->RGBA, n * 16);
+    add(sc->k, n * 4);
+    if (sc->cond) {
+        add(sc->cond, n * 192);
+        add(sc->features, (size_t)LUT * 4);
+        add(sc->A1, 64 * 128 * 2);
+        add(sc->A2, 64 * 64 * 2);
+        add(sc->A3, 16 * 64 * 2);
+        add(sc->b1, 64 * 4);
+        add(sc->b2, 64 * 4);
+        add(sc->b3, 16 * 4);
+    }
+    FLARE_CUDA_TRY(cudaMemsetAsync(out, 0, sizeof(unsigned long long), st));
+    checksum_kernel<<<r->num_sms * 4, 256, 0, st>>>(hb, out);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+static void cache_key(const flare_scene *sc, const float *O, const float *v, int R, float T_thr, unsigned long long geom,
+                      unsigned long long *key) {
+    key[0] = (unsigned long long)(uintptr_t)O;
+    key[1] = (unsigned long long)(uintptr_t)v;
+    key[2] = (unsigned long long)R;
+    key[3] = (unsigned long long)sc->n;
+    key[4] = (unsigned long long)(uintptr_t)sc->m;
+    key[5] = (unsigned long long)(uintptr_t)sc->s;
+    key[6] = (unsigned long long)(uintptr_t)sc->q;
+    key[7] = (unsigned long long)(uintptr_t)sc->RGBA;
+    key[8] = (unsigned long long)(uintptr_t)sc->k;
+    key[9] = (unsigned long long)(uintptr_t)sc->cond;
+    key[10] = (unsigned long long)(uintptr_t)sc->A1;
+    key[11] = geom;
+    unsigned tb = 0;
+    memcpy(&tb, &T_thr, 4);
+    key[12] = tb;
+    key[13] = key[14] = key[15] = 0;
+}
+
+// Grows the cache to the ray-passes the last uncached forward needed, within a device-memory budget
+// (FLARE_HIT_CACHE_MB, default half of the free memory).  Runs before any pass, never inside the loop.
+static void grow_cache(flare_renderer *r) {
+    if (r->hc_need <= r->hc_cap) return;
+    size_t want = r->hc_need + r->hc_need / 8 + 1024;
+    size_t bytes = want * (4 + 16 * 8);
+    size_t freeb = 0, total = 0;
+    cudaMemGetInfo(&freeb, &total);
+    size_t budget = freeb / 2;
+    if (const char *e = getenv("FLARE_HIT_CACHE_MB")) budget = (size_t)atoll(e) << 20;
+    r->hc_need = 0;
+    if (bytes > budget) return;
+    cudaFree(r->hc_list); cudaFree(r->hc_t); cudaFree(r->hc_idx);
+    r->hc_list = nullptr; r->hc_t = nullptr; r->hc_idx = nullptr; r->hc_cap = 0;
+    if (cudaMalloc(&r->hc_list, want * 4) != cudaSuccess || cudaMalloc(&r->hc_t, want * 16 * 4) != cudaSuccess ||
+        cudaMalloc(&r->hc_idx, want * 16 * 4) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(r->hc_list); cudaFree(r->hc_t); cudaFree(r->hc_idx);
+        r->hc_list = nullptr; r->hc_t = nullptr; r->hc_idx = nullptr;
+        return;
+    }
+    r->hc_cap = want;
+}
+
 // Runs the pass loop: trace -> shade -> compaction, until no ray is active.
 template <typename ShadeFn>
 static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, cudaStream_t st, int shade_kind,
-                     ShadeFn shade) {
+                     ShadeFn shade, bool cache = false) {
     int count = R;
     int cur = 0;
     long long passes = 0;
+    size_t off = 0;
+    bool cached = cache;
     const long long max_passes = (long long)(r->n / K_HITS) + 4;
     while (count > 0) {
         if (passes > max_passes) {
             set_error("pass loop did not terminate after %lld passes", passes);
             return FLARE_E_DEVICE;
         }
+        float *ht = r->hit_t;
+        int *hi = r->hit_idx;
+        if (cached && (off + count > r->hc_cap || passes >= flare_renderer::HC_MAX_PASSES)) cached = false;
+        if (cached) {  // hits go straight into the cache; the active list is copied beside them
+            ht = r->hc_t + 16 * off;
+            hi = r->hc_idx + 16 * off;
+            FLARE_CUDA_TRY(cudaMemcpyAsync(r->hc_list + off, r->list[cur], (size_t)count * sizeof(int),
+                                           cudaMemcpyDeviceToDevice, st));
+            r->hc_off[passes] = off;
+            r->hc_cnt[passes] = count;
+        }
+        off += count;
         int slot = prof_begin(r, PK_TRACE, st);
-        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, r->hit_t, r->hit_idx, count, st);
+        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st);
         prof_end(r, slot, st);
         if (e) return e;
         FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
         slot = prof_begin(r, shade_kind, st);
-        e = shade(r->list[cur], count, r->list[cur ^ 1]);
+        e = shade(r->list[cur], count, r->list[cur ^ 1], ht, hi);
         prof_end(r, slot, st);
         if (e) return e;
         FLARE_CUDA_TRY(cudaMemcpyAsync(r->h_count, r->counters, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -1237,6 +1363,11 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
         count = *r->h_count;
         cur ^= 1;
         ++passes;
+    }
+    if (cache) {
+        r->hc_valid = cached;
+        r->hc_npass = cached ? (int)passes : 0;
+        if (!cached) r->hc_need = off;  // the next forward grows the cache before its first pass
     }
     unsigned long long p = (unsigned long long)passes;
     FLARE_CUDA_TRY(cudaMemcpyAsync(r->dstats + ST_PASSES, &p, sizeof(p), cudaMemcpyHostToDevice, st));
@@ -1276,13 +1407,27 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
         if (e) return e;
     }
     PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
-    return pass_loop(r, a->O, a->v, R, st, PK_SHADE_FWD, [&](const int *lin, int count, int *lout) -> int {
-        PassP pp = base;
-        pp.list_in = lin;
-        pp.count = count;
-        pp.list_out = lout;
-        return dec ? launch_fwd_mode<true>(r, a->mode, sp, pp, fo, st) : launch_fwd_mode<false>(r, a->mode, sp, pp, fo, st);
-    });
+    const bool cache = a->mode == FLARE_FWD_TRAINING;
+    r->hc_valid = false;
+    if (cache) {
+        grow_cache(r);
+        cache_key(sc, a->O, a->v, R, a->T_threshold, r->geom_version, r->hc_key);
+        int e = input_checksum(r, sc, a->O, a->v, R, r->hc_sum, st);
+        if (e) return e;
+    }
+    return pass_loop(
+        r, a->O, a->v, R, st, PK_SHADE_FWD,
+        [&](const int *lin, int count, int *lout, const float *ht, const int *hi) -> int {
+            PassP pp = base;
+            pp.list_in = lin;
+            pp.count = count;
+            pp.list_out = lout;
+            pp.hit_t = ht;
+            pp.hit_idx = hi;
+            return dec ? launch_fwd_mode<true>(r, a->mode, sp, pp, fo, st)
+                       : launch_fwd_mode<false>(r, a->mode, sp, pp, fo, st);
+        },
+        cache);
 }
 
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st) {
@@ -1318,11 +1463,13 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
                                             SM_BWD_BYTES));
     }
     PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
-    int e = pass_loop(r, a->O, a->v, R, st, PK_SHADE_BWD, [&](const int *lin, int count, int *lout) -> int {
+    auto shade = [&](const int *lin, int count, int *lout, const float *ht, const int *hi) -> int {
         PassP pp = base;
         pp.list_in = lin;
         pp.count = count;
         pp.list_out = lout;
+        pp.hit_t = ht;
+        pp.hit_idx = hi;
         int chunks = (count + 127) / 128;
         if (dec) {
             int grid = std::min(chunks, r->num_sms * 2);
@@ -1332,7 +1479,36 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         }
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
-    });
+    };
+    bool replay = false;
+    if (r->hc_valid) {
+        unsigned long long key[16];
+        cache_key(sc, a->O, a->v, R, a->T_threshold, r->geom_version, key);
+        if (memcmp(key, r->hc_key, sizeof(key)) == 0) {
+            int e = input_checksum(r, sc, a->O, a->v, R, r->hc_sum + 1, st);
+            if (e) return e;
+            unsigned long long h[2];
+            FLARE_CUDA_TRY(cudaMemcpyAsync(h, r->hc_sum, sizeof(h), cudaMemcpyDeviceToHost, st));
+            FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+            replay = h[0] == h[1];
+        }
+    }
+    int e = FLARE_OK;
+    if (replay) {  // the forward's passes, back to back, without tracing or host round trips
+        for (int p = 0; p < r->hc_npass && !e; ++p) {
+            FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
+            int slot = prof_begin(r, PK_SHADE_BWD, st);
+            const size_t off = r->hc_off[p];
+            e = shade(r->hc_list + off, r->hc_cnt[p], r->list[1], r->hc_t + 16 * off, r->hc_idx + 16 * off);
+            prof_end(r, slot, st);
+        }
+        unsigned long long np = (unsigned long long)r->hc_npass;
+        FLARE_CUDA_TRY(cudaMemcpyAsync(r->dstats + ST_PASSES, &np, sizeof(np), cudaMemcpyHostToDevice, st));
+        FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+        prof_collect(r);
+    } else {
+        e = pass_loop(r, a->O, a->v, R, st, PK_SHADE_BWD, shade);
+    }
     if (e) return e;
     if (dec) {
         pack_dw_kernel<<<32, 256, 0, st>>>(r->dw, a->dL_dw1, a->dL_db1, a->dL_dw2, a->dL_db2, a->dL_dw3, a->dL_db3);

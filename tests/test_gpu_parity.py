@@ -335,3 +335,27 @@ def test_backward_matches_autograd(case_dense, base, reg):
         if not e < GRAD_TOL:
             bad[k] = e
     assert not bad, f"relative L2 above {GRAD_TOL}: {bad}"
+
+
+def test_backward_replay_equals_retrace(case_dense):
+    """A Backward that follows its Forward_training replays the cached passes; one whose geometry was
+    rebuilt in between re-traverses.  Both must give the same gradients."""
+    c = case_dense
+    R, n = c.R, c.sc.n
+    outs = []
+    for rebuild in (False, True):
+        for _ in range(2):  # the first forward on a renderer sizes the cache, the second fills it
+            bitmap, dacc, nacc, dai, sn = z(R, 3), z(R, 4), z(R, 4), z(R, 2), z(R, 3)
+            c.r.Forward_training(*c.dec(), c.Og, c.vg, bitmap, 0.1, 0.2, 0.3, *c.geo(), 1e-4, dacc, REG_A, REG_B, dai,
+                                 sn, nacc)
+        if rebuild:
+            c.r.SetGeometry(*[t.contiguous() for t in c.g.activated()])
+        dLdI = torch.randn(R, 3, generator=torch.Generator().manual_seed(4)).cuda() / R
+        G = dict(RGB=z(n, 3), A=z(n, 1), k=z(n, 1), m=z(n, 3), s=z(n, 2), q=z(n, 4), cond=z(n, 96), f=z(13154))
+        W = [z(1, 512), z(1, 64), z(1, 4096), z(1, 512), z(1, 8192), z(1, 512)]
+        c.r.Backward(*c.dec(), c.Og, c.vg, 0.1, 0.2, 0.3, *c.geo(), bitmap.clone(), dLdI, G["RGB"], G["A"], G["k"], *W,
+                     G["cond"], G["f"], G["m"], G["s"], G["q"], 1e-4, dacc, z(R, 4), 0.0, REG_A, REG_B, dai, sn, nacc,
+                     0.0)
+        outs.append({**G, "w1": W[4]})
+    for k in outs[0]:
+        assert grad_oracle.rel_l2(outs[0][k].cpu().numpy(), outs[1][k].cpu().numpy()) < 1e-5, k
