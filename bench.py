@@ -198,14 +198,24 @@ class CpuPort:
 
         from oracle import grad_oracle, oracle
         t1 = time.perf_counter()
-        csr = oracle.hit_lists(self.frames, self.O, self.v)
+
+        def stop(ids, per_t, per_i):
+            # composite what each ray has so far; a ray whose transmittance fell below the threshold is done
+            off = np.zeros(len(ids) + 1, np.int64)
+            off[1:] = np.cumsum([len(per_i[r]) for r in ids])
+            part = (off, np.array([x for r in ids for x in per_t[r]], np.float32),
+                    np.array([x for r in ids for x in per_i[r]], np.int32))
+            f = oracle.forward(self.sc, self.O[ids], self.v[ids], part, "training")
+            return f["T"] < 1e-4
+
+        csr = oracle.hit_lists(self.frames, self.O, self.v, stop=stop)
         ref = oracle.forward(self.sc, self.O, self.v, csr, "training", reg_a=-0.1 * 1000 / 999.9,
                              reg_b=1000 / 999.9)
         img = np.clip(ref["rgb"], 0, 1)
         dLdI = (np.sign(img - self.target) / (3 * len(self.O))).astype(np.float32)
         t2 = time.perf_counter()
         if self.train:
-            grad_oracle.gradients(self.sc, self.O, self.v, csr, ref["nhits"], dLdI)
+            grad_oracle.gradients(self.sc, self.O, self.v, csr, ref["nhits"], dLdI, compact=True)
         t3 = time.perf_counter()
         self.last = (t2 - t1, t3 - t2, int(ref["total_hits"]))
         return t3 - t1
@@ -214,7 +224,8 @@ class CpuPort:
         fwd, bwd, hits = self.last
         c = CONFIGS[self.cfg]
         return (f"{len(self.O)} central rays of config {self.cfg} view 0 per step ({hits} composited hits); "
-                f"brute-force k-nearest traversal over all {c['n_prims']} primitives + decode/composite (C, OpenMP) "
+                f"brute-force k-nearest traversal over all {c['n_prims']} primitives, passes until termination, "
+                f"+ decode/composite (C, OpenMP) "
                 f"+ autograd backward (torch fp64); frame prep {self.prep_s:.2f}s once, per step fwd {fwd:.2f}s "
                 f"bwd {bwd:.2f}s")
 
@@ -319,7 +330,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="flare", choices=["flare", "reference"])
     ap.add_argument("--config", type=int, default=3, choices=[2, 3])
-    ap.add_argument("--ref-rays", type=int, default=8)
+    ap.add_argument("--ref-rays", type=int, default=32)
     ap.add_argument("--no-extra", action="store_true", help="skip the config-1/2 extras and the CPU baseline")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)

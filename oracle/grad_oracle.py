@@ -71,13 +71,28 @@ def _pe(v):
 
 
 def gradients(scene, O, v, csr, nhits, dL_dI, base=False, bg=(0.0, 0.0, 0.0), reg_a=0.0, reg_b=0.0,
-              lambda_depth=0.0, lambda_normal=0.0, surface_normal=None, exact_t=False):
+              lambda_depth=0.0, lambda_normal=0.0, surface_normal=None, exact_t=False, compact=False):
     """Returns a dict of float64 gradients (dense layouts) and the composited image C.
-    exact_t=True evaluates at the float64 ray-plane t instead of the fp32 traversal t (self-checks)."""
+    exact_t=True evaluates at the float64 ray-plane t instead of the fp32 traversal t (self-checks).
+    compact=True returns per-primitive gradients only for the primitives that were hit (in sorted index
+    order) instead of scattering them into full-size tensors."""
     g = scene if isinstance(scene, dict) else scene.__dict__
     dt = torch.float64
-    P = {k: torch.as_tensor(np.asarray(x.detach().cpu().float() if hasattr(x, "detach") else x), dtype=dt)
-         for k, x in g.items()}
+    off0, _, ii0 = csr
+    nh0 = np.asarray(nhits, np.int64)
+    ray0 = np.repeat(np.arange(len(nh0)), nh0)
+    pos0 = np.concatenate([np.arange(k) for k in nh0]) if len(nh0) else np.zeros(0, np.int64)
+    used = np.unique(np.asarray(ii0, np.int64)[np.asarray(off0[:-1], np.int64)[ray0] + pos0])
+    n_all = None
+    P = {}
+    for k, x in g.items():
+        a = x.detach().cpu() if hasattr(x, "detach") else torch.as_tensor(np.asarray(x))
+        if k in ("m", "s", "q", "RGBA", "k", "cond"):  # per-primitive: only the rows that are hit
+            n_all = a.shape[0]
+            a = a[torch.as_tensor(used)]
+        P[k] = a.float().to(dt)
+    remap = np.full(max(n_all or 0, 1), -1, np.int64)
+    remap[used] = np.arange(len(used))
     names = ["m", "s", "q", "RGBA", "k"] + ([] if base else ["cond", "features", "A1", "b1", "A2", "b2", "A3", "b3"])
     for k in names:
         P[k].requires_grad_(True)
@@ -90,7 +105,7 @@ def gradients(scene, O, v, csr, nhits, dL_dI, base=False, bg=(0.0, 0.0, 0.0), re
     ray = np.repeat(np.arange(R), nhits)
     pos = np.concatenate([np.arange(n) for n in nhits]) if len(nhits) else np.zeros(0, np.int64)
     flat = np.asarray(off[:-1], np.int64)[ray] + pos
-    hidx = np.asarray(ii, np.int64)[flat]
+    hidx = remap[np.asarray(ii, np.int64)[flat]]
     t_trav = torch.as_tensor(np.asarray(tt_csr, np.float32)[flat], dtype=dt)
     ray_t, idx_t = torch.as_tensor(ray), torch.as_tensor(hidx)
     Oh, vh = O[ray_t], v[ray_t]
@@ -148,7 +163,14 @@ def gradients(scene, O, v, csr, nhits, dL_dI, base=False, bg=(0.0, 0.0, 0.0), re
         Ln = (valid * wd * (1.0 - sgn * (sn[ray_t] * N).sum(1))).sum()
         loss = loss + lambda_normal * Ln
     loss.backward()
-    out = {k: P[k].grad.detach().clone() if P[k].grad is not None else torch.zeros_like(P[k]) for k in names}
+    out = {}
+    for k in names:
+        gk = P[k].grad.detach() if P[k].grad is not None else torch.zeros_like(P[k])
+        if k in ("m", "s", "q", "RGBA", "k", "cond") and not compact:
+            full = torch.zeros((n_all,) + tuple(gk.shape[1:]), dtype=dt)
+            full[torch.as_tensor(used)] = gk
+            gk = full
+        out[k] = gk.clone()
     out["C"] = C.detach()
     out["RGB"] = out["RGBA"][:, :3]
     out["A"] = out["RGBA"][:, 3:4]

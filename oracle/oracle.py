@@ -90,10 +90,12 @@ def next_tmin(t16):
     return np.nextafter(np.float32(t16), np.float32(np.inf), dtype=np.float32)
 
 
-def hit_lists(frames, O, v, nsides=8, max_passes=100000):
+def hit_lists(frames, O, v, nsides=8, max_passes=100000, stop=None):
     """Runs the multi-pass restart loop to exhaustion: every hit of every ray in ascending (t, idx)
     order, with the reference's restart t_min = nextafter(t_16) (ties at t_16 with a larger index are
-    dropped, as the reference's k-buffer drops them).  Returns CSR (off (R+1) int64, t, idx)."""
+    dropped, as the reference's k-buffer drops them).  Returns CSR (off (R+1) int64, t, idx).
+    `stop`, if given, ends rays early (the renderer stops a ray once its transmittance falls below the
+    threshold)."""
     O, v = _f32(_np(O)), _f32(_np(v))
     R = O.shape[0]
     t_min = np.zeros(R, np.float32)
@@ -108,6 +110,8 @@ def hit_lists(frames, O, v, nsides=8, max_passes=100000):
             per_ray_t[r].extend(t[valid, j].tolist())
             per_ray_i[r].extend(idx[valid, j].tolist())
         full = idx[K - 1] >= 0
+        if stop is not None:  # stop(ray ids, CSR so far) -> rays whose compositing has terminated
+            full &= ~stop(active, per_ray_t, per_ray_i)
         t_min[active[full]] = np.nextafter(t[K - 1, full], np.float32(np.inf), dtype=np.float32)
         active = active[full]
         passes += 1

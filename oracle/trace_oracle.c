@@ -92,10 +92,58 @@ static inline int hit_test(const float *f, const float *O, const float *v, float
 
 /* Brute-force k-nearest: for each ray r, the K_HITS smallest (t, idx) with t >= t_min[r].
    t_out / idx_out are slot-major (K_HITS, R).  Optionally returns the count of hits found. */
+static void kbuf_push(float *tb, int *ib, float t, int i) {
+    if (!(t < tb[K_HITS - 1] || (t == tb[K_HITS - 1] && i < ib[K_HITS - 1]))) return;
+    float ct = t;
+    int ci = i;
+    for (int k = 0; k < K_HITS; ++k) {
+        int sw = (ct < tb[k]) || (ct == tb[k] && ci < ib[k]);
+        if (sw) {
+            float tt = tb[k]; int ii = ib[k];
+            tb[k] = ct; ib[k] = ci;
+            ct = tt; ci = ii;
+        }
+    }
+}
+
+/* Few rays: the primitives are split over the threads, each keeps its own buffer, the buffers merge. */
+static void oracle_hits_few(const float *frames, int n, const float *O, const float *v, const float *t_min, int R,
+                            int nsides, const float *pc, const float *ps, float *t_out, int *idx_out) {
+    for (int r = 0; r < R; ++r) {
+        float tb[K_HITS];
+        int ib[K_HITS];
+        for (int k = 0; k < K_HITS; ++k) { tb[k] = INFINITY; ib[k] = 0x7fffffff; }
+        const float *o = O + 3 * r, *d = v + 3 * r;
+#pragma omp parallel
+        {
+            float lt[K_HITS];
+            int li[K_HITS];
+            for (int k = 0; k < K_HITS; ++k) { lt[k] = INFINITY; li[k] = 0x7fffffff; }
+#pragma omp for schedule(static)
+            for (int i = 0; i < n; ++i) {
+                float t;
+                if (hit_test(frames + 12 * (long)i, o, d, t_min[r], nsides, pc, ps, &t)) kbuf_push(lt, li, t, i);
+            }
+#pragma omp critical
+            for (int k = 0; k < K_HITS; ++k)
+                if (li[k] != 0x7fffffff) kbuf_push(tb, ib, lt[k], li[k]);
+        }
+        for (int k = 0; k < K_HITS; ++k) {
+            int valid = ib[k] != 0x7fffffff;
+            t_out[(long)k * R + r] = valid ? tb[k] : INFINITY;
+            idx_out[(long)k * R + r] = valid ? ib[k] : -1;
+        }
+    }
+}
+
 void oracle_hits(const float *frames, int n, const float *O, const float *v, const float *t_min, int R,
                  int nsides, float *t_out, int *idx_out) {
     float pc[64], ps[64];
     oracle_polygon_constants(nsides, pc, ps);
+    if (R < 64 && n > 4096) {
+        oracle_hits_few(frames, n, O, v, t_min, R, nsides, pc, ps, t_out, idx_out);
+        return;
+    }
 #pragma omp parallel for schedule(dynamic, 16)
     for (int r = 0; r < R; ++r) {
         float tb[K_HITS];
@@ -104,7 +152,7 @@ void oracle_hits(const float *frames, int n, const float *O, const float *v, con
         const float *o = O + 3 * r, *d = v + 3 * r;
         for (int i = 0; i < n; ++i) {
             float t;
-            if (!hit_test(frames + 12 * i, o, d, t_min[r], nsides, pc, ps, &t)) continue;
+            if (!hit_test(frames + 12 * (long)i, o, d, t_min[r], nsides, pc, ps, &t)) continue;
             if (!(t < tb[K_HITS - 1] || (t == tb[K_HITS - 1] && i < ib[K_HITS - 1]))) continue;
             float ct = t;
             int ci = i;
