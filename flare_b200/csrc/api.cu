@@ -150,8 +150,8 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
     ALLOC(r->T, R * sizeof(float));
     ALLOC(r->list[0], R * sizeof(int));
     ALLOC(r->list[1], R * sizeof(int));
-    ALLOC(r->hit_t, R * K_HITS * sizeof(float));
-    ALLOC(r->hit_idx, R * K_HITS * sizeof(int));
+    ALLOC(r->hit_t, R * K_PASS * sizeof(float));
+    ALLOC(r->hit_idx, R * K_PASS * sizeof(int));
     ALLOC(r->counters, 64 * sizeof(int));
     ALLOC(r->dw, 16384 * sizeof(float));
     ALLOC(r->gscale, 64);

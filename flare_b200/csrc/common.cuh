@@ -8,7 +8,13 @@
 
 namespace flare {
 
-constexpr int K_HITS = FLARE_HIT_BUFFER_SIZE;  // 16
+constexpr int K_HITS = FLARE_HIT_BUFFER_SIZE;  // 16: hits per Render call (the reference's k-buffer)
+#ifndef FLARE_K_PASS
+#define FLARE_K_PASS 48
+#endif
+// Hits gathered per pass inside Forward / Backward.  The composited result does not depend on it (hits
+// are consumed in (t, index) order either way); it trades traversal restarts against buffer registers.
+constexpr int K_PASS = FLARE_K_PASS;
 constexpr int COND = FLARE_COND_DIM;           // 96
 constexpr int LUT = FLARE_LUT_SIZE;            // 13154 floats
 constexpr int MAX_SIDES = 64;

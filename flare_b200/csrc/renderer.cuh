@@ -104,7 +104,7 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
 // trace.cu: traces `count` rays.  Ray j is ray_ids[j] (or j when ray_ids is null); t_min is indexed by
 // ray id; outputs (16, out_stride) slot-major at column j.
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
-                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st);
+                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k = K_HITS);
 
 // trace.cu: writes the coherence order of R rays into list_out
 int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st);

@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
         }
         int ind = -1;
         float t_hit = 0.0f;
-        for (int h = 0; h < K_HITS; ++h) {
+        for (int h = 0; h < K_PASS; ++h) {
             ind = have ? pp.hit_idx[(size_t)h * pp.count + slot] : -1;
             t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
             bool valid = ind >= 0 && T >= pp.T_thr;
@@ -717,7 +717,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
         }
         int ind = -1;
         float t_hit = 0.0f;
-        for (int h = 0; h < K_HITS; ++h) {
+        for (int h = 0; h < K_PASS; ++h) {
             ind = have ? pp.hit_idx[(size_t)h * pp.count + slot] : -1;
             t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
             const bool valid = ind >= 0 && T >= pp.T_thr;
@@ -1302,7 +1302,7 @@ static void cache_key(const flare_scene *sc, const float *O, const float *v, int
 static void grow_cache(flare_renderer *r) {
     if (r->hc_need <= r->hc_cap) return;
     size_t want = r->hc_need + r->hc_need / 8 + 1024;
-    size_t bytes = want * (4 + 16 * 8);
+    size_t bytes = want * (4 + (size_t)K_PASS * 8);
     size_t freeb = 0, total = 0;
     cudaMemGetInfo(&freeb, &total);
     size_t budget = freeb / 2;
@@ -1311,8 +1311,8 @@ static void grow_cache(flare_renderer *r) {
     if (bytes > budget) return;
     cudaFree(r->hc_list); cudaFree(r->hc_t); cudaFree(r->hc_idx);
     r->hc_list = nullptr; r->hc_t = nullptr; r->hc_idx = nullptr; r->hc_cap = 0;
-    if (cudaMalloc(&r->hc_list, want * 4) != cudaSuccess || cudaMalloc(&r->hc_t, want * 16 * 4) != cudaSuccess ||
-        cudaMalloc(&r->hc_idx, want * 16 * 4) != cudaSuccess) {
+    if (cudaMalloc(&r->hc_list, want * 4) != cudaSuccess || cudaMalloc(&r->hc_t, want * K_PASS * 4) != cudaSuccess ||
+        cudaMalloc(&r->hc_idx, want * K_PASS * 4) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(r->hc_list); cudaFree(r->hc_t); cudaFree(r->hc_idx);
         r->hc_list = nullptr; r->hc_t = nullptr; r->hc_idx = nullptr;
@@ -1330,7 +1330,7 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
     long long passes = 0;
     size_t off = 0;
     bool cached = cache;
-    const long long max_passes = (long long)(r->n / K_HITS) + 4;
+    const long long max_passes = (long long)(r->n / K_PASS) + 4;
     while (count > 0) {
         if (passes > max_passes) {
             set_error("pass loop did not terminate after %lld passes", passes);
@@ -1340,8 +1340,8 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
         int *hi = r->hit_idx;
         if (cached && (off + count > r->hc_cap || passes >= flare_renderer::HC_MAX_PASSES)) cached = false;
         if (cached) {  // hits go straight into the cache; the active list is copied beside them
-            ht = r->hc_t + 16 * off;
-            hi = r->hc_idx + 16 * off;
+            ht = r->hc_t + (size_t)K_PASS * off;
+            hi = r->hc_idx + (size_t)K_PASS * off;
             FLARE_CUDA_TRY(cudaMemcpyAsync(r->hc_list + off, r->list[cur], (size_t)count * sizeof(int),
                                            cudaMemcpyDeviceToDevice, st));
             r->hc_off[passes] = off;
@@ -1349,7 +1349,7 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
         }
         off += count;
         int slot = prof_begin(r, PK_TRACE, st);
-        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st);
+        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st, K_PASS);
         prof_end(r, slot, st);
         if (e) return e;
         FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
@@ -1499,7 +1499,7 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
             FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
             int slot = prof_begin(r, PK_SHADE_BWD, st);
             const size_t off = r->hc_off[p];
-            e = shade(r->hc_list + off, r->hc_cnt[p], r->list[1], r->hc_t + 16 * off, r->hc_idx + 16 * off);
+            e = shade(r->hc_list + off, r->hc_cnt[p], r->list[1], r->hc_t + (size_t)K_PASS * off, r->hc_idx + (size_t)K_PASS * off);
             prof_end(r, slot, st);
         }
         unsigned long long np = (unsigned long long)r->hc_npass;

@@ -14,18 +14,24 @@
 
 #include "renderer.cuh"
 
+#ifndef FLARE_TRACE_MIN_BLOCKS
+#define FLARE_TRACE_MIN_BLOCKS 3  // resident 128-thread blocks per SM the register budget aims for
+#endif
+
 namespace flare {
 
+template <int K>
 struct KBuf {
-    float t[K_HITS];
-    int i[K_HITS];
+    float t[K];
+    int i[K];
 };
 
-__device__ __forceinline__ void kbuf_insert(KBuf &b, float t, int id) {
+template <int K>
+__device__ __forceinline__ void kbuf_insert(KBuf<K> &b, float t, int id) {
     float ct = t;
     int ci = id;
 #pragma unroll
-    for (int k = 0; k < K_HITS; ++k) {
+    for (int k = 0; k < K; ++k) {
         bool sw = (ct < b.t[k]) || (ct == b.t[k] && ci < b.i[k]);
         float tt = b.t[k];
         int ii = b.i[k];
@@ -73,129 +79,14 @@ __device__ __forceinline__ bool slab(float lx, float ly, float lz, float hx, flo
     return tn <= tf;
 }
 
-template <bool STATS>
-__global__ void __launch_bounds__(128) trace_kernel(const float *__restrict__ O_, const float *__restrict__ v_,
-                                                    const float *__restrict__ tmin_, const int *__restrict__ ray_ids,
-                                                    int count, const Node *__restrict__ nodes,
-                                                    const float4 *__restrict__ rec, const int *__restrict__ ids,
-                                                    int n, float *__restrict__ t_out, int *__restrict__ idx_out,
-                                                    int stride, const PolyConst poly, int *__restrict__ status,
-                                                    unsigned long long *__restrict__ stats) {
-    int j = blockIdx.x * blockDim.x + threadIdx.x;
-    unsigned long long nprim = 0, nnode = 0;
-    if (j < count) {
-        int ray = ray_ids ? ray_ids[j] : j;
-        float3 O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
-        float3 v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
-        float t_min = tmin_[ray];
-        KBuf kb;
-#pragma unroll
-        for (int k = 0; k < K_HITS; ++k) {
-            kb.t[k] = INFINITY;
-            kb.i[k] = 0x7fffffff;
-        }
-        float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
-                                1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
-                                1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
-        const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);  // culling slack; the exact test decides hits
-        if (n == 1) {
-            float t;
-            ++nprim;
-            if (hit_prim(rec, 0, O, v, t_min, poly, t)) kbuf_insert(kb, t, ids[0]);
-        } else if (n > 1) {
-            int stk[TRACE_STACK];
-            float stt[TRACE_STACK];
-            int sp = 0;
-            int node = 0;
-            const unsigned long long max_visits = 2ull * (unsigned long long)n + 64ull;
-            while (true) {
-                if (++nnode > max_visits) {  // malformed hierarchy: report instead of spinning
-                    atomicOr(status, ERR_INDEX);
-                    break;
-                }
-                const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
-                float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
-                int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
-                float thi = __fmaf_rn(fabsf(kb.t[K_HITS - 1]), 1e-5f, kb.t[K_HITS - 1]);
-                float t0, t1;
-                bool h0 = slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
-                bool h1 = slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
-                if (h0 && d.x < 0) {
-                    float t;
-                    ++nprim;
-                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t)) {
-                        int pid = __ldg(ids + ~d.x);
-                        if (t < kb.t[K_HITS - 1] || (t == kb.t[K_HITS - 1] && pid < kb.i[K_HITS - 1]))
-                            kbuf_insert(kb, t, pid);
-                    }
-                    h0 = false;
-                }
-                if (h1 && d.y < 0) {
-                    float t;
-                    ++nprim;
-                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t)) {
-                        int pid = __ldg(ids + ~d.y);
-                        if (t < kb.t[K_HITS - 1] || (t == kb.t[K_HITS - 1] && pid < kb.i[K_HITS - 1]))
-                            kbuf_insert(kb, t, pid);
-                    }
-                    h1 = false;
-                }
-                if (h0 && h1) {
-                    bool first0 = t0 <= t1;
-                    int far = first0 ? d.y : d.x;
-                    float tfar = first0 ? t1 : t0;
-                    node = first0 ? d.x : d.y;
-                    if (sp < TRACE_STACK) {
-                        stk[sp] = far;
-                        stt[sp] = tfar;
-                        ++sp;
-                    } else {
-                        atomicOr(status, ERR_STACK);
-                    }
-                    continue;
-                }
-                if (h0) { node = d.x; continue; }
-                if (h1) { node = d.y; continue; }
-                // pop, skipping subtrees whose entry is now beyond the 16th hit
-                bool found = false;
-                while (sp > 0) {
-                    --sp;
-                    if (stt[sp] <= __fmaf_rn(fabsf(kb.t[K_HITS - 1]), 1e-5f, kb.t[K_HITS - 1])) {
-                        node = stk[sp];
-                        found = true;
-                        break;
-                    }
-                }
-                if (!found) break;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < K_HITS; ++k) {
-            bool valid = kb.i[k] != 0x7fffffff;
-            t_out[(size_t)k * stride + j] = valid ? kb.t[k] : INFINITY;
-            idx_out[(size_t)k * stride + j] = valid ? kb.i[k] : -1;
-        }
-    }
-    if (STATS) {
-        for (int o = 16; o > 0; o >>= 1) {
-            nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
-            nnode += __shfl_xor_sync(0xffffffffu, nnode, o);
-        }
-        if ((threadIdx.x & 31) == 0 && (nprim | nnode)) {
-            atomicAdd(stats + ST_PRIM_TESTS, nprim);
-            atomicAdd(stats + ST_NODES, nnode);
-        }
-    }
-}
-
-// Warp-packet variant: the 32 rays of a warp share one traversal stack (in shared memory) and every node
+// Traversal kernel: the 32 rays of a warp share one traversal stack (in shared memory) and every node
 // fetch; each lane keeps its own k-buffer and interval [t_min, t_16], and a child is entered when any
 // lane's interval overlaps its box (lane masks ride on the stack).  Control flow is warp-uniform, so
 // the per-ray divergence of the one-thread-per-ray walk disappears; coherent rays (sorted by origin and
 // direction before the first pass) share most of their node visits.  The hit set is the same exact
 // k-nearest set as any other traversal order.
-template <bool STATS>
-__global__ void __launch_bounds__(128, 6) trace_packet_kernel(
+template <bool STATS, int K>
+__global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kernel(
     const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
@@ -214,9 +105,9 @@ __global__ void __launch_bounds__(128, 6) trace_packet_kernel(
         v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
         t_min = tmin_[ray];
     }
-    KBuf kb;
+    KBuf<K> kb;
 #pragma unroll
-    for (int k = 0; k < K_HITS; ++k) {
+    for (int k = 0; k < K; ++k) {
         kb.t[k] = INFINITY;
         kb.i[k] = 0x7fffffff;
     }
@@ -244,7 +135,7 @@ __global__ void __launch_bounds__(128, 6) trace_packet_kernel(
             const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
             const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
             const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
-            const float thi = __fmaf_rn(fabsf(kb.t[K_HITS - 1]), 1e-5f, kb.t[K_HITS - 1]);
+            const float thi = __fmaf_rn(fabsf(kb.t[K - 1]), 1e-5f, kb.t[K - 1]);
             float t0 = 0.0f, t1 = 0.0f;
             bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
             bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
@@ -252,9 +143,9 @@ __global__ void __launch_bounds__(128, 6) trace_packet_kernel(
                 if (h0) {
                     float t;
                     ++nprim;
-                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, kb.t[K_HITS - 1])) {
+                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, kb.t[K - 1])) {
                         const int pid = __ldg(ids + ~d.x);
-                        if (t < kb.t[K_HITS - 1] || (t == kb.t[K_HITS - 1] && pid < kb.i[K_HITS - 1]))
+                        if (t < kb.t[K - 1] || (t == kb.t[K - 1] && pid < kb.i[K - 1]))
                             kbuf_insert(kb, t, pid);
                     }
                 }
@@ -264,9 +155,9 @@ __global__ void __launch_bounds__(128, 6) trace_packet_kernel(
                 if (h1) {
                     float t;
                     ++nprim;
-                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, kb.t[K_HITS - 1])) {
+                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, kb.t[K - 1])) {
                         const int pid = __ldg(ids + ~d.y);
-                        if (t < kb.t[K_HITS - 1] || (t == kb.t[K_HITS - 1] && pid < kb.i[K_HITS - 1]))
+                        if (t < kb.t[K - 1] || (t == kb.t[K - 1] && pid < kb.i[K - 1]))
                             kbuf_insert(kb, t, pid);
                     }
                 }
@@ -302,7 +193,7 @@ __global__ void __launch_bounds__(128, 6) trace_packet_kernel(
     }
     if (live) {
 #pragma unroll
-        for (int k = 0; k < K_HITS; ++k) {
+        for (int k = 0; k < K; ++k) {
             const bool valid = kb.i[k] != 0x7fffffff;
             t_out[(size_t)k * stride + j] = valid ? kb.t[k] : INFINITY;
             idx_out[(size_t)k * stride + j] = valid ? kb.i[k] : -1;
@@ -416,10 +307,18 @@ size_t ray_sort_temp_bytes(int max_rays) {
 }
 
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
-                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st) {
+                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k) {
     if (count <= 0) return FLARE_OK;
     const int B = 128;
-    trace_packet_kernel<true><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes, r->rec,
+    if (k == K_PASS && K_PASS != K_HITS) {
+        trace_packet_kernel<true, K_PASS><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes,
+                                                                             r->rec, r->ids_sorted, r->n, t_out,
+                                                                             idx_out, out_stride, r->poly, r->dstatus,
+                                                                             r->dstats);
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    }
+    trace_packet_kernel<true, K_HITS><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes, r->rec,
                                                            r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
                                                            r->dstatus, r->dstats);
     FLARE_CUDA_TRY(cudaGetLastError());
@@ -432,7 +331,7 @@ int launch_trace_geom(const Node *nodes, const float4 *rec, const int *ids_sorte
                       int *status, cudaStream_t st) {
     if (count <= 0) return FLARE_OK;
     const int B = 128;
-    trace_packet_kernel<false><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, nullptr, count, nodes, rec, ids_sorted,
+    trace_packet_kernel<false, K_HITS><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, nullptr, count, nodes, rec, ids_sorted,
                                                                    n, t_out, idx_out, count, poly, status, nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
