@@ -15,7 +15,7 @@
 #include "renderer.cuh"
 
 #ifndef FLARE_TRACE_MIN_BLOCKS
-#define FLARE_TRACE_MIN_BLOCKS 3  // resident 128-thread blocks per SM the register budget aims for
+#define FLARE_TRACE_MIN_BLOCKS 4  // resident 128-thread blocks per SM the register budget aims for
 #endif
 
 namespace flare {
