@@ -164,6 +164,11 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
         r->ray_sort_tmp_bytes = ray_sort_temp_bytes((int)R);
         e = cudaMalloc(&r->ray_sort_tmp, r->ray_sort_tmp_bytes);
     }
+    ALLOC(r->pass_flags, R);
+    if (e == cudaSuccess) {
+        r->select_tmp_bytes = select_temp_bytes((int)R);
+        e = cudaMalloc(&r->select_tmp, r->select_tmp_bytes);
+    }
     ALLOC(r->dstatus, 64);
     ALLOC(r->dstats, ST_NSTATS * sizeof(unsigned long long));
 #undef ALLOC
@@ -186,7 +191,7 @@ int flare_destroy(flare_renderer *r) {
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
-                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (r->h_count) cudaFreeHost(r->h_count);

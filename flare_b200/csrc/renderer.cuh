@@ -37,6 +37,9 @@ struct flare_renderer {
     int *ray_ids_tmp = nullptr;              // (max_rays)
     void *ray_sort_tmp = nullptr;
     size_t ray_sort_tmp_bytes = 0;
+    unsigned char *pass_flags = nullptr;     // (max_rays) per list slot: still active after the pass
+    void *select_tmp = nullptr;              // stable compaction of the active list
+    size_t select_tmp_bytes = 0;
     int *h_count = nullptr;   // pinned host mirror of counters[0]
 
     // ---- decoder scratch ----
@@ -109,6 +112,8 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
 // trace.cu: writes the coherence order of R rays into list_out
 int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st);
 size_t ray_sort_temp_bytes(int max_rays);
+int compact_active(flare_renderer *r, const int *list_in, int count, int *list_out, cudaStream_t st);
+size_t select_temp_bytes(int max_rays);
 
 // shade.cu
 int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st);

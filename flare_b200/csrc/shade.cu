@@ -25,6 +25,7 @@
 // (from max |dL/dI|) so small image gradients do not underflow.
 #include <cuda_fp16.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 
@@ -86,8 +87,7 @@ struct PassP {
     const float *hit_t;
     const int *hit_idx;
     float *T, *t_min;
-    int *list_out;
-    int *count_out;
+    unsigned char *flags;  // per list slot: the ray stays active (compacted in list order after the pass)
     int *status;
     unsigned long long *stats;
     float bg0, bg1, bg2, T_thr;
@@ -424,17 +424,6 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
     return ok;
 }
 
-__device__ __forceinline__ void append_active(bool active, int ray, int *list_out, int *count_out) {
-    unsigned mask = __ballot_sync(0xffffffffu, active);
-    if (mask == 0) return;
-    int lane = threadIdx.x & 31;
-    int leader = __ffs(mask) - 1;
-    int base = 0;
-    if (lane == leader) base = atomicAdd(count_out, __popc(mask));
-    base = __shfl_sync(0xffffffffu, base, leader);
-    if (active) list_out[base + __popc(mask & ((1u << lane) - 1))] = ray;
-}
-
 // ================================================================================================
 // Forward
 // ================================================================================================
@@ -595,7 +584,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                 pp.t_min[ray] = ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY;
                 pp.T[ray] = T;
             }
-            append_active(active, ray, pp.list_out, pp.count_out);
+            if (have) pp.flags[slot] = active;
         }
     }
 done:
@@ -1045,7 +1034,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 pp.t_min[ray] = ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY;
                 pp.T[ray] = T;
             }
-            append_active(active, ray, pp.list_out, pp.count_out);
+            if (have) pp.flags[slot] = active;
         }
     }
 done:
@@ -1352,13 +1341,22 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
         int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st, K_PASS);
         prof_end(r, slot, st);
         if (e) return e;
-        FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
         slot = prof_begin(r, shade_kind, st);
-        e = shade(r->list[cur], count, r->list[cur ^ 1], ht, hi);
+        e = shade(r->list[cur], count, ht, hi);
         prof_end(r, slot, st);
+        if (e) return e;
+        e = compact_active(r, r->list[cur], count, r->list[cur ^ 1], st);
         if (e) return e;
         FLARE_CUDA_TRY(cudaMemcpyAsync(r->h_count, r->counters, sizeof(int), cudaMemcpyDeviceToHost, st));
         FLARE_CUDA_TRY(cudaStreamSynchronize(st));
+#ifdef FLARE_PASS_TRACE
+        if (r->prof_on && r->prof_n >= 2) {
+            float tms = 0.0f, sms = 0.0f;
+            cudaEventElapsedTime(&tms, r->prof_ev[2 * (r->prof_n - 2)], r->prof_ev[2 * (r->prof_n - 2) + 1]);
+            cudaEventElapsedTime(&sms, r->prof_ev[2 * (r->prof_n - 1)], r->prof_ev[2 * (r->prof_n - 1) + 1]);
+            fprintf(stderr, "pass %lld rays %d trace %.3f ms shade %.3f ms\n", passes, count, tms, sms);
+        }
+#endif
         prof_collect(r);
         count = *r->h_count;
         cur ^= 1;
@@ -1381,7 +1379,7 @@ static PassP make_pass(flare_renderer *r, const float *O, const float *v, float 
     pp.O = O; pp.v = v;
     pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
     pp.T = r->T; pp.t_min = r->t_min;
-    pp.count_out = r->counters;
+    pp.flags = r->pass_flags;
     pp.status = r->dstatus;
     pp.stats = r->dstats;
     pp.bg0 = bg0; pp.bg1 = bg1; pp.bg2 = bg2;
@@ -1417,12 +1415,11 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
     }
     return pass_loop(
         r, a->O, a->v, R, st, PK_SHADE_FWD,
-        [&](const int *lin, int count, int *lout, const float *ht, const int *hi) -> int {
+        [&](const int *lin, int count, const float *ht, const int *hi) -> int {
             PassP pp = base;
             pp.list_in = lin;
             pp.count = count;
-            pp.list_out = lout;
-            pp.hit_t = ht;
+                pp.hit_t = ht;
             pp.hit_idx = hi;
             return dec ? launch_fwd_mode<true>(r, a->mode, sp, pp, fo, st)
                        : launch_fwd_mode<false>(r, a->mode, sp, pp, fo, st);
@@ -1463,11 +1460,10 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
                                             SM_BWD_BYTES));
     }
     PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
-    auto shade = [&](const int *lin, int count, int *lout, const float *ht, const int *hi) -> int {
+    auto shade = [&](const int *lin, int count, const float *ht, const int *hi) -> int {
         PassP pp = base;
         pp.list_in = lin;
         pp.count = count;
-        pp.list_out = lout;
         pp.hit_t = ht;
         pp.hit_idx = hi;
         int chunks = (count + 127) / 128;
@@ -1496,10 +1492,9 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     int e = FLARE_OK;
     if (replay) {  // the forward's passes, back to back, without tracing or host round trips
         for (int p = 0; p < r->hc_npass && !e; ++p) {
-            FLARE_CUDA_TRY(cudaMemsetAsync(r->counters, 0, sizeof(int), st));
             int slot = prof_begin(r, PK_SHADE_BWD, st);
             const size_t off = r->hc_off[p];
-            e = shade(r->hc_list + off, r->hc_cnt[p], r->list[1], r->hc_t + (size_t)K_PASS * off, r->hc_idx + (size_t)K_PASS * off);
+            e = shade(r->hc_list + off, r->hc_cnt[p], r->hc_t + (size_t)K_PASS * off, r->hc_idx + (size_t)K_PASS * off);
             prof_end(r, slot, st);
         }
         unsigned long long np = (unsigned long long)r->hc_npass;

@@ -11,6 +11,7 @@
 // The hit test is exact fp32 with explicit rounding intrinsics; oracle/trace_oracle.c executes the
 // identical sequence, which is what makes hit lists bit-comparable.
 #include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_select.cuh>
 
 #include "renderer.cuh"
 
@@ -28,18 +29,22 @@ struct KBuf {
 
 template <int K>
 __device__ __forceinline__ void kbuf_insert(KBuf<K> &b, float t, int id) {
-    float ct = t;
-    int ci = id;
+    // Sorted by (t, index).  Slot k takes the old slot k-1 when (t, id) precedes both old entries, the
+    // new entry when it precedes only old slot k, else keeps its own.  Every comparison reads the old
+    // buffer (slots are rewritten from the top down), so the K steps are independent instead of one
+    // serial compare-and-swap chain.
+    bool lt_k = t < b.t[K - 1] || (t == b.t[K - 1] && id < b.i[K - 1]);
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-        bool sw = (ct < b.t[k]) || (ct == b.t[k] && ci < b.i[k]);
-        float tt = b.t[k];
-        int ii = b.i[k];
-        b.t[k] = sw ? ct : tt;
-        b.i[k] = sw ? ci : ii;
-        ct = sw ? tt : ct;
-        ci = sw ? ii : ci;
+    for (int k = K - 1; k > 0; --k) {
+        const float tp = b.t[k - 1];
+        const int ip = b.i[k - 1];
+        const bool lt_p = t < tp || (t == tp && id < ip);
+        b.t[k] = lt_k ? (lt_p ? tp : t) : b.t[k];
+        b.i[k] = lt_k ? (lt_p ? ip : id) : b.i[k];
+        lt_k = lt_p;
     }
+    b.t[0] = lt_k ? t : b.t[0];
+    b.i[0] = lt_k ? id : b.i[0];
 }
 
 // Exact hit test on the record of sorted primitive p (same operation order as the oracle).
@@ -297,6 +302,24 @@ int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *li
                                                    r->ray_ids_tmp, list_out, R, 0, 64, st));
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
+}
+
+// Keeps the active rays of a pass in list order (a stable select on the shading kernel's per-slot
+// flags), so each 32-ray traversal packet of the next pass is a run of the first pass's coherence order;
+// the count goes to r->counters[0].
+int compact_active(flare_renderer *r, const int *list_in, int count, int *list_out, cudaStream_t st) {
+    size_t tmp = r->select_tmp_bytes;
+    FLARE_CUDA_TRY(cub::DeviceSelect::Flagged(r->select_tmp, tmp, list_in, r->pass_flags, list_out, r->counters, count,
+                                              st));
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+size_t select_temp_bytes(int max_rays) {
+    size_t tmp = 0;
+    cub::DeviceSelect::Flagged(nullptr, tmp, (const int *)nullptr, (const unsigned char *)nullptr, (int *)nullptr,
+                               (int *)nullptr, max_rays, (cudaStream_t)0);
+    return tmp;
 }
 
 size_t ray_sort_temp_bytes(int max_rays) {
