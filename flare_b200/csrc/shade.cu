@@ -130,6 +130,25 @@ struct Geo {
     float r2, pk, r2k, G;    // r^2, (r^2)^(kappa-1), (r^2)^kappa, exp(-r2k / (2 kappa))
 };
 
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Pulls the per-primitive rows the next hit slot reads into L2 while the current slot's tiles run.
+__device__ __forceinline__ void prefetch_hit(const SceneP &sc, int idx) {
+    if (idx < 0) return;
+    prefetch_l2(sc.m + 3 * (size_t)idx);
+    prefetch_l2(sc.s + 2 * (size_t)idx);
+    prefetch_l2(sc.q + 4 * (size_t)idx);
+    prefetch_l2(sc.k + idx);
+    prefetch_l2(sc.RGBA + 4 * (size_t)idx);
+    if (sc.cond) {  // the 192-byte descriptor row spans two 128-byte lines
+        const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)idx * 12);
+        prefetch_l2(c);
+        prefetch_l2(c + 128);
+    }
+}
+
 __device__ __forceinline__ void geometry(const SceneP &sc, int idx, float t, float3 O, float3 v, Geo &g) {
     float2 s = __ldg(reinterpret_cast<const float2 *>(sc.s) + idx);
     float4 q = __ldg(reinterpret_cast<const float4 *>(sc.q) + idx);
@@ -617,13 +636,14 @@ __device__ __forceinline__ void gadd(float *dst, float v) {
     atomicAdd(dst, v);
 }
 
-// LUT feature gradient accumulation
-__device__ __forceinline__ void lut_add(float *dst, float v) {
+// LUT feature gradient accumulation: the (x, y) features of one cell are adjacent, so one 8-byte
+// vector reduction adds both (dst is 8-byte aligned: per-CTA copies start at even float offsets).
+__device__ __forceinline__ void lut_add2(float *dst, float a, float b) {
 #ifdef FLARE_EXPERIMENT_NO_LUT_ATOMICS
-    if (v == 12345.678f) dst[0] = v;
+    if (a == 12345.678f) dst[0] = b;
     return;
 #endif
-    atomicAdd(dst, v);
+    asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(dst), "f"(a), "f"(b) : "memory");
 }
 
 __device__ __forceinline__ void red_add4(float *dst, bool vec, float a, float b, float c, float d) {
@@ -706,9 +726,11 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
         }
         int ind = -1;
         float t_hit = 0.0f;
+        int ind_next = have ? pp.hit_idx[slot] : -1;
         for (int h = 0; h < K_PASS; ++h) {
-            ind = have ? pp.hit_idx[(size_t)h * pp.count + slot] : -1;
+            ind = ind_next;
             t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
+            ind_next = (have && ind >= 0 && h + 1 < K_PASS) ? pp.hit_idx[(size_t)(h + 1) * pp.count + slot] : -1;
             const bool valid = ind >= 0 && T >= pp.T_thr;
             const int idc = ind >= 0 ? ind : 0;
             Geo g;
@@ -724,6 +746,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 tc_fence_before();
                 __syncthreads();
                 mlp_forward_tile(smem, xt, h1t, h2t, mm, y4, hd1, 64);
+                prefetch_hit(sc, ind_next);
                 __syncthreads();
                 if (s_abort) goto done;
             }
@@ -952,14 +975,10 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                         dxu += sc_ * __fmaf_rn(dx_, dfx_x, dy_ * dfx_y);
                         dxw += sc_ * __fmaf_rn(dx_, dfy_x, dy_ * dfy_y);
                         float *F = bo.dfeat_priv + (size_t)blockIdx.x * LUT_PRIV_STRIDE + 2 * (size_t)c.i00;
-                        lut_add(F, dx_ * vx * vy);
-                        lut_add(F + 1, dy_ * vx * vy);
-                        lut_add(F + 2, dx_ * ux * vy);
-                        lut_add(F + 3, dy_ * ux * vy);
-                        lut_add(F + 2 * c.R, dx_ * vx * uy);
-                        lut_add(F + 2 * c.R + 1, dy_ * vx * uy);
-                        lut_add(F + 2 * c.R + 2, dx_ * ux * uy);
-                        lut_add(F + 2 * c.R + 3, dy_ * ux * uy);
+                        lut_add2(F, dx_ * vx * vy, dy_ * vx * vy);
+                        lut_add2(F + 2, dx_ * ux * vy, dy_ * ux * vy);
+                        lut_add2(F + 2 * c.R, dx_ * vx * uy, dy_ * vx * uy);
+                        lut_add2(F + 2 * c.R + 2, dx_ * ux * uy, dy_ * ux * uy);
                     }
                 }
                 gu += dxu;
@@ -1354,7 +1373,15 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
             float tms = 0.0f, sms = 0.0f;
             cudaEventElapsedTime(&tms, r->prof_ev[2 * (r->prof_n - 2)], r->prof_ev[2 * (r->prof_n - 2) + 1]);
             cudaEventElapsedTime(&sms, r->prof_ev[2 * (r->prof_n - 1)], r->prof_ev[2 * (r->prof_n - 1) + 1]);
-            fprintf(stderr, "pass %lld rays %d trace %.3f ms shade %.3f ms\n", passes, count, tms, sms);
+            static unsigned long long last[ST_NSTATS];
+            unsigned long long h[ST_NSTATS];
+            cudaMemcpy(h, r->dstats, sizeof(h), cudaMemcpyDeviceToHost);
+            fprintf(stderr, "pass %lld rays %d trace %.3f ms shade %.3f ms nodes %llu prims %llu hits %llu\n", passes,
+                    count, tms, sms, h[ST_NODES] - last[ST_NODES], h[ST_PRIM_TESTS] - last[ST_PRIM_TESTS],
+                    h[ST_HITS] - last[ST_HITS]);
+            fprintf(stderr, "   max nodes per walk %llu\n", h[5]);
+            cudaMemset(r->dstats + 5, 0, 8);
+            memcpy(last, h, sizeof(h));
         }
 #endif
         prof_collect(r);
