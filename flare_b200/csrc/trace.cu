@@ -1,17 +1,19 @@
 // trace.cu -- k-nearest proxy traversal (replaces the reference's OptiX raygen + any-hit programs,
 // source/renderer/shaders.cu:81-189, and the diagnostic raygen used by Render, shaders.cu:19-77).
 //
-// One thread per ray walks the LBVH with a short local stack, nearer child first, and keeps the 16
-// smallest (t, primitive index) hits with t >= t_min in a register-resident sorted buffer (the
-// reference's any-hit insertion sort, shaders.cu:166-188, with ties broken by the smaller index so
-// the result is independent of traversal order).  A subtree is pruned when its box entry lies beyond
-// the current 16th hit.  Nodes are 64-byte records read as four 16-byte loads; primitive records are
-// 48 bytes in Morton order read as three 16-byte loads.
+// A warp walks the LBVH for a packet of 32 coherent rays (a whole warp per ray once a pass is sparse),
+// nearer child first, and each ray keeps the K smallest (t, primitive index) hits with t >= t_min in a
+// register-resident sorted buffer (the reference's any-hit insertion sort, shaders.cu:166-188, with ties
+// broken by the smaller index so the result is independent of traversal order).  A subtree is pruned
+// when its box entry lies beyond the ray's current K-th hit.  Nodes are 64-byte records read as four
+// 16-byte loads; primitive records are 48 bytes in Morton order read as three 16-byte loads.
 //
 // The hit test is exact fp32 with explicit rounding intrinsics; oracle/trace_oracle.c executes the
 // identical sequence, which is what makes hit lists bit-comparable.
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_select.cuh>
+
+#include <cstdlib>
 
 #include "renderer.cuh"
 
@@ -214,6 +216,171 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
 }
 
 
+// Group-per-ray traversal for sparse late passes: once few rays remain, a pass lasts as long as its
+// longest single walk, so G lanes (a quarter, half or whole warp) split one ray's walk.  Each step the
+// group pops up to G nodes of its shared stack, tests their children and pushes the entered internal
+// ones; a leaf is tested by the lane that met it, into that lane's own K-buffer.  The pruning bound is
+// the group minimum of the lanes' K-th hits: the ray's K-th nearest hit over all lanes lies no farther
+// than any one lane's K-th.  At the end a group merge emits the K nearest (t, index) entries in order.
+constexpr int WIDE_WARP_STACK = 2048;  // stack entries per warp, split evenly between its rays
+
+__device__ __forceinline__ bool key_less(float ta, int ia, float tb, int ib) {
+    return ta < tb || (ta == tb && ia < ib);
+}
+
+template <int K, int G>
+__global__ void __launch_bounds__(128) trace_group_kernel(
+    const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
+    const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
+    const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats) {
+    static_assert(G == 8 || G == 16 || G == 32, "group of 8, 16 or 32 lanes");
+    constexpr int CAP = WIDE_WARP_STACK * G / 32;
+    __shared__ int s_stack[4][WIDE_WARP_STACK];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int gl = lane % G, gid = lane / G;                 // lane within the group, group within the warp
+    const unsigned gmask = (G == 32 ? 0xffffffffu : ((1u << G) - 1u) << (gid * G));
+    const int j = (blockIdx.x * 4 + wib) * (32 / G) + gid;  // this group's ray slot
+    const bool live = j < count;
+    const unsigned lt_mask = (1u << gl) - 1u;
+    const int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
+    float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+    float t_min = INFINITY;
+    if (live) {
+        O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
+        v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
+        t_min = tmin_[ray];
+    }
+    unsigned long long nprim = 0, nnode = 0;
+    KBuf<K> kb;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        kb.t[k] = INFINITY;
+        kb.i[k] = 0x7fffffff;
+    }
+    const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
+                                  1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
+                                  1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
+    const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);
+    if (n == 1) {
+        float t;
+        if (gl == 0 && t_min < INFINITY) {
+            ++nprim;
+            if (hit_prim(rec, 0, O, v, t_min, poly, t)) kbuf_insert(kb, t, ids[0]);
+        }
+    } else if (n > 1) {
+        int *stack = s_stack[wib] + gid * CAP;
+        int sp = t_min < INFINITY ? 1 : 0;  // uniform within the group
+        if (gl == 0) stack[0] = 0;
+        const unsigned long long max_steps = 2ull * (unsigned long long)n + 64ull;
+        unsigned long long steps = 0;
+        __syncwarp();
+        // the whole warp steps together (shuffles and ballots span it); a group with an empty stack idles
+        while (__any_sync(0xffffffffu, sp > 0)) {
+            if (++steps > max_steps) {
+                if (lane == 0) atomicOr(status, ERR_INDEX);
+                break;
+            }
+            const int take = min(G, sp);
+            const int node = gl < take ? stack[sp - 1 - gl] : -1;
+            sp -= take;
+            float bound = kb.t[K - 1];
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1) bound = fminf(bound, __shfl_xor_sync(0xffffffffu, bound, o));
+            bool push_near = false, push_far = false;
+            int near_c = 0, far_c = 0;
+            if (node >= 0) {
+                ++nnode;
+                const float thi = __fmaf_rn(fabsf(bound), 1e-5f, bound);
+                const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
+                const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
+                const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
+                float t0 = 0.0f, t1 = 0.0f;
+                bool h0 = slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
+                bool h1 = slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
+                if (d.x < 0) {
+                    if (h0) {
+                        float t;
+                        ++nprim;
+                        if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bound)) {
+                            const int pid = __ldg(ids + ~d.x);
+                            if (key_less(t, pid, kb.t[K - 1], kb.i[K - 1])) kbuf_insert(kb, t, pid);
+                        }
+                    }
+                    h0 = false;
+                }
+                if (d.y < 0) {
+                    if (h1) {
+                        float t;
+                        ++nprim;
+                        if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bound)) {
+                            const int pid = __ldg(ids + ~d.y);
+                            if (key_less(t, pid, kb.t[K - 1], kb.i[K - 1])) kbuf_insert(kb, t, pid);
+                        }
+                    }
+                    h1 = false;
+                }
+                // the nearer child goes on top of the stack (pushed last)
+                const bool first0 = !h1 || (h0 && t0 <= t1);
+                push_near = h0 || h1;
+                push_far = h0 && h1;
+                near_c = first0 ? d.x : d.y;
+                far_c = first0 ? d.y : d.x;
+            }
+            const unsigned bf = (__ballot_sync(0xffffffffu, push_far) & gmask) >> (gid * G);
+            const unsigned bn = (__ballot_sync(0xffffffffu, push_near) & gmask) >> (gid * G);
+            const int nf = __popc(bf), nn = __popc(bn);
+            if (sp + nf + nn > CAP) {
+                if (gl == 0) atomicOr(status, ERR_STACK);
+                sp = 0;  // this ray's list is incomplete; the error bit reports it
+            } else {
+                if (push_far) stack[sp + __popc(bf & lt_mask)] = far_c;
+                if (push_near) stack[sp + nf + __popc(bn & lt_mask)] = near_c;
+                sp += nf + nn;
+            }
+            __syncwarp();
+        }
+    }
+    // merge: K rounds of a group argmin over the lanes' buffer heads
+    for (int k = 0; k < K; ++k) {
+        float bt = kb.t[0];
+        int bi = kb.i[0];
+#pragma unroll
+        for (int o = G / 2; o > 0; o >>= 1) {
+            const float ot = __shfl_xor_sync(0xffffffffu, bt, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (key_less(ot, oi, bt, bi)) {
+                bt = ot;
+                bi = oi;
+            }
+        }
+        if (gl == 0 && live) {
+            const bool valid = bi != 0x7fffffff;
+            t_out[(size_t)k * stride + j] = valid ? bt : INFINITY;
+            idx_out[(size_t)k * stride + j] = valid ? bi : -1;
+        }
+        if (bi != 0x7fffffff && kb.i[0] == bi && kb.t[0] == bt) {  // the winning lane drops its head
+#pragma unroll
+            for (int q = 0; q < K - 1; ++q) {
+                kb.t[q] = kb.t[q + 1];
+                kb.i[q] = kb.i[q + 1];
+            }
+            kb.t[K - 1] = INFINITY;
+            kb.i[K - 1] = 0x7fffffff;
+        }
+    }
+    if (stats) {
+        for (int o = 16; o > 0; o >>= 1) {
+            nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
+            nnode += __shfl_xor_sync(0xffffffffu, nnode, o);
+        }
+        if (lane == 0 && (nprim | nnode)) {
+            atomicAdd(stats + ST_PRIM_TESTS, nprim);
+            atomicAdd(stats + ST_NODES, nnode);
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // Ray ordering: rays are visited in the order of a 64-bit key, origin Morton code (30 bits, within the
 // batch's origin bounds) above the Morton code of the octahedral direction (2 x 16 bits), so the 32 rays
@@ -329,10 +496,35 @@ size_t ray_sort_temp_bytes(int max_rays) {
     return tmp;
 }
 
+static int getenv_int(const char *name, int dflt) {
+    const char *e = getenv(name);
+    return e ? atoi(e) : dflt;
+}
+
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
                  int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k) {
     if (count <= 0) return FLARE_OK;
     const int B = 128;
+    // Sparse passes: G lanes per ray, G chosen so the pass still spreads over the whole GPU
+    static const int g32_max = getenv_int("FLARE_TRACE_G32_MAX", 4096);
+    static const int g16_max = getenv_int("FLARE_TRACE_G16_MAX", 0);
+    static const int g8_max = getenv_int("FLARE_TRACE_G8_MAX", 0);
+    if (k == K_PASS && K_PASS != K_HITS && (count <= g32_max || count <= g16_max || count <= g8_max)) {
+        if (count <= g32_max)
+            trace_group_kernel<K_PASS, 32><<<(count + 3) / 4, B, 0, st>>>(
+                O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+                r->dstatus, r->dstats);
+        else if (count <= g16_max)
+            trace_group_kernel<K_PASS, 16><<<(count + 7) / 8, B, 0, st>>>(
+                O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+                r->dstatus, r->dstats);
+        else
+            trace_group_kernel<K_PASS, 8><<<(count + 15) / 16, B, 0, st>>>(
+                O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+                r->dstatus, r->dstats);
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    }
     if (k == K_PASS && K_PASS != K_HITS) {
         trace_packet_kernel<true, K_PASS><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes,
                                                                              r->rec, r->ids_sorted, r->n, t_out,
