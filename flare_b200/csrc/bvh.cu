@@ -6,7 +6,7 @@
 //      quaternion with S = 2/|q|^2, radius rho = max(0, kappa (11.3449 + 2 ln sigma))^(1/(2 kappa)))
 //      stored as [m, N, U/(e^sx rho), V/(e^sy rho)], plus a conservative AABB and the centre;
 //   2. scene bounds of the centres (ordered-int atomics);
-//   3. 30-bit Morton codes, CUB radix sort of (code, index) pairs;
+//   3. 32-bit extended Morton codes (centre + size class), CUB radix sort of (code, index) pairs;
 //   4. Karras (2012) radix-tree hierarchy, one thread per internal node;
 //   5. bottom-up box refit with one atomic flag per node; child boxes are stored in the parent so one
 //      64-byte node fetch tests both children.
@@ -101,18 +101,52 @@ __device__ __forceinline__ unsigned expand_bits10(unsigned v) {
     return v;
 }
 
-__global__ void morton_kernel(const float *__restrict__ m, int n, const int *__restrict__ bounds,
-                              unsigned *__restrict__ codes, int *__restrict__ ids) {
+// Sort key = extended Morton code: the top EMC_P bits of the 30-bit centre code, then EMC_S bits of
+// box-size class, then the next centre bits.  Primitives of very different sizes are separated just
+// below the top levels, so small primitives' nodes are not inflated by large overlapping neighbours
+// (cf. Vinkler et al. 2017, "Extended Morton codes for high performance bounding volume hierarchy
+// construction").  The size class splits log2(box extent / scene diagonal) over [EMC_LO, EMC_HI) evenly;
+// boxes outside clamp to the end classes, so scenes of uniformly small primitives get a plain Morton order.
+#ifndef FLARE_EMC_S
+#define FLARE_EMC_S 2
+#endif
+#ifndef FLARE_EMC_P
+#define FLARE_EMC_P 6
+#endif
+#ifndef FLARE_EMC_LO
+#define FLARE_EMC_LO -10.0f
+#endif
+#ifndef FLARE_EMC_HI
+#define FLARE_EMC_HI -3.0f
+#endif
+constexpr int MORTON_END_BIT = FLARE_EMC_S ? 32 : 30;
+
+__global__ void morton_kernel(const float *__restrict__ m, const float *__restrict__ aabb, int n,
+                              const int *__restrict__ bounds, unsigned *__restrict__ codes, int *__restrict__ ids) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     unsigned c = 0;
+    float diag2 = 0.0f;
 #pragma unroll
     for (int a = 0; a < 3; ++a) {
         float lo = ord2f(bounds[a]), hi = ord2f(bounds[3 + a]);
         float ext = hi - lo;
+        diag2 += ext * ext;
         float x = ext > 0.0f ? (m[3 * i + a] - lo) / ext : 0.5f;
         unsigned q = (unsigned)fminf(fmaxf(x * 1024.0f, 0.0f), 1023.0f);
         c |= expand_bits10(q) << (2 - a);
+    }
+    if (FLARE_EMC_S) {
+        const float *bx = aabb + 6 * (size_t)i;
+        float e = fmaxf(fmaxf(bx[3] - bx[0], bx[4] - bx[1]), bx[5] - bx[2]);
+        float rel = e * rsqrtf(fmaxf(diag2, 1e-30f));
+        // size class: log2 of the box extent over the scene diagonal, [LO, HI) in 2^S steps
+        float l = (log2f(fmaxf(rel, 1e-30f)) - FLARE_EMC_LO) * ((float)(1 << FLARE_EMC_S) / (FLARE_EMC_HI - FLARE_EMC_LO));
+        unsigned sz = (unsigned)fminf(fmaxf(l, 0.0f), (float)((1 << FLARE_EMC_S) - 1));
+        constexpr int P = FLARE_EMC_P, S = FLARE_EMC_S, L = 32 - P - S;
+        unsigned hi = P ? (c >> (30 - P)) : 0u;
+        unsigned lo = (L >= 30 - P) ? ((c << (L - (30 - P))) & ((1u << L) - 1u)) : ((c >> ((30 - P) - L)) & ((1u << L) - 1u));
+        c = (P ? (hi << (32 - P)) : 0u) | (sz << L) | lo;
     }
     codes[i] = c;
     ids[i] = i;
@@ -221,7 +255,7 @@ static int grow(flare_renderer *r, int n, cudaStream_t st) {
     FLARE_CUDA_TRY(cudaMalloc(&r->parent, (2 * N) * sizeof(int)));
     FLARE_CUDA_TRY(cudaMalloc(&r->refit_flag, (N > 1 ? N - 1 : 1) * sizeof(unsigned)));
     size_t tmp = 0;
-    cub::DeviceRadixSort::SortPairs(nullptr, tmp, r->morton, r->morton_sorted, r->ids, r->ids_sorted, n, 0, 30, st);
+    cub::DeviceRadixSort::SortPairs(nullptr, tmp, r->morton, r->morton_sorted, r->ids, r->ids_sorted, n, 0, MORTON_END_BIT, st);
     FLARE_CUDA_TRY(cudaMalloc(&r->sort_tmp, tmp));
     r->sort_tmp_bytes = tmp;
     r->cap_n = n;
@@ -239,10 +273,10 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
     init_bounds_kernel<<<1, 32, 0, st>>>(reinterpret_cast<int *>(r->bounds));
     prep_kernel<<<G, B, 0, st>>>(m, scale, q, opacity, kappa, n, r->frames, r->aabb,
                                  reinterpret_cast<int *>(r->bounds));
-    morton_kernel<<<G, B, 0, st>>>(m, n, reinterpret_cast<int *>(r->bounds), r->morton, r->ids);
+    morton_kernel<<<G, B, 0, st>>>(m, r->aabb, n, reinterpret_cast<int *>(r->bounds), r->morton, r->ids);
     size_t tmp = r->sort_tmp_bytes;
     FLARE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(r->sort_tmp, tmp, r->morton, r->morton_sorted, r->ids,
-                                                   r->ids_sorted, n, 0, 30, st));
+                                                   r->ids_sorted, n, 0, MORTON_END_BIT, st));
     if (n > 1) {
         FLARE_CUDA_TRY(cudaMemsetAsync(r->refit_flag, 0, (size_t)(n - 1) * sizeof(unsigned), st));
         karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(r->morton_sorted, n, r->nodes, r->parent);
@@ -262,10 +296,10 @@ int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, c
     int G = (n + B - 1) / B;
     init_bounds_kernel<<<1, 32, 0, st>>>(reinterpret_cast<int *>(g.bounds));
     prep_kernel<<<G, B, 0, st>>>(m, scale, q, opacity, kappa, n, g.frames, g.aabb, reinterpret_cast<int *>(g.bounds));
-    morton_kernel<<<G, B, 0, st>>>(m, n, reinterpret_cast<int *>(g.bounds), g.morton, g.ids);
+    morton_kernel<<<G, B, 0, st>>>(m, g.aabb, n, reinterpret_cast<int *>(g.bounds), g.morton, g.ids);
     size_t tmp = g.sort_tmp_bytes;
     FLARE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(g.sort_tmp, tmp, g.morton, g.morton_sorted, g.ids, g.ids_sorted, n,
-                                                   0, 30, st));
+                                                   0, MORTON_END_BIT, st));
     if (n > 1) {
         FLARE_CUDA_TRY(cudaMemsetAsync(g.refit_flag, 0, (size_t)(n - 1) * sizeof(unsigned), st));
         karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(g.morton_sorted, n, g.nodes, g.parent);
@@ -278,7 +312,7 @@ int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, c
 size_t geometry_sort_temp_bytes(int n) {
     size_t tmp = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, tmp, (unsigned *)nullptr, (unsigned *)nullptr, (int *)nullptr,
-                                    (int *)nullptr, n, 0, 30, (cudaStream_t)0);
+                                    (int *)nullptr, n, 0, MORTON_END_BIT, (cudaStream_t)0);
     return tmp;
 }
 
