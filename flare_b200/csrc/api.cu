@@ -156,7 +156,7 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
     ALLOC(r->dw, 16384 * sizeof(float));
     ALLOC(r->gscale, 64);
     ALLOC(r->hc_sum, 64);
-    ALLOC(r->dfeat_priv, (size_t)r->num_sms * 2 * 13184 * sizeof(float));
+    ALLOC(r->dfeat_priv, (size_t)r->num_sms * 2 * LUT_PRIV_FLOATS * sizeof(float));
     ALLOC(r->bounds, 128);
     ALLOC(r->ray_keys, 2 * R * sizeof(unsigned long long));
     ALLOC(r->ray_ids_tmp, R * sizeof(int));
@@ -191,7 +191,7 @@ int flare_destroy(flare_renderer *r) {
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
-                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->pgrad, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (r->h_count) cudaFreeHost(r->h_count);

@@ -19,6 +19,11 @@ constexpr int COND = FLARE_COND_DIM;           // 96
 constexpr int LUT = FLARE_LUT_SIZE;            // 13154 floats
 constexpr int MAX_SIDES = 64;
 constexpr int TRACE_STACK = 64;
+// Per-CTA LUT-gradient copy in the backward, "pair-major": 4 floats per cell hold the (x, y) gradient of
+// the cell and of its right neighbour, so the two corners of a bilinear row are one 16-byte reduction.
+constexpr int LUT_PRIV_FLOATS = 26368;  // 4 * 13154 / 2 = 26308, rounded up to 128 floats
+// Packed per-primitive gradient of the decoder backward: dm 3, ds 2, dq 4, dRGB 3, dA 1, dk 1, 2 pad.
+constexpr int PGRAD_FLOATS = 16;
 constexpr float LUT_SCALE = 0.29689279887990428378374198030042f;  // 1/sqrt(11.3449)
 
 // Device status word bits (first word of renderer->dstatus).

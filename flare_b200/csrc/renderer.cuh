@@ -45,7 +45,9 @@ struct flare_renderer {
     // ---- decoder scratch ----
     float *dw = nullptr;      // dense weight-gradient accumulators (see shade.cu)
     float *gscale = nullptr;  // backward gradient scale (1 float)
-    float *dfeat_priv = nullptr;  // per-CTA LUT gradient copies (2 * num_sms * 13184 floats)
+    float *dfeat_priv = nullptr;  // per-CTA LUT gradient copies (2 * num_sms * LUT_PRIV_FLOATS floats)
+    float *pgrad = nullptr;       // packed per-primitive gradients of the decoder backward (PGRAD_FLOATS each)
+    size_t pgrad_cap = 0;         // primitives pgrad holds
 
     // ---- hit cache: the passes of the last Forward_training, replayed by a matching Backward ----
     unsigned long long geom_version = 0;  // bumped by every flare_set_geometry

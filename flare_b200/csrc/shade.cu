@@ -63,7 +63,7 @@ constexpr int TM_DW = 128;  // backward: weight-gradient region starts at this c
 
 // The 6577-cell LUT receives 32 gradient atomics per hit; one table shared by every CTA serialises them
 // in L2, so each CTA accumulates into its own copy (L2-resident) and one kernel sums the copies.
-constexpr int LUT_PRIV_STRIDE = 13184;  // 13154 rounded up to 128 floats
+constexpr int LUT_PRIV_STRIDE = LUT_PRIV_FLOATS;
 
 // dense weight-gradient accumulator layout in renderer->dw (floats)
 constexpr int DW_W1 = 0, DW_B1 = 8192, DW_W2 = 8256, DW_B2 = 12352, DW_W3 = 12416, DW_B3 = 13440;
@@ -104,7 +104,8 @@ struct BwdIO {
     const float *dL_dI;
     float *dRGB, *dA, *dk, *dm, *ds, *dq, *dcond, *dfeat;
     float *dw;  // dense MLP gradient accumulators (DW_*)
-    float *dfeat_priv;  // per-CTA private LUT gradients (LUT_PRIV_STRIDE floats per CTA), reduced at the end
+    float *dfeat_priv;  // per-CTA private LUT gradients (pair-major, LUT_PRIV_STRIDE floats per CTA), reduced at the end
+    float *pgrad;       // packed per-primitive gradients (PGRAD_FLOATS per primitive), scattered at the end
     const float *dacc;
     float *prefix;
     const float *surface_normal;
@@ -661,6 +662,94 @@ __device__ __forceinline__ void red_add4(float *dst, bool vec, float a, float b,
     }
 }
 
+// Per-primitive gradients of one hit, in the order of the PG_* slots below.
+enum { PG_M = 0, PG_S = 3, PG_Q = 5, PG_RGB = 9, PG_A = 12, PG_K = 13, PG_N = 14 };
+static_assert(PG_N <= PGRAD_FLOATS, "packed layout");
+
+__device__ __forceinline__ float *pg_dst(const BwdIO &bo, int prim, int j) {
+    if (j < PG_S) return bo.dm + 3 * (size_t)prim + j;
+    if (j < PG_Q) return bo.ds + 2 * (size_t)prim + (j - PG_S);
+    if (j < PG_RGB) return bo.dq + 4 * (size_t)prim + (j - PG_Q);
+    if (j < PG_A) return bo.dRGB + 3 * (size_t)prim + (j - PG_RGB);
+    if (j == PG_A) return bo.dA + prim;
+    return bo.dk + prim;
+}
+
+// Geometry gradients (dm, ds, dq) from dL/du, dL/dw and dL/dt (restates Backward.cu:1587-1608, 2033-2216).
+__device__ __forceinline__ void geom_grads(const Geo &g, float3 v, float gu, float gw, float dLdt_depth, float ow,
+                                           float sgn, bool nvalid, const float Nm[3], float lambda_normal,
+                                           float pg[PG_N]) {
+            // ---- primitive geometry gradients from dL/du, dL/dw and dL/dt (depth) ----
+            float ndv = __fmaf_rn(g.N[0], v.x, __fmaf_rn(g.N[1], v.y, g.N[2] * v.z));
+            float inv_ndv = 1.0f / ndv;
+            float Uv = __fmaf_rn(g.U[0], v.x, __fmaf_rn(g.U[1], v.y, g.U[2] * v.z));
+            float Vv = __fmaf_rn(g.V[0], v.x, __fmaf_rn(g.V[1], v.y, g.V[2] * v.z));
+            // total dL/dt through u, w (P = O + t v) and the depth regulariser
+            float dLdt = __fmaf_rn(gu * g.sx, Uv, __fmaf_rn(gw * g.sy, Vv, dLdt_depth));
+            float kt = dLdt * inv_ndv;
+            // dL/dm = dL/dt N/(N.v) - (gu e^-sx U + gw e^-sy V)
+            float su = gu * g.sx, sw = gw * g.sy;
+            pg[PG_M] = kt * g.N[0] - (su * g.U[0] + sw * g.V[0]);
+            pg[PG_M + 1] = kt * g.N[1] - (su * g.U[1] + sw * g.V[1]);
+            pg[PG_M + 2] = kt * g.N[2] - (su * g.U[2] + sw * g.V[2]);
+            // dL/ds = -u dL/du (u = e^-s U.(P - m))
+            pg[PG_S] = -g.u * gu;
+            pg[PG_S + 1] = -g.w * gw;
+            // dL/dR for R = [U V N]: G_U = gu e^-sx (P-m), G_V = gw e^-sy (P-m),
+            // G_N = -dL/dt (P-m)/(N.v) - lambda_n o sgn N_target (the normal regulariser's opacity is held)
+            float ln = nvalid ? lambda_normal * (-ow * sgn) : 0.0f;
+            float Gm[3][3];
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                Gm[i][0] = su * g.d[i];
+                Gm[i][1] = sw * g.d[i];
+                Gm[i][2] = -kt * g.d[i] + ln * Nm[i];
+            }
+            // R = I + S M(q) with S = 2/|q|^2; dR/dq_k = S (dM/dq_k - S q_k M)
+            const float a = g.q[0], b = g.q[1], c = g.q[2], d = g.q[3], S = g.S;
+            float GM = Gm[0][0] * (-(c * c + d * d)) + Gm[0][1] * (b * c - a * d) + Gm[0][2] * (b * d + a * c) +
+                       Gm[1][0] * (b * c + a * d) + Gm[1][1] * (-(b * b + d * d)) + Gm[1][2] * (c * d - a * b) +
+                       Gm[2][0] * (b * d - a * c) + Gm[2][1] * (c * d + a * b) + Gm[2][2] * (-(b * b + c * c));
+            float dMa = -d * Gm[0][1] + c * Gm[0][2] + d * Gm[1][0] - b * Gm[1][2] - c * Gm[2][0] + b * Gm[2][1];
+            float dMb = c * Gm[0][1] + d * Gm[0][2] + c * Gm[1][0] - 2.0f * b * Gm[1][1] - a * Gm[1][2] +
+                        d * Gm[2][0] + a * Gm[2][1] - 2.0f * b * Gm[2][2];
+            float dMc = -2.0f * c * Gm[0][0] + b * Gm[0][1] + a * Gm[0][2] + b * Gm[1][0] + d * Gm[1][2] -
+                        a * Gm[2][0] + d * Gm[2][1] - 2.0f * c * Gm[2][2];
+            float dMd = -2.0f * d * Gm[0][0] - a * Gm[0][1] + b * Gm[0][2] + a * Gm[1][0] - 2.0f * d * Gm[1][1] +
+                        c * Gm[1][2] + b * Gm[2][0] + c * Gm[2][1];
+            pg[PG_Q] = S * (dMa - S * a * GM);
+            pg[PG_Q + 1] = S * (dMb - S * b * GM);
+            pg[PG_Q + 2] = S * (dMc - S * c * GM);
+            pg[PG_Q + 3] = S * (dMd - S * d * GM);
+}
+
+// One hit's per-primitive gradients straight into the caller's arrays (decoder-free path).
+__device__ __forceinline__ void flush_prim_direct(const BwdIO &bo, int prim, const float pg[PG_N]) {
+#pragma unroll
+    for (int j = 0; j < PG_N; ++j)
+        if (j < PG_Q || j >= PG_RGB) gadd(pg_dst(bo, prim, j), pg[j]);
+    red_add4(bo.dq + 4 * (size_t)prim, bo.vec4, pg[PG_Q], pg[PG_Q + 1], pg[PG_Q + 2], pg[PG_Q + 3]);
+}
+
+// Asynchronous bulk reduction of `bytes` (a multiple of 16, both addresses 16-byte aligned) from shared
+// to global memory: the copy engine performs the adds, so one instruction replaces a row of per-lane
+// vector reductions.  The issuing thread waits (wait_bulk_read) before the source is overwritten.
+__device__ __forceinline__ void bulk_red_add_f32(float *gdst, const float *ssrc, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gdst),
+                 "r"(smem_u32(ssrc)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void wait_bulk_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void wait_bulk_done() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Per-lane staging rows: 96 descriptor-gradient floats then the PGRAD_FLOATS packed primitive gradients
+// (row stride an odd number of 16-byte chunks so the lanes' vector stores hit distinct banks); warps 0-1
+// use the X tile, 2-3 the H1-H2 tiles, which are free between the last tensor-core stage of a slot and the
+// next slot's X row.
+constexpr int DC_ROW = 116;
+static_assert(2 * 32 * DC_ROW * 4 <= 32768, "two warps' rows fit the X tile and the H1-H2 tiles");
+
 template <bool DEC>
 __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, BwdIO bo) {
     extern __shared__ __align__(1024) char smem[];
@@ -739,6 +828,9 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             const float cu = g.u * LUT_SCALE, cw = g.w * LUT_SCALE;
             float y4[4] = {0, 0, 0, 0};
             float hd1[64];
+            float pg[PG_N];  // this hit's per-primitive gradients (layout PG_*)
+#pragma unroll
+            for (int e = 0; e < PG_N; ++e) pg[e] = 0.0f;
             if (DEC) {
                 if (!__syncthreads_or(valid)) continue;  // uniform
                 write_x_row(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
@@ -806,14 +898,14 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 run[0] = __fmaf_rn(dRGB0, rgba.x, run[0]);
                 run[1] = __fmaf_rn(dRGB1, rgba.y, run[1]);
                 run[2] = __fmaf_rn(dRGB2, rgba.z, run[2]);
-                gadd(bo.dRGB + 3 * (size_t)ind, dRGB0 * dLdI[0]);
-                gadd(bo.dRGB + 3 * (size_t)ind + 1, dRGB1 * dLdI[1]);
-                gadd(bo.dRGB + 3 * (size_t)ind + 2, dRGB2 * dLdI[2]);
-                gadd(bo.dA + ind, alpha * (1.0f - opa1) * gsum);
                 // kappa = 1 + softplus(k): dG/dkappa (Backward.cu:1882-1894)
                 float dk = alpha * gsum * 0.5f * g.r2k * sigm(g.kraw) * g.kinv * (g.kinv - __logf(g.r2));
                 if (isnan(dk)) dk = 0.0f;
-                gadd(bo.dk + ind, dk);
+                pg[PG_RGB] = dRGB0 * dLdI[0];
+                pg[PG_RGB + 1] = dRGB1 * dLdI[1];
+                pg[PG_RGB + 2] = dRGB2 * dLdI[2];
+                pg[PG_A] = alpha * (1.0f - opa1) * gsum;
+                pg[PG_K] = dk;
                 // delta3: gradients of the layer-3 pre-activations
                 d3[0] = dLdI[0] * rgba.x * alpha * T_prev * dz3[0];
                 d3[1] = dLdI[1] * rgba.y * alpha * T_prev * dz3[1];
@@ -954,6 +1046,32 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     mma_commit(mm.mbar);
                 }
                 mma_wait(mm);
+                // descriptor gradient: dX[32:128) at TMEM columns [16, 112) -> this lane's staging row ->
+                // one bulk reduction into the primitive's row (vector reductions when not 16-byte aligned)
+                float *dc = bo.dcond + (size_t)idc * 96;
+                const int wid = tid >> 5;
+                float *dcrow = reinterpret_cast<float *>(wid < 2 ? xt : h1t) + ((wid & 1) * 32 + (tid & 31)) * DC_ROW;
+#pragma unroll
+                for (int b = 0; b < 6; ++b) {
+                    float v16[16];
+                    tmem_ld16(mm.tmem + lane + 16 + 16 * b, v16);
+                    tmem_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int e = 0; e < 16; e += 4) {
+                            if (bo.vec4)
+                                *reinterpret_cast<float4 *>(dcrow + 16 * b + e) =
+                                    make_float4(v16[e] * ginv, v16[e + 1] * ginv, v16[e + 2] * ginv, v16[e + 3] * ginv);
+                            else
+                                red_add4(dc + 16 * b + e, false, v16[e] * ginv, v16[e + 1] * ginv, v16[e + 2] * ginv,
+                                         v16[e + 3] * ginv);
+                        }
+                    }
+                }
+                if (valid && bo.vec4) {
+                    fence_async_smem();
+                    bulk_red_add_f32(dc, dcrow, 96 * 4);
+                }
                 float dx16[16];
                 tmem_ld16(mm.tmem + lane, dx16);
                 tmem_wait_ld();
@@ -974,75 +1092,35 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                         float sc_ = 0.5f * LUT_SCALE * ((float)c.R - 1.0f);
                         dxu += sc_ * __fmaf_rn(dx_, dfx_x, dy_ * dfx_y);
                         dxw += sc_ * __fmaf_rn(dx_, dfy_x, dy_ * dfy_y);
-                        float *F = bo.dfeat_priv + (size_t)blockIdx.x * LUT_PRIV_STRIDE + 2 * (size_t)c.i00;
-                        lut_add2(F, dx_ * vx * vy, dy_ * vx * vy);
-                        lut_add2(F + 2, dx_ * ux * vy, dy_ * ux * vy);
-                        lut_add2(F + 2 * c.R, dx_ * vx * uy, dy_ * vx * uy);
-                        lut_add2(F + 2 * c.R + 2, dx_ * ux * uy, dy_ * ux * uy);
+                        float *F = bo.dfeat_priv + (size_t)blockIdx.x * LUT_PRIV_STRIDE + 4 * (size_t)c.i00;
+                        red_add_v4(F, dx_ * vx * vy, dy_ * vx * vy, dx_ * ux * vy, dy_ * ux * vy);
+                        red_add_v4(F + 4 * c.R, dx_ * vx * uy, dy_ * vx * uy, dx_ * ux * uy, dy_ * ux * uy);
                     }
                 }
                 gu += dxu;
                 gw += dxw;
-                // descriptor gradient: dX[32:128) at TMEM columns [16, 112)
-                float *dc = bo.dcond + (size_t)idc * 96;
+                if (valid) {
+                    geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
+                    if (bo.vec4) {  // the packed row rides behind the descriptor row in the staging row
 #pragma unroll
-                for (int b = 0; b < 6; ++b) {
-                    float v16[16];
-                    tmem_ld16(mm.tmem + lane + 16 + 16 * b, v16);
-                    tmem_wait_ld();
-                    if (valid) {
-#pragma unroll
-                        for (int e = 0; e < 16; e += 4)
-                            red_add4(dc + 16 * b + e, bo.vec4, v16[e] * ginv, v16[e + 1] * ginv,
-                                     v16[e + 2] * ginv, v16[e + 3] * ginv);
+                        for (int e = 0; e < PG_N; e += 2)
+                            *reinterpret_cast<float2 *>(dcrow + 96 + e) = make_float2(pg[e], pg[e + 1]);
+                        *reinterpret_cast<float2 *>(dcrow + 96 + PG_N) = make_float2(0.0f, 0.0f);
+                        fence_async_smem();
+                        bulk_red_add_f32(bo.pgrad + (size_t)ind * PGRAD_FLOATS, dcrow + 96, PGRAD_FLOATS * 4);
+                    } else {
+                        flush_prim_direct(bo, ind, pg);
                     }
                 }
+                if (valid && bo.vec4) wait_bulk_read();  // the staging rows are overwritten next slot
                 tc_fence_before();
                 __syncthreads();
                 if (tid == 0) s_first = 0;
                 if (s_abort) goto done;
             }
-            if (valid) {
-                // ---- primitive geometry gradients from dL/du, dL/dw and dL/dt (depth) ----
-                float ndv = __fmaf_rn(g.N[0], v.x, __fmaf_rn(g.N[1], v.y, g.N[2] * v.z));
-                float inv_ndv = 1.0f / ndv;
-                float Uv = __fmaf_rn(g.U[0], v.x, __fmaf_rn(g.U[1], v.y, g.U[2] * v.z));
-                float Vv = __fmaf_rn(g.V[0], v.x, __fmaf_rn(g.V[1], v.y, g.V[2] * v.z));
-                // total dL/dt through u, w (P = O + t v) and the depth regulariser
-                float dLdt = __fmaf_rn(gu * g.sx, Uv, __fmaf_rn(gw * g.sy, Vv, dLdt_depth));
-                float kt = dLdt * inv_ndv;
-                // dL/dm = dL/dt N/(N.v) - (gu e^-sx U + gw e^-sy V)
-                float su = gu * g.sx, sw = gw * g.sy;
-                gadd(bo.dm + 3 * (size_t)ind, kt * g.N[0] - (su * g.U[0] + sw * g.V[0]));
-                gadd(bo.dm + 3 * (size_t)ind + 1, kt * g.N[1] - (su * g.U[1] + sw * g.V[1]));
-                gadd(bo.dm + 3 * (size_t)ind + 2, kt * g.N[2] - (su * g.U[2] + sw * g.V[2]));
-                // dL/ds = -u dL/du (u = e^-s U.(P - m))
-                gadd(bo.ds + 2 * (size_t)ind, -g.u * gu);
-                gadd(bo.ds + 2 * (size_t)ind + 1, -g.w * gw);
-                // dL/dR for R = [U V N]: G_U = gu e^-sx (P-m), G_V = gw e^-sy (P-m),
-                // G_N = -dL/dt (P-m)/(N.v) - lambda_n o sgn N_target (the normal regulariser's opacity is held)
-                float ln = nvalid ? bo.lambda_normal * (-ow * sgn) : 0.0f;
-                float Gm[3][3];
-#pragma unroll
-                for (int i = 0; i < 3; ++i) {
-                    Gm[i][0] = su * g.d[i];
-                    Gm[i][1] = sw * g.d[i];
-                    Gm[i][2] = -kt * g.d[i] + ln * Nm[i];
-                }
-                // R = I + S M(q) with S = 2/|q|^2; dR/dq_k = S (dM/dq_k - S q_k M)
-                const float a = g.q[0], b = g.q[1], c = g.q[2], d = g.q[3], S = g.S;
-                float GM = Gm[0][0] * (-(c * c + d * d)) + Gm[0][1] * (b * c - a * d) + Gm[0][2] * (b * d + a * c) +
-                           Gm[1][0] * (b * c + a * d) + Gm[1][1] * (-(b * b + d * d)) + Gm[1][2] * (c * d - a * b) +
-                           Gm[2][0] * (b * d - a * c) + Gm[2][1] * (c * d + a * b) + Gm[2][2] * (-(b * b + c * c));
-                float dMa = -d * Gm[0][1] + c * Gm[0][2] + d * Gm[1][0] - b * Gm[1][2] - c * Gm[2][0] + b * Gm[2][1];
-                float dMb = c * Gm[0][1] + d * Gm[0][2] + c * Gm[1][0] - 2.0f * b * Gm[1][1] - a * Gm[1][2] +
-                            d * Gm[2][0] + a * Gm[2][1] - 2.0f * b * Gm[2][2];
-                float dMc = -2.0f * c * Gm[0][0] + b * Gm[0][1] + a * Gm[0][2] + b * Gm[1][0] + d * Gm[1][2] -
-                            a * Gm[2][0] + d * Gm[2][1] - 2.0f * c * Gm[2][2];
-                float dMd = -2.0f * d * Gm[0][0] - a * Gm[0][1] + b * Gm[0][2] + a * Gm[1][0] - 2.0f * d * Gm[1][1] +
-                            c * Gm[1][2] + b * Gm[2][0] + c * Gm[2][1];
-                red_add4(bo.dq + 4 * (size_t)ind, bo.vec4, S * (dMa - S * a * GM), S * (dMb - S * b * GM),
-                         S * (dMc - S * c * GM), S * (dMd - S * d * GM));
+            if (!DEC && valid) {  // decoder-free path: straight into the caller's arrays
+                geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
+                flush_prim_direct(bo, ind, pg);
             }
         }
         {
@@ -1058,6 +1136,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     }
 done:
     if (DEC) {
+        wait_bulk_done();
         if (s_abort && tid == 0) atomicOr(pp.status, ERR_MBAR);
         tc_fence_before();
         __syncthreads();
@@ -1136,12 +1215,37 @@ __global__ void grad_scale_finish_kernel(float *scale) {
 }
 
 // dfeat[i] += sum over the per-CTA copies
+// Sums the per-CTA pair-major copies: feature i of cell c = i / 2 is the cell's own slot plus the
+// right-neighbour slot of cell c - 1 (a bilinear row never spans two rows or levels, so that slot is
+// zero wherever c - 1 is not a left corner of c).
 __global__ void reduce_lut_kernel(const float *__restrict__ priv, int copies, float *__restrict__ dfeat) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= LUT) return;
+    const int cell = i >> 1, f = i & 1;
     float acc = 0.0f;
-    for (int c = 0; c < copies; ++c) acc += priv[(size_t)c * LUT_PRIV_STRIDE + i];
+    for (int c = 0; c < copies; ++c) {
+        const float *P = priv + (size_t)c * LUT_PRIV_STRIDE;
+        acc += P[4 * cell + f];
+        if (cell > 0) acc += P[4 * (cell - 1) + 2 + f];
+    }
     dfeat[i] += acc;
+}
+
+// Adds the packed per-primitive gradients of the decoder backward into the caller's arrays.
+__global__ void scatter_pgrad_kernel(const float4 *__restrict__ pg, int n, float *dm, float *ds, float *dq, float *dRGB,
+                                     float *dA, float *dk) {
+    int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= n) return;
+    const float4 a = pg[4 * (size_t)p], b = pg[4 * (size_t)p + 1], c = pg[4 * (size_t)p + 2], d = pg[4 * (size_t)p + 3];
+    if (a.x == 0.0f && a.y == 0.0f && a.z == 0.0f && a.w == 0.0f && b.x == 0.0f && b.y == 0.0f && b.z == 0.0f &&
+        b.w == 0.0f && c.x == 0.0f && c.y == 0.0f && c.z == 0.0f && c.w == 0.0f && d.x == 0.0f && d.y == 0.0f)
+        return;  // not hit
+    dm[3 * (size_t)p] += a.x; dm[3 * (size_t)p + 1] += a.y; dm[3 * (size_t)p + 2] += a.z;
+    ds[2 * (size_t)p] += a.w; ds[2 * (size_t)p + 1] += b.x;
+    dq[4 * (size_t)p] += b.y; dq[4 * (size_t)p + 1] += b.z; dq[4 * (size_t)p + 2] += b.w; dq[4 * (size_t)p + 3] += c.x;
+    dRGB[3 * (size_t)p] += c.y; dRGB[3 * (size_t)p + 1] += c.z; dRGB[3 * (size_t)p + 2] += c.w;
+    dA[p] += d.x;
+    dk[p] += d.y;
 }
 
 // Adds the dense MLP gradients into row 0 of the reference's fragment-layout buffers
@@ -1469,6 +1573,14 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     bo.lambda_depth = a->lambda_depth; bo.reg_a = a->reg_a; bo.reg_b = a->reg_b; bo.lambda_normal = a->lambda_normal;
     bo.gscale = r->gscale;
     bo.dfeat_priv = r->dfeat_priv;
+    if (dec && (size_t)sc->n > r->pgrad_cap) {
+        cudaFree(r->pgrad);
+        r->pgrad = nullptr;
+        r->pgrad_cap = 0;
+        FLARE_CUDA_TRY(cudaMalloc(&r->pgrad, (size_t)sc->n * PGRAD_FLOATS * sizeof(float)));
+        r->pgrad_cap = sc->n;
+    }
+    bo.pgrad = r->pgrad;
     bo.vec4 = ((reinterpret_cast<uintptr_t>(a->dL_dq) | reinterpret_cast<uintptr_t>(dec ? a->dL_dcond : a->dL_dq)) & 15) == 0;
     init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
@@ -1483,6 +1595,7 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
                                                                              r->gscale);
         grad_scale_finish_kernel<<<1, 1, 0, st>>>(r->gscale);
         FLARE_CUDA_TRY(cudaMemsetAsync(r->dfeat_priv, 0, (size_t)r->num_sms * 2 * LUT_PRIV_STRIDE * sizeof(float), st));
+        if (sc->n > 0) FLARE_CUDA_TRY(cudaMemsetAsync(r->pgrad, 0, (size_t)sc->n * PGRAD_FLOATS * sizeof(float), st));
         FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             SM_BWD_BYTES));
     }
@@ -1535,6 +1648,10 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     if (dec) {
         pack_dw_kernel<<<32, 256, 0, st>>>(r->dw, a->dL_dw1, a->dL_db1, a->dL_dw2, a->dL_db2, a->dL_dw3, a->dL_db3);
         reduce_lut_kernel<<<(LUT + 255) / 256, 256, 0, st>>>(r->dfeat_priv, r->num_sms * 2, a->dL_dfeatures);
+        if (sc->n > 0)
+            scatter_pgrad_kernel<<<(sc->n + 255) / 256, 256, 0, st>>>(reinterpret_cast<const float4 *>(r->pgrad), sc->n,
+                                                                      a->dL_dm, a->dL_ds, a->dL_dq, a->dL_dRGB,
+                                                                      a->dL_dA, a->dL_dk);
         FLARE_CUDA_TRY(cudaGetLastError());
     }
     return FLARE_OK;
