@@ -88,6 +88,7 @@ struct PassP {
     const int *hit_idx;
     float *T, *t_min;
     unsigned char *flags;  // per list slot: the ray stays active (compacted in list order after the pass)
+    int *work;             // next unclaimed list slot (zeroed before each launch that claims rays)
     int *status;
     unsigned long long *stats;
     float bg0, bg1, bg2, T_thr;
@@ -787,37 +788,58 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     }
     const float2 *lut2 = reinterpret_cast<const float2 *>(sc.features);
     char *xt = smem + SM_BWD_X, *d3t = smem + SM_BWD_D3, *h1t = smem + SM_BWD_H1, *h2t = smem + SM_BWD_H2;
-    const int nchunks = (pp.count + 127) / 128;
-    for (int chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
-        const int slot = chunk * 128 + tid;
-        const bool have = slot < pp.count;
-        const int ray = have ? pp.list_in[slot] : -1;
-        float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
-        float T = 0.0f;
-        float dLdI[3] = {0, 0, 0}, run[3] = {0, 0, 0};  // run = -(colour from this hit onwards, incl. bg)
-        float D[4] = {0, 0, 0, 0}, P[4] = {0, 0, 0, 0};
-        float Nm[3] = {0, 0, 0};
-        bool nvalid = false;
-        if (have) {
-            O = make_float3(pp.O[3 * (size_t)ray], pp.O[3 * (size_t)ray + 1], pp.O[3 * (size_t)ray + 2]);
-            v = make_float3(pp.v[3 * (size_t)ray], pp.v[3 * (size_t)ray + 1], pp.v[3 * (size_t)ray + 2]);
-            T = pp.T[ray];
-            for (int c = 0; c < 3; ++c) {
-                dLdI[c] = bo.dL_dI[3 * (size_t)ray + c];
-                run[c] = -bo.I[3 * (size_t)ray + c];
+    // Each row (thread) works through rays of the pass list, one hit slot per iteration; when its ray
+    // finishes the pass (a slot that no longer composites, or all K_PASS slots done) the row claims the
+    // next ray, so the tiles stay full instead of idling until the tile's slowest ray is done.
+    int slot = -1, ray = 0, h = 0;
+    bool have = false, exhausted = false;
+    float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+    float T = 0.0f;
+    float dLdI[3] = {0, 0, 0}, run[3] = {0, 0, 0};  // run = -(colour from this hit onwards, incl. bg)
+    float D[4] = {0, 0, 0, 0}, P[4] = {0, 0, 0, 0};
+    float Nm[3] = {0, 0, 0};
+    bool nvalid = false;
+    int ind = -1, ind_next = -1;
+    float t_hit = 0.0f;
+    while (true) {
+        {   // rows without a ray claim the next ones (one atomic per warp)
+            const bool need = !have && !exhausted;
+            const unsigned nm = __ballot_sync(0xffffffffu, need);
+            if (nm) {
+                const int ln = tid & 31, leader = __ffs(nm) - 1;
+                int base = 0;
+                if (ln == leader) base = atomicAdd(pp.work, __popc(nm));
+                base = __shfl_sync(0xffffffffu, base, leader);
+                if (need) {
+                    const int s_ = base + __popc(nm & ((1u << ln) - 1u));
+                    if (s_ < pp.count) {
+                        slot = s_;
+                        have = true;
+                        h = 0;
+                        ray = pp.list_in[slot];
+                        O = make_float3(pp.O[3 * (size_t)ray], pp.O[3 * (size_t)ray + 1], pp.O[3 * (size_t)ray + 2]);
+                        v = make_float3(pp.v[3 * (size_t)ray], pp.v[3 * (size_t)ray + 1], pp.v[3 * (size_t)ray + 2]);
+                        T = pp.T[ray];
+                        for (int c = 0; c < 3; ++c) {
+                            dLdI[c] = bo.dL_dI[3 * (size_t)ray + c];
+                            run[c] = -bo.I[3 * (size_t)ray + c];
+                        }
+                        for (int c = 0; c < 4; ++c) {
+                            D[c] = bo.dacc[4 * (size_t)ray + c];
+                            P[c] = bo.prefix[4 * (size_t)ray + c];
+                        }
+                        for (int c = 0; c < 3; ++c) Nm[c] = bo.surface_normal[3 * (size_t)ray + c];
+                        nvalid = __fmaf_rn(Nm[0], Nm[0], __fmaf_rn(Nm[1], Nm[1], Nm[2] * Nm[2])) > 0.0f;
+                        ind_next = pp.hit_idx[slot];
+                    } else {
+                        exhausted = true;
+                    }
+                }
             }
-            for (int c = 0; c < 4; ++c) {
-                D[c] = bo.dacc[4 * (size_t)ray + c];
-                P[c] = bo.prefix[4 * (size_t)ray + c];
-            }
-            for (int c = 0; c < 3; ++c) Nm[c] = bo.surface_normal[3 * (size_t)ray + c];
-            nvalid = __fmaf_rn(Nm[0], Nm[0], __fmaf_rn(Nm[1], Nm[1], Nm[2] * Nm[2])) > 0.0f;
         }
-        int ind = -1;
-        float t_hit = 0.0f;
-        int ind_next = have ? pp.hit_idx[slot] : -1;
-        for (int h = 0; h < K_PASS; ++h) {
-            ind = ind_next;
+        if (!__syncthreads_or(have)) break;
+        {
+            ind = have ? ind_next : -1;
             t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
             ind_next = (have && ind >= 0 && h + 1 < K_PASS) ? pp.hit_idx[(size_t)(h + 1) * pp.count + slot] : -1;
             const bool valid = ind >= 0 && T >= pp.T_thr;
@@ -831,8 +853,8 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             float pg[PG_N];  // this hit's per-primitive gradients (layout PG_*)
 #pragma unroll
             for (int e = 0; e < PG_N; ++e) pg[e] = 0.0f;
-            if (DEC) {
-                if (!__syncthreads_or(valid)) continue;  // uniform
+            const bool any_valid = DEC ? __syncthreads_or(valid) : false;  // uniform
+            if (DEC && any_valid) {
                 write_x_row(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
                 fence_async_smem();
                 tc_fence_before();
@@ -918,7 +940,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 ow = o;
             }
             // ---- decoder backward on the tensor core ----
-            if (DEC) {
+            if (DEC && any_valid) {
                 {   // delta3 tile row, scaled into the f16 range and split into hi (columns 0..3) and
                     // lo = delta3 - hi (columns 4..7); zero for rows that do not contribute
                     uint4 *T3 = reinterpret_cast<uint4 *>(d3t);
@@ -1122,16 +1144,18 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
                 flush_prim_direct(bo, ind, pg);
             }
-        }
-        {
-            const bool active = have && ind >= 0 && T >= pp.T_thr;
             if (have) {
-                for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
-                for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
-                pp.t_min[ray] = ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY;
-                pp.T[ray] = T;
+                ++h;
+                if (!valid || h == K_PASS) {  // this ray's pass is done: write its state back
+                    const bool active = valid && T >= pp.T_thr;  // all K_PASS slots composited, not terminated
+                    for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
+                    for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
+                    pp.t_min[ray] = active ? nextafterf(t_hit, INFINITY) : INFINITY;
+                    pp.T[ray] = T;
+                    pp.flags[slot] = active;
+                    have = false;
+                }
             }
-            if (have) pp.flags[slot] = active;
         }
     }
 done:
@@ -1511,6 +1535,7 @@ static PassP make_pass(flare_renderer *r, const float *O, const float *v, float 
     pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
     pp.T = r->T; pp.t_min = r->t_min;
     pp.flags = r->pass_flags;
+    pp.work = r->counters + 1;
     pp.status = r->dstatus;
     pp.stats = r->dstats;
     pp.bg0 = bg0; pp.bg1 = bg1; pp.bg2 = bg2;
@@ -1607,6 +1632,7 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         pp.hit_t = ht;
         pp.hit_idx = hi;
         int chunks = (count + 127) / 128;
+        FLARE_CUDA_TRY(cudaMemsetAsync(pp.work, 0, sizeof(int), st));
         if (dec) {
             int grid = std::min(chunks, r->num_sms * 2);
             shade_bwd_kernel<true><<<grid, 128, SM_BWD_BYTES, st>>>(sp, pp, bo);
