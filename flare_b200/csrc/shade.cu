@@ -41,8 +41,14 @@ constexpr int SM_W1 = 0;                  // 64x128 f16, K chunk stride 1024
 constexpr int SM_W2 = SM_W1 + 16384;      // 64x64 f16, K chunk stride 1024
 constexpr int SM_W3 = SM_W2 + 8192;       // 16x64 f16, K chunk stride 256
 constexpr int SM_BIAS = SM_W3 + 2048;     // b1 64, b2 64, b3 16 floats
+#ifndef FLARE_FWD_LUT_SMEM
+#define FLARE_FWD_LUT_SMEM 0  // 1: the forward stages the LUT in shared memory; 0: reads it through L1 (3 CTAs/SM fit)
+#endif
+#ifndef FLARE_FWD_CTAS
+#define FLARE_FWD_CTAS 3      // resident forward CTAs per SM the grid is sized for
+#endif
 constexpr int SM_FWD_LUT = SM_BIAS + 1024;                    // 13154 floats
-constexpr int SM_FWD_TILE = ((SM_FWD_LUT + LUT * 4 + 1023) / 1024) * 1024;  // 128x128 f16
+constexpr int SM_FWD_TILE = ((SM_FWD_LUT + (FLARE_FWD_LUT_SMEM ? LUT * 4 : 0) + 1023) / 1024) * 1024;  // 128x128 f16
 constexpr int SM_FWD_MISC = SM_FWD_TILE + 32768;
 constexpr int SM_FWD_BYTES = SM_FWD_MISC + 64;
 
@@ -462,7 +468,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             s_abort = 0;
         }
         if (tid < 32) tmem_alloc(tmem_slot, TM_FWD_COLS);
-        load_decoder(smem, sc, true);
+        load_decoder(smem, sc, FLARE_FWD_LUT_SMEM);
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
@@ -471,7 +477,8 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
         mm.mbar = smem + SM_FWD_MISC;
         mm.abort = &s_abort;
     }
-    const float2 *lut2 = reinterpret_cast<const float2 *>(smem + SM_FWD_LUT);
+    const float2 *lut2 = FLARE_FWD_LUT_SMEM ? reinterpret_cast<const float2 *>(smem + SM_FWD_LUT)
+                                            : reinterpret_cast<const float2 *>(sc.features);
     char *tile = smem + SM_FWD_TILE;
     unsigned long long nhits = 0;
     const int nchunks = (pp.count + 127) / 128;
@@ -1328,7 +1335,7 @@ static int launch_fwd(flare_renderer *r, const SceneP &sp, const PassP &pp, cons
     int smem = DEC ? SM_FWD_BYTES : 0;
     if (DEC) FLARE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int chunks = (pp.count + 127) / 128;
-    int grid = DEC ? std::min(chunks, r->num_sms * 2) : chunks;
+    int grid = DEC ? std::min(chunks, r->num_sms * FLARE_FWD_CTAS) : chunks;
     kern<<<grid, 128, smem, st>>>(sp, pp, fo);
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
