@@ -44,6 +44,11 @@ B_HIT_TRACE = 64                 # one 64-B node per composited hit
 B_HIT_FWD = 56 + 192             # primitive record + fp16 descriptor row
 B_HIT_BWD = 56 + 192 + 440       # re-read + gradient writes (14 geometry + 96 descriptor fp32)
 B_RAY_FWD, B_RAY_BWD = 44, 24
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per traversal launch, measured with a one-pass
+# ncu capture of the config-3 bench command (mean of six launches: passes 0, 1 and 2 of two views).  Most
+# of it is the 48-slot (t, index) hit lists each pass writes (8 B per slot); node and record fetches are
+# mostly L2 hits.  Only valid for the config-3 workload; other workloads report null.
+TRACE_DRAM_BYTES_PER_LAUNCH = {3: 585.2e6}
 FLOP_HIT_FWD = 2 * (128 * 64 + 64 * 64 + 64 * 4)
 
 
@@ -152,10 +157,12 @@ def time_steps(fn, steps, world):
     return ms
 
 
-def kernel_roofline(kt, hits, rays, hbm):
-    """Achieved GB/s of each kernel = algorithmic bytes / kernel time; the dominant one is returned."""
+def kernel_roofline(kt, hits, rays, hbm, traversals=1.0):
+    """Achieved GB/s of each kernel = algorithmic bytes / kernel time; the dominant one is returned.
+    `traversals` = traversals of the hit lists per step (1 when the backward replays the forward's cached
+    hits, 2 when it traces again)."""
     algo = {
-        "trace": 2 * hits * B_HIT_TRACE,  # forward and backward traversals
+        "trace": traversals * hits * B_HIT_TRACE,
         "shade_forward": hits * B_HIT_FWD + rays * B_RAY_FWD,
         "shade_backward": hits * B_HIT_BWD + rays * B_RAY_BWD,
     }
@@ -294,6 +301,7 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     # profiled steps (per-kernel CUDA events + hit counts), outside the headline timing
     step.collect_stats = True
     step.hits = 0
+    step.fwd_passes = 0
     r.profile(True)
     time_steps(step, 1, world)
     kt = r.kernel_times()
@@ -301,10 +309,12 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     step.collect_stats = False
     hits = step.hits
     my_rays = sum(s.O.shape[0] for s in shards)
-    dom, per = kernel_roofline(kt, hits, my_rays, hbm)
+    traversals = kt.get("trace", (0.0, 0))[1] / max(step.fwd_passes, 1)  # 1.0 when the backward replays
+    dom, per = kernel_roofline(kt, hits, my_rays, hbm, traversals)
     step_bytes = hits * (2 * B_HIT_TRACE + B_HIT_FWD + B_HIT_BWD) + my_rays * (B_RAY_FWD + B_RAY_BWD)
     out = dict(workload=f"config {cfg} training step", ms_per_step=ms, value=total_rays / (ms * 1e-3) / 1e6,
                hits_per_ray=hits / max(my_rays, 1), hits=hits, kernels=per, dominant=dom, step_algo_bytes=step_bytes,
+               traversals_per_step=traversals,
                kernel_times={k: v for k, v in kt.items()}, grad_allreduce_bytes=step.grads.nbytes)
     # end to end: rays and target from pinned host memory every step, loss read back every step
     def e2e_step():
@@ -362,7 +372,9 @@ def main():
     dom = res["dominant"]
     d = per[dom]
     roof = {"bound": "hbm", "kernel": dom, "achieved": d["achieved_gbs"], "peak": hbm, "unit": "GB/s",
-            "frac": d["achieved_gbs"] / hbm, "traffic": None, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+            "frac": d["achieved_gbs"] / hbm,
+            "traffic": TRACE_DRAM_BYTES_PER_LAUNCH.get(main_cfg) if dom == "trace" else None,
+            "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
             if peak_kind == "measured" else "fallback 6.65 TB/s",
             "algo_bytes_per_launch": d["algo_bytes"] / max(d["launches"], 1),
             "avg_launch_ms": d["ms"] / max(d["launches"], 1)}

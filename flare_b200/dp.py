@@ -116,6 +116,7 @@ class TrainStep:
         self.loss = self.grads["loss"]  # summed by the same all-reduce as the gradients
         self.collect_stats = False
         self.hits = 0
+        self.fwd_passes = 0
 
     def geometry(self):
         sc = self.sc
@@ -138,7 +139,9 @@ class TrainStep:
             else:
                 r.Forward_training_base(*fargs)
             if self.collect_stats:
-                self.hits += r.stats()["hits_composited"]
+                st = r.stats()
+                self.hits += st["hits_composited"]
+                self.fwd_passes += st["passes"]
             img = b["bitmap"].clamp(0.0, 1.0)
             diff = img - sh.target
             self.loss += diff.abs().sum() * inv
