@@ -23,6 +23,7 @@ struct flare_renderer {
     unsigned *refit_flag = nullptr;
     float *bounds = nullptr;                    // 6 floats (scene centre bounds, ordered-int encoded)
     void *sort_tmp = nullptr;
+    void *ploc_scratch = nullptr;               // clustering build scratch (ploc.cu)
     size_t sort_tmp_bytes = 0;
 
     // ---- per-ray scratch, sized max_rays ----
@@ -99,6 +100,9 @@ struct GeomBufs {
 int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, const float *q, const float *opacity,
                         const float *kappa, int n, cudaStream_t st);
 size_t geometry_sort_temp_bytes(int n);
+size_t ploc_scratch_bytes(int n);
+int build_hierarchy_ploc(int n, const int *ids_sorted, const float *aabb, const float *frames, Node *nodes,
+                         float4 *rec, void *scratch, unsigned long long *h_total, cudaStream_t st);
 int launch_trace_geom(const Node *nodes, const float4 *rec, const int *ids_sorted, int n, const PolyConst &poly,
                       const float *O, const float *v, const float *t_min, int count, float *t_out, int *idx_out,
                       int *status, cudaStream_t st);

@@ -216,6 +216,185 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
 }
 
 
+// Per-lane k-buffer as a max-heap in shared memory ([slot][thread] layout: every lane reads its own
+// column, so accesses are bank-conflict free).  An accepted hit replaces the root (the current K-th
+// nearest) and sifts down about log2 K levels instead of shifting a sorted register array; the heap is
+// sorted once when the pass ends.  Frees the ~2K registers of the register buffer.
+template <int K>
+struct HeapBuf {
+    float *t;  // t[k * 128 + lane]
+    int *i;
+    float rt;  // root key (the current K-th nearest), cached
+    int ri;
+};
+
+__device__ __forceinline__ bool key_greater(float ta, int ia, float tb, int ib) {
+    return ta > tb || (ta == tb && ia > ib);
+}
+
+template <int K>
+__device__ __forceinline__ void heap_sift(HeapBuf<K> &h, int size, float t, int id) {
+    const int c = threadIdx.x;
+    int pos = 0;
+    while (true) {
+        const int l = 2 * pos + 1;
+        if (l >= size) break;
+        float tc = h.t[l * 128 + c];
+        int ic = h.i[l * 128 + c];
+        int ch = l;
+        if (l + 1 < size) {
+            const float tr = h.t[(l + 1) * 128 + c];
+            const int ir = h.i[(l + 1) * 128 + c];
+            if (key_greater(tr, ir, tc, ic)) {
+                tc = tr;
+                ic = ir;
+                ch = l + 1;
+            }
+        }
+        if (!key_greater(tc, ic, t, id)) break;
+        h.t[pos * 128 + c] = tc;
+        h.i[pos * 128 + c] = ic;
+        pos = ch;
+    }
+    h.t[pos * 128 + c] = t;
+    h.i[pos * 128 + c] = id;
+}
+
+template <int K>
+__device__ __forceinline__ void heap_insert(HeapBuf<K> &h, float t, int id) {
+    heap_sift(h, K, t, id);
+    h.rt = h.t[threadIdx.x];
+    h.ri = h.i[threadIdx.x];
+}
+
+template <bool STATS, int K>
+__global__ void __launch_bounds__(128) trace_heap_kernel(
+    const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
+    const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
+    const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats) {
+    __shared__ int s_node[4][TRACE_STACK];
+    __shared__ unsigned s_mask[4][TRACE_STACK];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = j < count;
+    unsigned long long nprim = 0, nnode = 0;
+    int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
+    float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+    float t_min = INFINITY;
+    if (live) {
+        O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
+        v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
+        t_min = tmin_[ray];
+    }
+    extern __shared__ __align__(16) unsigned char heap_smem[];
+    HeapBuf<K> kb;
+    kb.t = reinterpret_cast<float *>(heap_smem);
+    kb.i = reinterpret_cast<int *>(heap_smem + (size_t)K * 128 * sizeof(float));
+    for (int k = 0; k < K; ++k) {
+        kb.t[k * 128 + threadIdx.x] = INFINITY;
+        kb.i[k * 128 + threadIdx.x] = 0x7fffffff;
+    }
+    kb.rt = INFINITY;
+    kb.ri = 0x7fffffff;
+    const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
+                                  1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
+                                  1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
+    const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);
+    const bool want = live && t_min < INFINITY;
+    if (n == 1) {
+        float t;
+        if (want) {
+            ++nprim;
+            if (hit_prim(rec, 0, O, v, t_min, poly, t)) heap_insert(kb, t, ids[0]);
+        }
+    } else if (n > 1) {
+        unsigned mask = __ballot_sync(0xffffffffu, want);
+        int node = 0, sp = 0;
+        const unsigned long long max_visits = 2ull * (unsigned long long)n + 64ull;
+        while (mask) {
+            if (++nnode > max_visits) {
+                if (lane == 0) atomicOr(status, ERR_INDEX);
+                break;
+            }
+            const bool in = (mask >> lane) & 1u;
+            const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
+            const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
+            const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
+            const float thi = __fmaf_rn(fabsf(kb.rt), 1e-5f, kb.rt);
+            float t0 = 0.0f, t1 = 0.0f;
+            bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
+            bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
+            if (d.x < 0) {  // warp-uniform: leaf child 0
+                if (h0) {
+                    float t;
+                    ++nprim;
+                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, kb.rt)) {
+                        const int pid = __ldg(ids + ~d.x);
+                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                    }
+                }
+                h0 = false;
+            }
+            if (d.y < 0) {
+                if (h1) {
+                    float t;
+                    ++nprim;
+                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, kb.rt)) {
+                        const int pid = __ldg(ids + ~d.y);
+                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                    }
+                }
+                h1 = false;
+            }
+            const unsigned m0 = __ballot_sync(0xffffffffu, h0), m1 = __ballot_sync(0xffffffffu, h1);
+            if (m0 && m1) {
+                // nearer child first by lane vote (lanes that hit only one child vote for it)
+                const unsigned v0 = __ballot_sync(0xffffffffu, h0 && (!h1 || t0 <= t1));
+                const bool first0 = __popc(v0) * 2 >= __popc(m0 | m1);
+                if (sp < TRACE_STACK) {
+                    if (lane == 0) {
+                        s_node[wib][sp] = first0 ? d.y : d.x;
+                        s_mask[wib][sp] = first0 ? m1 : m0;
+                    }
+                    ++sp;
+                } else if (lane == 0) {
+                    atomicOr(status, ERR_STACK);
+                }
+                node = first0 ? d.x : d.y;
+                mask = first0 ? m0 : m1;
+                __syncwarp();
+                continue;
+            }
+            if (m0) { node = d.x; mask = m0; continue; }
+            if (m1) { node = d.y; mask = m1; continue; }
+            __syncwarp();
+            if (sp == 0) break;
+            --sp;
+            node = s_node[wib][sp];
+            mask = s_mask[wib][sp];
+        }
+    }
+    if (live) {  // heap sort: the largest key leaves first, into the last slot
+        for (int k = K - 1; k >= 0; --k) {
+            const float tk = kb.t[threadIdx.x];
+            const int ik = kb.i[threadIdx.x];
+            const bool valid = ik != 0x7fffffff;
+            t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
+            idx_out[(size_t)k * stride + j] = valid ? ik : -1;
+            if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
+        }
+    }
+    if (STATS) {
+        for (int o = 16; o > 0; o >>= 1) nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
+        if (lane == 0 && (nprim | nnode)) {
+            atomicAdd(stats + ST_PRIM_TESTS, nprim);
+            atomicAdd(stats + ST_NODES, nnode);
+        }
+    }
+}
+
+
 // Group-per-ray traversal for sparse late passes: once few rays remain, a pass lasts as long as its
 // longest single walk, so G lanes (a quarter, half or whole warp) split one ray's walk.  Each step the
 // group pops up to G nodes of its shared stack, tests their children and pushes the entered internal
@@ -522,6 +701,19 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
             trace_group_kernel<K_PASS, 8><<<(count + 15) / 16, B, 0, st>>>(
                 O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
                 r->dstatus, r->dstats);
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    }
+    // Internal passes keep each ray's K_PASS-entry buffer as a shared-memory heap (FLARE_TRACE_HEAP=0: the
+    // sorted register buffer of the packet kernel).
+    static const bool heap = getenv_int("FLARE_TRACE_HEAP", 1) != 0;
+    if (k == K_PASS && K_PASS != K_HITS && heap) {
+        const size_t smem = (size_t)K_PASS * 128 * 8;
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap_kernel<true, K_PASS>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        trace_heap_kernel<true, K_PASS><<<(count + B - 1) / B, B, smem, st>>>(
+            O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+            r->dstatus, r->dstats);
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
     }

@@ -359,3 +359,34 @@ def test_backward_replay_equals_retrace(case_dense):
         outs.append({**G, "w1": W[4]})
     for k in outs[0]:
         assert grad_oracle.rel_l2(outs[0][k].cpu().numpy(), outs[1][k].cpu().numpy()) < 1e-5, k
+
+
+def test_clustering_hierarchy_hits_bit_exact():
+    """The alternative hierarchy builder (FLARE_BVH=ploc, read once per process) gives the same hit lists."""
+    import subprocess
+    import sys
+    code = r"""
+import numpy as np, torch
+from flare_b200.renderer import CPyOptiXFLARERenderer
+from flare_b200.scene import camera_rays, make_scene
+from oracle import oracle
+sc = make_scene(20000, 3)
+O, v = camera_rays(48, 48, 60.0, eye=(0.0, 0.0, 3.0))
+R = O.shape[0]
+r = CPyOptiXFLARERenderer(8, 11.3449, R)
+g = sc.to("cuda")
+r.SetGeometry(*[t.contiguous() for t in g.activated()])
+frames = r.frames().cpu().numpy()
+tmin = np.zeros(R, np.float32)
+for p in range(3):
+    t, idx = r.Render(O.cuda(), v.cuda(), torch.from_numpy(tmin).cuda(), R)
+    to, io = oracle.hits(frames, O, v, tmin)
+    assert np.array_equal(idx.cpu().numpy(), io) and np.array_equal(t.cpu().numpy(), to), p
+    full = io[15] >= 0
+    tmin = np.where(full, np.nextafter(to[15], np.float32(np.inf), dtype=np.float32), np.float32(np.inf))
+print("OK")
+"""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, FLARE_BVH="ploc", PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0 and "OK" in out.stdout, out.stdout[-2000:] + out.stderr[-2000:]
