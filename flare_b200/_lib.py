@@ -42,6 +42,17 @@ class BackwardArgs(ctypes.Structure):
                 ("lambda_normal", ctypes.c_float)]
 
 
+class ViewerArgs(ctypes.Structure):
+    _fields_ = [("O", vp), ("v", vp), ("bitmap", vp), ("n_rays", ctypes.c_int), ("bg", ctypes.c_float * 3),
+                ("T_threshold", ctypes.c_float), ("spheres", vp), ("materials", vp), ("n_spheres", ctypes.c_int),
+                ("lights", vp), ("n_lights", ctypes.c_int), ("epsilon", ctypes.c_float),
+                ("shadow_multiplier", ctypes.c_float), ("ambient", ctypes.c_float * 3),
+                ("max_recursion_depth", ctypes.c_int)]
+
+
+VIEWER_MAX_SPHERES, VIEWER_MAX_LIGHTS = 16, 8
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("rays", ctypes.c_longlong), ("passes", ctypes.c_longlong), ("hits_composited", ctypes.c_longlong),
                 ("prim_tests", ctypes.c_longlong), ("node_visits", ctypes.c_longlong)]
@@ -65,6 +76,7 @@ EXPORTS = {
                                            vp]),
     "flare_forward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(ForwardArgs), vp]),
     "flare_backward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(BackwardArgs), vp]),
+    "flare_viewer_forward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(ViewerArgs), vp]),
     "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
     "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
     "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),

@@ -191,7 +191,7 @@ int flare_destroy(flare_renderer *r) {
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
-                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->pgrad, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->pgrad, r->vw_buf, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (r->h_count) cudaFreeHost(r->h_count);
@@ -284,6 +284,25 @@ int flare_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_
     e = run_forward(r, sc, a, S(stream));
     if (e) return e;
     return check_status(r, S(stream), "flare_forward");
+}
+
+int flare_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r && a, "flare_viewer_forward: NULL argument");
+    int e = check_scene(r, sc, "flare_viewer_forward");
+    if (e) return e;
+    CHECK_ARG(a->n_rays >= 0 && a->n_rays <= r->max_rays, "flare_viewer_forward: n_rays %d exceeds max_batch_size %d",
+              a->n_rays, r->max_rays);
+    if (a->n_rays == 0) return FLARE_OK;
+    CHECK_ARG(a->O && a->v && a->bitmap, "flare_viewer_forward: NULL rays / bitmap");
+    CHECK_ARG((a->n_spheres == 0 || (a->spheres && a->materials)) && (a->n_lights == 0 || a->lights),
+              "flare_viewer_forward: NULL sphere / material / light table");
+    DeviceGuard dg(r->device);
+    FLARE_CUDA_TRY(cudaMemsetAsync(r->dstats, 0, ST_NSTATS * sizeof(unsigned long long), S(stream)));
+    r->last_stream = S(stream);
+    e = run_viewer_forward(r, sc, a, S(stream));
+    if (e) return e;
+    return check_status(r, S(stream), "flare_viewer_forward");
 }
 
 int flare_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, void *stream) {

@@ -26,6 +26,10 @@ constexpr int LUT_PRIV_FLOATS = 26368;  // 4 * 13154 / 2 = 26308, rounded up to 
 constexpr int PGRAD_FLOATS = 16;
 constexpr float LUT_SCALE = 0.29689279887990428378374198030042f;  // 1/sqrt(11.3449)
 
+// Internal forward mode of the secondary-ray (viewer) path: colour of a shadowed hit times the shadow
+// multiplier, no background at the end of a pass (added when the ray generation ends).
+constexpr int FWD_VIEWER = 100;
+
 // Device status word bits (first word of renderer->dstatus).
 enum : int {
     ERR_STACK = 1,     // traversal stack overflow (hits may be incomplete)

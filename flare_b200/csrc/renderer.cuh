@@ -49,6 +49,9 @@ struct flare_renderer {
     float *dfeat_priv = nullptr;  // per-CTA LUT gradient copies (2 * num_sms * LUT_PRIV_FLOATS floats)
     float *pgrad = nullptr;       // packed per-primitive gradients of the decoder backward (PGRAD_FLOATS each)
     size_t pgrad_cap = 0;         // primitives pgrad holds
+    void *vw_buf = nullptr;       // secondary-ray path: ray sets and per-generation scratch (viewer.cu)
+    int vw_sets = 0;
+    long long vw_generations = 0; // ray generations of the last flare_viewer_forward
 
     // ---- hit cache: the passes of the last Forward_training, replayed by a matching Backward ----
     unsigned long long geom_version = 0;  // bumped by every flare_set_geometry
@@ -113,7 +116,8 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
 // trace.cu: traces `count` rays.  Ray j is ray_ids[j] (or j when ray_ids is null); t_min is indexed by
 // ray id; outputs (16, out_stride) slot-major at column j.
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
-                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k = K_HITS);
+                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k = K_HITS,
+                 const float *t_max = nullptr);  // t_max: optional per-ray bound, hits at t >= t_max[ray] excluded
 
 // trace.cu: writes the coherence order of R rays into list_out
 int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st);
@@ -124,6 +128,7 @@ size_t select_temp_bytes(int max_rays);
 // shade.cu
 int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st);
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
+int run_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, cudaStream_t st);
 int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
                  const void *A3, const float *b3, float *Y, cudaStream_t st);
 

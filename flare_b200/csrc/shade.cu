@@ -104,6 +104,8 @@ struct FwdOut {
     float *bitmap, *dacc, *nacc, *normal, *alpha, *edn, *med;
     const float *surface_normal;
     float reg_a, reg_b;
+    const unsigned char *shadow;  // FWD_VIEWER: per hit slot (slot-major like the hit lists), lit = 0
+    float shadow_mult;
 };
 
 struct BwdIO {
@@ -554,6 +556,11 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                     c1 *= fmaxf(y4[1], 0.0f);
                     c2 *= fmaxf(y4[2], 0.0f);
                 }
+                if (MODE == FWD_VIEWER && fo.shadow[(size_t)h * pp.count + slot]) {
+                    c0 *= fo.shadow_mult;
+                    c1 *= fo.shadow_mult;
+                    c2 *= fo.shadow_mult;
+                }
                 if (MODE == FLARE_FWD_PCA && sc.override_colors) {
                     c0 = sc.override_colors[3 * (size_t)ind];
                     c1 = sc.override_colors[3 * (size_t)ind + 1];
@@ -588,7 +595,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
             if (have) {
                 if (MODE != FLARE_FWD_MEDIAN) {
-                    if (!active) {
+                    if (!active && MODE != FWD_VIEWER) {
                         rgb[0] = __fmaf_rn(pp.bg0, T, rgb[0]);
                         rgb[1] = __fmaf_rn(pp.bg1, T, rgb[1]);
                         rgb[2] = __fmaf_rn(pp.bg2, T, rgb[2]);
@@ -1355,6 +1362,13 @@ static int launch_fwd_mode(flare_renderer *r, int mode, const SceneP &sp, const 
     return FLARE_E_INVALID;
 }
 
+// One pass of the secondary-ray path: decode + composite the hit lists of `count` rays (list `lin`)
+// into bitmap, with shadowed hits darkened; per-ray T and t_min are the generation's own arrays.  The
+// per-slot still-active flags land in r->pass_flags for the compaction.
+int launch_shade_viewer(flare_renderer *r, const flare_scene *sc, const float *O, const float *v, const int *lin,
+                        int count, const float *ht, const int *hi, const unsigned char *shadow, float shadow_mult,
+                        float *T, float *t_min, float *bitmap, float T_thr, cudaStream_t st);
+
 // ------------------------------------------------------------------------------------------------
 // Hit cache.  A Backward re-walks exactly the passes of the Forward_training that produced its image
 // (same rays, geometry and parameters give the same active rays and the same 16-hit lists per pass), so
@@ -1744,6 +1758,26 @@ int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const
     selftest_mlp_kernel<<<grid, 128, SM_FWD_BYTES, st>>>(reinterpret_cast<const uint4 *>(X), rows, sp, Y, status);
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
+}
+
+// One pass of the secondary-ray path (declared above the hit cache).
+int launch_shade_viewer(flare_renderer *r, const flare_scene *sc, const float *O, const float *v, const int *lin,
+                        int count, const float *ht, const int *hi, const unsigned char *shadow, float shadow_mult,
+                        float *T, float *t_min, float *bitmap, float T_thr, cudaStream_t st) {
+    if (count <= 0) return FLARE_OK;
+    SceneP sp = scene_params(sc, nullptr);
+    PassP pp = make_pass(r, O, v, 0.0f, 0.0f, 0.0f, T_thr);
+    pp.T = T;
+    pp.t_min = t_min;
+    pp.list_in = lin;
+    pp.count = count;
+    pp.hit_t = ht;
+    pp.hit_idx = hi;
+    FwdOut fo{};
+    fo.bitmap = bitmap;
+    fo.shadow = shadow;
+    fo.shadow_mult = shadow_mult;
+    return sc->cond ? launch_fwd<true, FWD_VIEWER>(r, sp, pp, fo, st) : launch_fwd<false, FWD_VIEWER>(r, sp, pp, fo, st);
 }
 
 }  // namespace flare

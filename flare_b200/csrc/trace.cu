@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
     const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
-    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats) {
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
+    const float *__restrict__ tmax_ = nullptr) {
     __shared__ int s_node[4][TRACE_STACK];
     __shared__ unsigned s_mask[4][TRACE_STACK];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
@@ -106,11 +107,12 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
     unsigned long long nprim = 0, nnode = 0;
     int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
     float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
-    float t_min = INFINITY;
+    float t_min = INFINITY, tcap = INFINITY;
     if (live) {
         O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
         v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
         t_min = tmin_[ray];
+        if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
     }
     KBuf<K> kb;
 #pragma unroll
@@ -127,7 +129,7 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
         float t;
         if (want) {
             ++nprim;
-            if (hit_prim(rec, 0, O, v, t_min, poly, t)) kbuf_insert(kb, t, ids[0]);
+            if (hit_prim(rec, 0, O, v, t_min, poly, t, tcap)) kbuf_insert(kb, t, ids[0]);
         }
     } else if (n > 1) {
         unsigned mask = __ballot_sync(0xffffffffu, want);
@@ -142,7 +144,8 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
             const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
             const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
             const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
-            const float thi = __fmaf_rn(fabsf(kb.t[K - 1]), 1e-5f, kb.t[K - 1]);
+            const float bk = fminf(kb.t[K - 1], tcap);
+            const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
             float t0 = 0.0f, t1 = 0.0f;
             bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
             bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
                 if (h0) {
                     float t;
                     ++nprim;
-                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, kb.t[K - 1])) {
+                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
                         const int pid = __ldg(ids + ~d.x);
                         if (t < kb.t[K - 1] || (t == kb.t[K - 1] && pid < kb.i[K - 1]))
                             kbuf_insert(kb, t, pid);
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
                 if (h1) {
                     float t;
                     ++nprim;
-                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, kb.t[K - 1])) {
+                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
                         const int pid = __ldg(ids + ~d.y);
                         if (t < kb.t[K - 1] || (t == kb.t[K - 1] && pid < kb.i[K - 1]))
                             kbuf_insert(kb, t, pid);
@@ -272,7 +275,8 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
     const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
-    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats) {
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
+    const float *__restrict__ tmax_ = nullptr) {
     __shared__ int s_node[4][TRACE_STACK];
     __shared__ unsigned s_mask[4][TRACE_STACK];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
@@ -281,11 +285,12 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
     unsigned long long nprim = 0, nnode = 0;
     int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
     float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
-    float t_min = INFINITY;
+    float t_min = INFINITY, tcap = INFINITY;
     if (live) {
         O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
         v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
         t_min = tmin_[ray];
+        if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
     }
     extern __shared__ __align__(16) unsigned char heap_smem[];
     HeapBuf<K> kb;
@@ -306,7 +311,7 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
         float t;
         if (want) {
             ++nprim;
-            if (hit_prim(rec, 0, O, v, t_min, poly, t)) heap_insert(kb, t, ids[0]);
+            if (hit_prim(rec, 0, O, v, t_min, poly, t, tcap)) heap_insert(kb, t, ids[0]);
         }
     } else if (n > 1) {
         unsigned mask = __ballot_sync(0xffffffffu, want);
@@ -321,7 +326,8 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
             const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
             const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
             const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
-            const float thi = __fmaf_rn(fabsf(kb.rt), 1e-5f, kb.rt);
+            const float bk = fminf(kb.rt, tcap);
+            const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
             float t0 = 0.0f, t1 = 0.0f;
             bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
             bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
@@ -329,7 +335,7 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
                 if (h0) {
                     float t;
                     ++nprim;
-                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, kb.rt)) {
+                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
                         const int pid = __ldg(ids + ~d.x);
                         if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
                     }
@@ -340,7 +346,7 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
                 if (h1) {
                     float t;
                     ++nprim;
-                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, kb.rt)) {
+                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
                         const int pid = __ldg(ids + ~d.y);
                         if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
                     }
@@ -412,7 +418,8 @@ __global__ void __launch_bounds__(128) trace_group_kernel(
     const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
-    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats) {
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
+    const float *__restrict__ tmax_ = nullptr) {
     static_assert(G == 8 || G == 16 || G == 32, "group of 8, 16 or 32 lanes");
     constexpr int CAP = WIDE_WARP_STACK * G / 32;
     __shared__ int s_stack[4][WIDE_WARP_STACK];
@@ -424,11 +431,12 @@ __global__ void __launch_bounds__(128) trace_group_kernel(
     const unsigned lt_mask = (1u << gl) - 1u;
     const int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
     float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
-    float t_min = INFINITY;
+    float t_min = INFINITY, tcap = INFINITY;
     if (live) {
         O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
         v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
         t_min = tmin_[ray];
+        if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
     }
     unsigned long long nprim = 0, nnode = 0;
     KBuf<K> kb;
@@ -445,7 +453,7 @@ __global__ void __launch_bounds__(128) trace_group_kernel(
         float t;
         if (gl == 0 && t_min < INFINITY) {
             ++nprim;
-            if (hit_prim(rec, 0, O, v, t_min, poly, t)) kbuf_insert(kb, t, ids[0]);
+            if (hit_prim(rec, 0, O, v, t_min, poly, t, tcap)) kbuf_insert(kb, t, ids[0]);
         }
     } else if (n > 1) {
         int *stack = s_stack[wib] + gid * CAP;
@@ -463,7 +471,7 @@ __global__ void __launch_bounds__(128) trace_group_kernel(
             const int take = min(G, sp);
             const int node = gl < take ? stack[sp - 1 - gl] : -1;
             sp -= take;
-            float bound = kb.t[K - 1];
+            float bound = fminf(kb.t[K - 1], tcap);
 #pragma unroll
             for (int o = G / 2; o > 0; o >>= 1) bound = fminf(bound, __shfl_xor_sync(0xffffffffu, bound, o));
             bool push_near = false, push_far = false;
@@ -681,7 +689,8 @@ static int getenv_int(const char *name, int dflt) {
 }
 
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
-                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k) {
+                 int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k,
+                 const float *t_max) {
     if (count <= 0) return FLARE_OK;
     const int B = 128;
     // Sparse passes: G lanes per ray, G chosen so the pass still spreads over the whole GPU
@@ -692,15 +701,15 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
         if (count <= g32_max)
             trace_group_kernel<K_PASS, 32><<<(count + 3) / 4, B, 0, st>>>(
                 O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
-                r->dstatus, r->dstats);
+                r->dstatus, r->dstats, t_max);
         else if (count <= g16_max)
             trace_group_kernel<K_PASS, 16><<<(count + 7) / 8, B, 0, st>>>(
                 O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
-                r->dstatus, r->dstats);
+                r->dstatus, r->dstats, t_max);
         else
             trace_group_kernel<K_PASS, 8><<<(count + 15) / 16, B, 0, st>>>(
                 O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
-                r->dstatus, r->dstats);
+                r->dstatus, r->dstats, t_max);
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
     }
@@ -713,7 +722,7 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         trace_heap_kernel<true, K_PASS><<<(count + B - 1) / B, B, smem, st>>>(
             O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
-            r->dstatus, r->dstats);
+            r->dstatus, r->dstats, t_max);
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
     }
@@ -721,13 +730,13 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
         trace_packet_kernel<true, K_PASS><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes,
                                                                              r->rec, r->ids_sorted, r->n, t_out,
                                                                              idx_out, out_stride, r->poly, r->dstatus,
-                                                                             r->dstats);
+                                                                             r->dstats, t_max);
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
     }
     trace_packet_kernel<true, K_HITS><<<(count + B - 1) / B, B, 0, st>>>(O, v, t_min, ray_ids, count, r->nodes, r->rec,
                                                            r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
-                                                           r->dstatus, r->dstats);
+                                                           r->dstatus, r->dstats, t_max);
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
 }

@@ -162,6 +162,37 @@ typedef struct flare_backward_args {
  */
 int flare_backward(flare_renderer *r, const flare_scene *scene, const flare_backward_args *a, void *stream);
 
+/*
+ * Secondary rays (replaces CPyOptiXFLAREVIEWERRenderer::Forward, source/viewer_renderer/
+ * CPyOptiXFLAREVIEWERRenderer.cpp -> *_CUDA_Forward.cu:912-1276 and shaders.cu, with analytic spheres
+ * standing in for its triangle-mesh instances).  Per ray generation: k-nearest passes over the
+ * primitives up to the nearest sphere, shadow tests of every buffered hit towards each directional
+ * light, compositing with shadowed colours times shadow_multiplier; then each ray that reached a sphere
+ * with T >= T_threshold is shaded there (Fresnel, refraction / total internal reflection, ambient,
+ * diffuse and specular) and splits: the child with more transmittance continues, the other is pushed;
+ * max_recursion_depth bounds the pushes like the reference's stack.  Rays reaching no sphere add
+ * bg * T.  scene->RGBA = [RGB | A]: the viewer's RGB (N,3) colours and A (N) opacity logits.
+ */
+#define FLARE_VIEWER_MAX_SPHERES 16
+#define FLARE_VIEWER_MAX_LIGHTS 8
+typedef struct flare_viewer_args {
+    const float *O, *v;          /* (R,3) primary rays, directions normalised (device) */
+    float *bitmap;               /* (R,3) accumulated (device, caller-zeroed) */
+    int n_rays;
+    float bg[3];
+    float T_threshold;
+    const float *spheres;        /* HOST (S,4): centre xyz, radius */
+    const float *materials;      /* HOST (S,6): Id rgb, kd, eta, n -- the reference's material rows */
+    int n_spheres;
+    const float *lights;         /* HOST (L,6): Is rgb, direction L (light travels along L) */
+    int n_lights;
+    float epsilon;               /* t_min of secondary and shadow rays */
+    float shadow_multiplier;
+    float ambient[3];            /* Ia */
+    int max_recursion_depth;
+} flare_viewer_args;
+int flare_viewer_forward(flare_renderer *r, const flare_scene *scene, const flare_viewer_args *a, void *stream);
+
 /* Statistics of the last forward/backward call (counted on the device; reading them synchronises the
    stream of that call): rays, passes, composited hits, primitive tests, BVH node visits. */
 typedef struct flare_stats {

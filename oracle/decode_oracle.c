@@ -272,3 +272,73 @@ long oracle_shade_csr(const float *m, const float *s, const float *q, const floa
 void oracle_lut(const float *features, const float *cu, const float *cw, int n, float *out) {
     for (int i = 0; i < n; ++i) lut_encode(features, cu[i], cw[i], out + 8 * i);
 }
+
+/*
+ * Secondary-ray compositing (viewer path, CPyOptiXFLAREVIEWERRenderer_CUDA_Forward.cu:695-897): the
+ * hits of ray ray[j] are hit_t / hit_idx [off[j], off[j+1]) ascending; a shadowed hit (flag != 0)
+ * contributes its colour times shadow_mult; no background.  T (by ray id) and rgb (R,3, by ray id) are
+ * read and updated.  RGBA = [RGB | A logit].  Returns the number of composited hits.
+ */
+long oracle_viewer_composite(const float *m, const float *s, const float *q, const float *RGBA, const float *k,
+                             const void *cond, const float *features, const void *A1, const float *b1, const void *A2,
+                             const float *b2, const void *A3, const float *b3, float T_thr, float shadow_mult,
+                             const float *O, const float *v, const int *ray, int n, const long *off,
+                             const float *hit_t, const int *hit_idx, const unsigned char *shadow, float *T_io,
+                             float *rgb_io) {
+    oscene S = {m, s, q, RGBA, k, (const _Float16 *)cond, features, (const _Float16 *)A1, (const _Float16 *)A2,
+                (const _Float16 *)A3, b1, b2, b3, NULL};
+    long total = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : total)
+    for (int j = 0; j < n; ++j) {
+        int r = ray[j];
+        float T = T_io[r];
+        float rgb[3] = {rgb_io[3 * (long)r], rgb_io[3 * (long)r + 1], rgb_io[3 * (long)r + 2]};
+        const float *o = O + 3 * (long)r, *d = v + 3 * (long)r;
+        for (long h = off[j]; h < off[j + 1]; ++h) {
+            int idx = hit_idx[h];
+            if (idx < 0 || !(T >= T_thr)) break;
+            float t = hit_t[h];
+            const float *qq = S.q + 4 * (long)idx;
+            float sx = expf(-S.s[2 * (long)idx]), sy = expf(-S.s[2 * (long)idx + 1]);
+            float aa = qq[0] * qq[0], bb = qq[1] * qq[1], cc = qq[2] * qq[2], dd = qq[3] * qq[3];
+            float Sq = 2.0f / (aa + bb + cc + dd);
+            float bs = qq[1] * Sq, cs = qq[2] * Sq, ds = qq[3] * Sq;
+            float ab = qq[0] * bs, ac = qq[0] * cs, ad = qq[0] * ds;
+            bb = bb * Sq;
+            float bc = qq[1] * cs, bd = qq[1] * ds;
+            cc = cc * Sq;
+            float cd = qq[2] * ds;
+            dd = dd * Sq;
+            float Q11 = sx * (1.0f - cc - dd), Q12 = sx * (bc + ad), Q13 = sx * (bd - ac);
+            float Q21 = sy * (bc - ad), Q22 = sy * (1.0f - bb - dd), Q23 = sy * (cd + ab);
+            float kap = 1.0f + logf(1.0f + expf(S.k[idx]));
+            float kinv = 1.0f / kap;
+            const float *mm = S.m + 3 * (long)idx;
+            float dx = fmaf(d[0], t, o[0]) - mm[0], dy = fmaf(d[1], t, o[1]) - mm[1], dz = fmaf(d[2], t, o[2]) - mm[2];
+            float u = fmaf(Q11, dx, fmaf(Q12, dy, Q13 * dz));
+            float w = fmaf(Q21, dx, fmaf(Q22, dy, Q23 * dz));
+            const float *rgba = S.RGBA + 4 * (long)idx;
+            float sig_y = 1.0f, crgb[3] = {rgba[0], rgba[1], rgba[2]};
+            if (S.cond) {
+                float y[4];
+                decode(&S, idx, u * LUT_SCALE, w * LUT_SCALE, d, y);
+                sig_y = 1.0f / (1.0f + expf(-y[3]));
+                for (int c = 0; c < 3; ++c) crgb[c] = rgba[c] * (y[c] > 0.0f ? y[c] : 0.0f);
+            }
+            if (shadow[h])
+                for (int c = 0; c < 3; ++c) crgb[c] *= shadow_mult;
+            float opa1 = 1.0f / (1.0f + expf(-rgba[3]));
+            float r2 = fmaf(u, u, w * w);
+            float pk = powf(r2, kap - 1.0f);
+            if (isnan(pk)) pk = 0.0f;
+            float alpha = opa1 * expf(-0.5f * kinv * (r2 * pk)) * sig_y;
+            float oo = T * alpha;
+            for (int c = 0; c < 3; ++c) rgb[c] = fmaf(crgb[c], oo, rgb[c]);
+            T = T - oo;
+            ++total;
+        }
+        T_io[r] = T;
+        for (int c = 0; c < 3; ++c) rgb_io[3 * (long)r + c] = rgb[c];
+    }
+    return total;
+}

@@ -175,3 +175,28 @@ void oracle_hits(const float *frames, int n, const float *O, const float *v, con
 
 /* Next-pass restart value used by the multi-pass driver (Forward_training.cu:929). */
 float oracle_next_tmin(float t16) { return nextafterf(t16, INFINITY); }
+
+/* As oracle_hits, with each ray's hits restricted to t < t_max[r] (the viewer path's nearest sphere). */
+void oracle_hits_tmax(const float *frames, int n, const float *O, const float *v, const float *t_min,
+                      const float *t_max, int R, int nsides, float *t_out, int *idx_out) {
+    float pc[64], ps[64];
+    oracle_polygon_constants(nsides, pc, ps);
+#pragma omp parallel for schedule(dynamic, 16)
+    for (int r = 0; r < R; ++r) {
+        float tb[K_HITS];
+        int ib[K_HITS];
+        for (int k = 0; k < K_HITS; ++k) { tb[k] = INFINITY; ib[k] = 0x7fffffff; }
+        const float *o = O + 3 * r, *d = v + 3 * r;
+        for (int i = 0; i < n; ++i) {
+            float t;
+            if (!hit_test(frames + 12 * (long)i, o, d, t_min[r], nsides, pc, ps, &t)) continue;
+            if (!(t < t_max[r])) continue;
+            kbuf_push(tb, ib, t, i);
+        }
+        for (int k = 0; k < K_HITS; ++k) {
+            int valid = ib[k] != 0x7fffffff;
+            t_out[(long)k * R + r] = valid ? tb[k] : INFINITY;
+            idx_out[(long)k * R + r] = valid ? ib[k] : -1;
+        }
+    }
+}
