@@ -37,6 +37,8 @@ CONFIGS = {
     1: dict(n_prims=1_000_000, width=800, height=800, views=1, mode="forward"),
     2: dict(n_prims=3_000_000, width=1600, height=1064, views=1, mode="train"),
     3: dict(n_prims=6_000_000, width=1920, height=1080, views=8, mode="train"),
+    # secondary rays: 1M primitives + a mirror and two glass spheres, recursion depth 3, forward only
+    4: dict(n_prims=1_000_000, width=1024, height=1024, views=1, mode="viewer", depth=3),
 }
 METRIC = "Mrays/s fwd and fwd+bwd at 1/2/4/8 B200; % of traversal/MLP roofline"
 # algorithmic bytes per composited hit / per ray and FLOPs per hit (roofline model of the path)
@@ -266,10 +268,44 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def measure_viewer(cfg, scene, sh, steps, warmup, device, world):
+    """Config 4: the secondary-ray forward (reflection, refraction, shadows) of one view."""
+    from flare_b200.scene import viewer_lights, viewer_spheres
+    from flare_b200.viewer import CPyFlareViewerRenderer
+    c = CONFIGS[cfg]
+    R = sh.O.shape[0]
+    r = CPyFlareViewerRenderer(8, 11.3449, R, c["depth"])
+    spheres, materials = viewer_spheres()
+    r.SetGeometry(scene.m, torch.exp(scene.s), scene.q, torch.sigmoid(scene.RGBA[:, 3]).contiguous(),
+                  (1.0 + torch.nn.functional.softplus(scene.k[:, 0])).contiguous(), spheres)
+    RGB, A = scene.RGBA[:, :3].contiguous(), scene.RGBA[:, 3].contiguous()
+    dec = (scene.cond, scene.features, RGB, scene.A1, scene.b1, scene.A2, scene.b2, scene.A3, scene.b3)
+    bitmap = torch.zeros(R, 3, device=device)
+    lights = viewer_lights()
+
+    def fwd():
+        bitmap.zero_()
+        r.Forward(*dec, sh.O, sh.v, bitmap, 0.0, 0.0, 0.0, scene.m, scene.s, scene.q, A, scene.k, 0.01, materials,
+                  lights, 1e-4, 0.55, 0.06, 0.06, 0.07)
+    for _ in range(warmup):
+        fwd()
+    ms = time_steps(fwd, steps, world) / steps
+    r.profile(True)
+    fwd()
+    torch.cuda.synchronize()
+    kt = r.kernel_times()
+    r.profile(False)
+    return dict(workload=f"config {cfg} secondary-ray forward (depth {c['depth']}, 3 spheres)", ms_per_step=ms,
+                value=R / (ms * 1e-3) / 1e6, traversal_passes=r.stats()["passes"],
+                kernels={k: dict(ms=v[0], launches=v[1]) for k, v in kt.items() if v[1]})
+
+
 def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     from flare_b200.dp import TrainStep
     from flare_b200.renderer import CPyOptiXFLARERenderer
     scene, shards, host, total_rays = build_workload(cfg, world, rank, device)
+    if CONFIGS[cfg]["mode"] == "viewer":
+        return measure_viewer(cfg, scene, shards[0], steps, warmup, device, world)
     max_rays = max(s.O.shape[0] for s in shards)
     r = CPyOptiXFLARERenderer(8, 11.3449, max_rays)
     out = {}
@@ -360,11 +396,12 @@ def main():
     clocks = cs.summary()
     extras = {}
     if world == 1 and not args.no_extra:
-        for c in ([2] if main_cfg == 3 else []) + [1]:
+        for c in ([2] if main_cfg == 3 else []) + [1, 4]:
             e = measure_config(c, 1, 0, max(2, args.steps), 2, device, hbm)
             e.pop("_r", None)
             extras[f"config{c}"] = {k: v for k, v in e.items() if k in ("workload", "ms_per_step", "value",
-                                                                          "hits_per_ray", "dominant", "kernels")}
+                                                                          "hits_per_ray", "dominant", "kernels",
+                                                                          "traversal_passes")}
     if rank != 0:
         dist.destroy_process_group()
         return

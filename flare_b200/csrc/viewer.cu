@@ -392,20 +392,25 @@ int run_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_vie
                     set_error("flare_viewer_forward: pass loop did not terminate");
                     return FLARE_E_DEVICE;
                 }
+                int slot = prof_begin(r, PK_TRACE, st);
                 e = launch_trace(r, cur->O, cur->v, cur->tmin, r->list[c], count, r->hit_t, r->hit_idx, count, st,
                                  K_PASS, t_sph);
+                prof_end(r, slot, st);
                 if (e) return e;
                 const size_t nh = (size_t)count * K_PASS;
                 shadow_flags_kernel<<<(unsigned)((nh + B - 1) / B), B, 0, st>>>(vc, r->list[c], count, K_PASS, cur->O,
                                                                                 cur->v, r->hit_t, r->hit_idx, shadow);
                 FLARE_CUDA_TRY(cudaGetLastError());
+                slot = prof_begin(r, PK_SHADE_FWD, st);
                 e = launch_shade_viewer(r, sc, cur->O, cur->v, r->list[c], count, r->hit_t, r->hit_idx, shadow,
                                         vc.shadow_mult, cur->T, cur->tmin, a->bitmap, vc.T_thr, st);
+                prof_end(r, slot, st);
                 if (e) return e;
                 e = compact_active(r, r->list[c], count, r->list[c ^ 1], st);
                 if (e) return e;
                 e = count_of(&count);
                 if (e) return e;
+                prof_collect(r);
                 c ^= 1;
             }
         }

@@ -121,3 +121,24 @@ def camera_rays(width: int, height: int, fov_x_deg: float = 60.0, eye=(0.0, 0.0,
     v = v / v.norm(dim=1, keepdim=True)
     O = O.double().expand_as(v)
     return O.float().contiguous().to(device), v.float().contiguous().to(device)
+
+
+def viewer_spheres():
+    """Config-4 stand-in for the reference viewer's meshes: a mirror and two glass spheres (IOR 1.5)
+    between the default camera (0, 0, 3) and the primitive cube, so that the refracted and reflected rays
+    travel into the primitives.  Returns (spheres (3,4) centre + radius, materials (3,6)); material rows
+    are the reference viewer's (Id rgb, kd, eta, n), the mirror an extreme-IOR dielectric (R0 -> 1, the
+    refracted child carries no transmittance)."""
+    spheres = torch.tensor([[-0.55, 0.0, 1.5, 0.35], [0.5, 0.1, 1.45, 0.32], [0.0, 0.55, 1.3, 0.25]])
+    materials = torch.tensor([[0.9, 0.9, 0.9, 0.0, 1.0e6, 64.0],
+                              [0.75, 0.88, 1.0, 0.03, 1.5, 64.0],
+                              [0.95, 0.8, 0.7, 0.03, 1.5, 64.0]])
+    return spheres, materials
+
+
+def viewer_lights():
+    """One white directional light along normalised (1, 1, 1) (the reference viewer's default,
+    source/viewer.py:72-76,194-196): rows (Is rgb, direction)."""
+    d = torch.tensor([1.0, 1.0, 1.0])
+    d = d / d.norm()
+    return torch.cat([torch.ones(3), d]).reshape(1, 6)

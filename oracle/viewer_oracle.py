@@ -150,21 +150,15 @@ def viewer_forward(frames, scene, spheres, materials, lights, O, v, bg=(0.0, 0.0
 
 
 def default_spheres():
-    """Config-4 stand-in for the reference viewer's meshes: a mirror and two glass spheres (IOR 1.5)
-    inside the primitive cloud.  Returns (spheres (3,4), materials (3,6)); material rows are the
-    reference's (Id rgb, kd, eta, n), the mirror as an extreme-IOR dielectric (R0 -> 1, no refraction
-    carries transmittance)."""
-    spheres = np.array([[-0.45, 0.0, 0.0, 0.35], [0.45, 0.05, 0.1, 0.3], [0.0, 0.45, -0.3, 0.25]], np.float32)
-    materials = np.array([[0.9, 0.9, 0.9, 0.0, 1.0e6, 64.0],
-                          [0.75, 0.88, 1.0, 0.03, 1.5, 64.0],
-                          [0.95, 0.8, 0.7, 0.03, 1.5, 64.0]], np.float32)
-    return spheres, materials
+    """The config-4 spheres and materials of flare_b200.scene.viewer_spheres, as numpy."""
+    from flare_b200.scene import viewer_spheres
+    sph, mat = viewer_spheres()
+    return sph.numpy(), mat.numpy()
 
 
 def default_lights():
-    d = np.array([1.0, 1.0, 1.0], np.float32)
-    d /= np.linalg.norm(d)
-    return np.array([[1.0, 1.0, 1.0, d[0], d[1], d[2]]], np.float32)
+    from flare_b200.scene import viewer_lights
+    return viewer_lights().numpy()
 
 
 __all__ = ["viewer_forward", "sphere_nearest", "hit_lists_tmax", "default_spheres", "default_lights"]
