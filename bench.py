@@ -364,6 +364,23 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     out["e2e"] = dict(value=total_rays / (ms_e2e * 1e-3) / 1e6, unit="Mrays/s",
                       h2d_bytes_per_step=sum(sum(t.numel() * t.element_size() for t in h) for h in host),
                       d2h_bytes_per_step=4)
+    # the optimizer step after the backward (reference train.py:833-953): one fused Adam launch over the
+    # 16 parameter groups; not part of the headline step (the reference's metric is fwd + bwd)
+    from flare_b200.optim import ModelOptimizer
+    opt = ModelOptimizer(scene, step.grads)
+    it = [0]
+
+    def ostep():
+        it[0] += 1
+        opt.step(it[0])
+    for _ in range(2):
+        ostep()
+    ms_opt = time_steps(ostep, steps, world) / steps
+    elems = sum(sg.grad.numel() for sg in opt.adam.segments)
+    half = sum(sg.grad.numel() for sg in opt.adam.segments if sg.mirror is not None)
+    obytes = elems * 28 + half * 2  # p, m, v read + write, g read; fp16 mirrors written
+    out["optimizer_step"] = dict(ms=ms_opt, elements=elems, algo_bytes=obytes,
+                                 achieved_gbs=obytes / (ms_opt * 1e-3) / 1e9)
     out["_r"] = r
     out["shards"] = [(s.O.shape[0]) for s in shards]
     return out
@@ -401,7 +418,7 @@ def main():
             e.pop("_r", None)
             extras[f"config{c}"] = {k: v for k, v in e.items() if k in ("workload", "ms_per_step", "value",
                                                                           "hits_per_ray", "dominant", "kernels",
-                                                                          "traversal_passes")}
+                                                                          "traversal_passes", "optimizer_step")}
     if rank != 0:
         dist.destroy_process_group()
         return
@@ -437,6 +454,7 @@ def main():
         "kernels": {k: {"ms": v["ms"], "launches": v["launches"], "achieved_gbs": v["achieved_gbs"]}
                     for k, v in per.items()},
         "e2e": res["e2e"],
+        "optimizer_step": res.get("optimizer_step"),
         "clocks": clocks,
         # own kernels per step: traversal + shading launches (counted), 6 build kernels per SetGeometry, 1 ray
         # init per call, 3 backward helpers; the CUB radix sort's own launches are not counted

@@ -51,6 +51,18 @@ class ViewerArgs(ctypes.Structure):
 
 
 VIEWER_MAX_SPHERES, VIEWER_MAX_LIGHTS = 16, 8
+ADAM_MAX_SEGMENTS = 24
+
+
+class AdamSegment(ctypes.Structure):
+    _fields_ = [("param", vp), ("grad", vp), ("exp_avg", vp), ("exp_avg_sq", vp), ("param_f16", vp),
+                ("rows", ctypes.c_longlong), ("width", ctypes.c_int), ("p_stride", ctypes.c_int),
+                ("p_offset", ctypes.c_int), ("lr", ctypes.c_float), ("scale_reg", ctypes.c_float)]
+
+
+class AdamArgs(ctypes.Structure):
+    _fields_ = [("n_segments", ctypes.c_int), ("seg", AdamSegment * ADAM_MAX_SEGMENTS), ("beta1", ctypes.c_float),
+                ("beta2", ctypes.c_float), ("eps", ctypes.c_float), ("step", ctypes.c_int)]
 
 
 class Stats(ctypes.Structure):
@@ -77,6 +89,7 @@ EXPORTS = {
     "flare_forward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(ForwardArgs), vp]),
     "flare_backward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(BackwardArgs), vp]),
     "flare_viewer_forward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(ViewerArgs), vp]),
+    "flare_adam_step": (ctypes.c_int, [ctypes.POINTER(AdamArgs), vp]),
     "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
     "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
     "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),

@@ -286,6 +286,25 @@ int flare_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_
     return check_status(r, S(stream), "flare_forward");
 }
 
+int flare_adam_step(const flare_adam_args *a, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(a, "flare_adam_step: NULL argument");
+    CHECK_ARG(a->n_segments >= 0 && a->n_segments <= FLARE_ADAM_MAX_SEGMENTS, "flare_adam_step: %d segments (max %d)",
+              a->n_segments, FLARE_ADAM_MAX_SEGMENTS);
+    CHECK_ARG(a->step >= 1, "flare_adam_step: step %d < 1", a->step);
+    for (int i = 0; i < a->n_segments; ++i) {
+        const flare_adam_segment &s = a->seg[i];
+        CHECK_ARG(s.param && s.grad && s.exp_avg && s.exp_avg_sq, "flare_adam_step: segment %d has a NULL buffer", i);
+        CHECK_ARG(s.rows >= 0 && s.width >= 1 && s.p_offset >= 0 && s.p_offset + s.width <= s.p_stride,
+                  "flare_adam_step: segment %d: rows %lld width %d stride %d offset %d", i, s.rows, s.width, s.p_stride,
+                  s.p_offset);
+        CHECK_ARG(s.scale_reg == 0.0f || s.width == 2, "flare_adam_step: segment %d: scale_reg needs width 2", i);
+    }
+    int e = run_adam(a, S(stream));
+    if (e) return e;
+    return FLARE_OK;
+}
+
 int flare_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, void *stream) {
     g_err[0] = 0;
     CHECK_ARG(r && a, "flare_viewer_forward: NULL argument");

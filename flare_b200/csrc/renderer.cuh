@@ -129,6 +129,7 @@ size_t select_temp_bytes(int max_rays);
 int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st);
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
 int run_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, cudaStream_t st);
+int run_adam(const flare_adam_args *a, cudaStream_t st);
 int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
                  const void *A3, const float *b3, float *Y, cudaStream_t st);
 

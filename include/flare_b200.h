@@ -193,6 +193,33 @@ typedef struct flare_viewer_args {
 } flare_viewer_args;
 int flare_viewer_forward(flare_renderer *r, const flare_scene *scene, const flare_viewer_args *a, void *stream);
 
+/*
+ * The optimizer step (replaces torch.optim.Adam over the reference's 16 parameter groups,
+ * scene/gaussian_model.py:318-336, and the scale regulariser added to the s gradient, train.py:850-852):
+ * one launch over all segments.  Segment i updates param[row * p_stride + p_offset + col] for
+ * row < rows, col < width from the dense grad / exp_avg / exp_avg_sq [row * width + col] (moments
+ * zero-initialised by the caller) with learning rate lr; param_f16 (optional) receives the updated value
+ * at the same address in fp16; scale_reg > 0 (width-2 s rows only) adds scale_reg * exp(s)^2 /
+ * sqrt(sum_row exp(s)^2) to the gradient.  step is Adam's step count t >= 1 (bias corrections).
+ */
+#define FLARE_ADAM_MAX_SEGMENTS 24
+typedef struct flare_adam_segment {
+    float *param;
+    const float *grad;
+    float *exp_avg, *exp_avg_sq;
+    void *param_f16;
+    long long rows;
+    int width, p_stride, p_offset;
+    float lr, scale_reg;
+} flare_adam_segment;
+typedef struct flare_adam_args {
+    int n_segments;
+    flare_adam_segment seg[FLARE_ADAM_MAX_SEGMENTS];
+    float beta1, beta2, eps;
+    int step;
+} flare_adam_args;
+int flare_adam_step(const flare_adam_args *a, void *stream);
+
 /* Statistics of the last forward/backward call (counted on the device; reading them synchronises the
    stream of that call): rays, passes, composited hits, primitive tests, BVH node visits. */
 typedef struct flare_stats {
