@@ -65,6 +65,13 @@ class AdamArgs(ctypes.Structure):
                 ("beta2", ctypes.c_float), ("eps", ctypes.c_float), ("step", ctypes.c_int)]
 
 
+GATHER_MAX_TENSORS = 32
+
+
+class GatherTensor(ctypes.Structure):
+    _fields_ = [("src", vp), ("src_alt", vp), ("dst", vp), ("row_bytes", ctypes.c_int)]
+
+
 class Stats(ctypes.Structure):
     _fields_ = [("rays", ctypes.c_longlong), ("passes", ctypes.c_longlong), ("hits_composited", ctypes.c_longlong),
                 ("prim_tests", ctypes.c_longlong), ("node_visits", ctypes.c_longlong)]
@@ -90,6 +97,8 @@ EXPORTS = {
     "flare_backward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(BackwardArgs), vp]),
     "flare_viewer_forward": (ctypes.c_int, [vp, ctypes.POINTER(Scene), ctypes.POINTER(ViewerArgs), vp]),
     "flare_adam_step": (ctypes.c_int, [ctypes.POINTER(AdamArgs), vp]),
+    "flare_gather_rows": (ctypes.c_int, [ctypes.POINTER(GatherTensor), ctypes.c_int, vp, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int, vp]),
     "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
     "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
     "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),

@@ -305,6 +305,19 @@ int flare_adam_step(const flare_adam_args *a, void *stream) {
     return FLARE_OK;
 }
 
+int flare_gather_rows(const flare_gather_tensor *t, int n_tensors, const int *src_row, int n_out, int alt_begin,
+                      int alt_end, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(n_tensors >= 0 && n_tensors <= FLARE_GATHER_MAX_TENSORS, "flare_gather_rows: %d tensors (max %d)",
+              n_tensors, FLARE_GATHER_MAX_TENSORS);
+    CHECK_ARG(n_out >= 0 && (n_out == 0 || src_row), "flare_gather_rows: NULL row map");
+    for (int i = 0; i < n_tensors; ++i)
+        CHECK_ARG(t && t[i].src && t[i].dst && t[i].row_bytes > 0 && (t[i].row_bytes & 3) == 0,
+                  "flare_gather_rows: tensor %d: NULL buffer or row of %d bytes (multiple of 4 required)", i,
+                  t ? t[i].row_bytes : 0);
+    return run_gather_rows(t, n_tensors, src_row, n_out, alt_begin, alt_end, S(stream));
+}
+
 int flare_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, void *stream) {
     g_err[0] = 0;
     CHECK_ARG(r && a, "flare_viewer_forward: NULL argument");

@@ -11,6 +11,8 @@
 // p -= (lr / (1 - b1^t)) m / (sqrt(v) / sqrt(1 - b2^t) + eps).
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "renderer.cuh"
 
 namespace flare {
@@ -116,6 +118,62 @@ int run_adam(const flare_adam_args *in, cudaStream_t st) {
         return FLARE_E_INVALID;
     }
     adam_kernel<<<(unsigned)blocks, ADAM_THREADS, 0, st>>>(a);
+    FLARE_CUDA_TRY(cudaGetLastError());
+    return FLARE_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Row gather for densification / pruning (reference train.py:955-1240): every per-primitive tensor
+// (parameters and their Adam moments) is rebuilt in one launch from a map out-row -> source row; rows
+// [alt_begin, alt_end) read a tensor's alternative source when it has one (the split primitives' first
+// copies take the centre and moments from before the optimizer step).  One warp per output row.
+// ------------------------------------------------------------------------------------------------
+struct GatherT {
+    const char *src, *alt;
+    char *dst;
+    int row_bytes;
+};
+struct GatherArgs {
+    int n;
+    GatherT t[FLARE_GATHER_MAX_TENSORS];
+};
+
+__global__ void gather_rows_kernel(const GatherArgs a, const int *__restrict__ src_row, int n_out, int alt_begin,
+                                   int alt_end) {
+    const int lane = threadIdx.x & 31;
+    for (long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_out;
+         r += ((long long)gridDim.x * blockDim.x) >> 5) {
+        const long long sr = src_row[r];
+        const bool use_alt = r >= alt_begin && r < alt_end;
+        for (int i = 0; i < a.n; ++i) {
+            const GatherT &t = a.t[i];
+            const char *s = (use_alt && t.alt ? t.alt : t.src) + sr * t.row_bytes;
+            char *d = t.dst + r * t.row_bytes;
+            if ((t.row_bytes & 15) == 0 && ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0) {
+                for (int b = lane * 16; b < t.row_bytes; b += 32 * 16)
+                    *reinterpret_cast<uint4 *>(d + b) = *reinterpret_cast<const uint4 *>(s + b);
+            } else {
+                for (int b = lane * 4; b < t.row_bytes; b += 32 * 4)
+                    *reinterpret_cast<unsigned *>(d + b) = *reinterpret_cast<const unsigned *>(s + b);
+            }
+        }
+    }
+}
+
+int run_gather_rows(const flare_gather_tensor *t, int n_tensors, const int *src_row, int n_out, int alt_begin,
+                    int alt_end, cudaStream_t st) {
+    GatherArgs a{};
+    a.n = n_tensors;
+    for (int i = 0; i < n_tensors; ++i) {
+        a.t[i].src = static_cast<const char *>(t[i].src);
+        a.t[i].alt = static_cast<const char *>(t[i].src_alt);
+        a.t[i].dst = static_cast<char *>(t[i].dst);
+        a.t[i].row_bytes = t[i].row_bytes;
+    }
+    if (n_out <= 0) return FLARE_OK;
+    const int B = 256;
+    const long long blocks = std::min<long long>(((long long)n_out * 32 + B - 1) / B, 148 * 64);
+    gather_rows_kernel<<<(unsigned)blocks, B, 0, st>>>(a, src_row, n_out, alt_begin, alt_end);
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
 }

@@ -130,6 +130,8 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
 int run_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, cudaStream_t st);
 int run_adam(const flare_adam_args *a, cudaStream_t st);
+int run_gather_rows(const flare_gather_tensor *t, int n_tensors, const int *src_row, int n_out, int alt_begin,
+                    int alt_end, cudaStream_t st);
 int selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
                  const void *A3, const float *b3, float *Y, cudaStream_t st);
 

@@ -118,6 +118,11 @@ class TrainStep:
         self.hits = 0
         self.fwd_passes = 0
 
+    def rebind(self, scene: Scene, grads: GradBuffer):
+        """Uses a new primitive set (after densification) and its gradient buffer."""
+        self.sc, self.grads = scene, grads
+        self.loss = grads["loss"]
+
     def geometry(self):
         sc = self.sc
         self.r.SetGeometry(sc.m, torch.exp(sc.s), sc.q, torch.sigmoid(sc.RGBA[:, 3]).contiguous(),

@@ -149,19 +149,22 @@ class ModelOptimizer:
 
     def __init__(self, scene, grads, lr_table=REFERENCE_LR, reg_scale_lambda=REG_SCALE_LAMBDA):
         sc = scene
-        n = sc.m.shape[0]
         self.scene, self.grads, self.lr_table = sc, grads, lr_table
+        self.reg_scale_lambda = reg_scale_lambda
         self.cond32 = sc.cond.float().contiguous()
         self.W1 = sc.A1.float().contiguous()
         self.W2 = sc.A2.float().contiguous()
         self.W3 = sc.A3.float().contiguous()
-        self.dense = {"w1_uv": torch.zeros(64, 8, device=sc.m.device), "w1_v": torch.zeros(64, 24, device=sc.m.device),
-                      "w1_conditioning": torch.zeros(64, 96, device=sc.m.device)}
-        dg = dense_decoder_grads(grads)
-        self._dec = {k: torch.zeros_like(v) for k, v in dg.items()}
-        G = grads
-        S = Segment
-        segs = [S("RGB", sc.RGBA, G["RGB"], 3, 0), S("A", sc.RGBA, G["A"], 1, 3), S("k", sc.k, G["k"], 1),
+        dev = sc.m.device
+        self.dense = {"w1_uv": torch.zeros(64, 8, device=dev), "w1_v": torch.zeros(64, 24, device=dev),
+                      "w1_conditioning": torch.zeros(64, 96, device=dev)}
+        self._dec = {k: torch.zeros_like(v) for k, v in dense_decoder_grads(grads).items()}
+        self.adam = FusedAdam(self._segments())
+
+    def _segments(self):
+        sc, G, S = self.scene, self.grads, Segment
+        n = sc.m.shape[0]
+        return [S("RGB", sc.RGBA, G["RGB"], 3, 0), S("A", sc.RGBA, G["A"], 1, 3), S("k", sc.k, G["k"], 1),
                 S("w1_uv", self.W1, self.dense["w1_uv"], 8, 0, sc.A1),
                 S("w1_v", self.W1, self.dense["w1_v"], 24, 8, sc.A1),
                 S("w1_conditioning", self.W1, self.dense["w1_conditioning"], 96, 32, sc.A1),
@@ -169,8 +172,19 @@ class ModelOptimizer:
                 S("b2", sc.b2, self._dec["b2"], 64), S("w3", self.W3, self._dec["w3"], 64, 0, sc.A3),
                 S("b3", sc.b3, self._dec["b3"], 16), S("conditioning", self.cond32, G["cond"], 96, 0, sc.cond),
                 S("features", sc.features, G["features"], 13154), S("m", sc.m, G["m"], 3),
-                S("s", sc.s, G["s"], 2, 0, None, reg_scale_lambda / n), S("q", sc.q, G["q"], 4)]
-        self.adam = FusedAdam(segs)
+                S("s", sc.s, G["s"], 2, 0, None, self.reg_scale_lambda / n), S("q", sc.q, G["q"], 4)]
+
+    def rebind(self, grads, moments: dict):
+        """After the primitive set changed (densification): the scene holds the new per-primitive
+        tensors, `grads` is the new gradient buffer and `moments` maps the per-primitive groups to their
+        rebuilt (exp_avg, exp_avg_sq); the decoder groups keep theirs, the step count is unchanged."""
+        old = {s.name: st for s, st in zip(self.adam.segments, self.adam.state)}
+        self.grads = grads
+        self.adam.segments = self._segments()
+        self.adam.state = [moments.get(s.name, old[s.name]) for s in self.adam.segments]
+        for s_, (m_, v_) in zip(self.adam.segments, self.adam.state):
+            if m_.numel() != s_.grad.numel():
+                raise ValueError(f"{s_.name}: {m_.numel()} moments for {s_.grad.numel()} gradients")
 
     def step(self, iteration: int):
         dg = dense_decoder_grads(self.grads)

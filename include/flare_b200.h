@@ -220,6 +220,21 @@ typedef struct flare_adam_args {
 } flare_adam_args;
 int flare_adam_step(const flare_adam_args *a, void *stream);
 
+/*
+ * Densification / pruning support (replaces the per-tensor index / cat sequence of train.py:955-1240):
+ * builds every output tensor in one launch, dst row r = source row src_row[r] (r < n_out); rows
+ * [alt_begin, alt_end) read src_alt instead of src when src_alt != NULL.  Rows are row_bytes long
+ * (multiple of 4); sources and destinations are device memory and must not overlap.
+ */
+#define FLARE_GATHER_MAX_TENSORS 32
+typedef struct flare_gather_tensor {
+    const void *src, *src_alt;
+    void *dst;
+    int row_bytes;
+} flare_gather_tensor;
+int flare_gather_rows(const flare_gather_tensor *tensors, int n_tensors, const int *src_row, int n_out, int alt_begin,
+                      int alt_end, void *stream);
+
 /* Statistics of the last forward/backward call (counted on the device; reading them synchronises the
    stream of that call): rays, passes, composited hits, primitive tests, BVH node visits. */
 typedef struct flare_stats {
