@@ -10,10 +10,12 @@ namespace flare {
 
 constexpr int K_HITS = FLARE_HIT_BUFFER_SIZE;  // 16: hits per Render call (the reference's k-buffer)
 #ifndef FLARE_K_PASS
-#define FLARE_K_PASS 48
+#define FLARE_K_PASS 42
 #endif
 // Hits gathered per pass inside Forward / Backward.  The composited result does not depend on it (hits
-// are consumed in (t, index) order either way); it trades traversal restarts against buffer registers.
+// are consumed in (t, index) order either way); it trades traversal restarts against the per-ray heap in
+// shared memory: 42 entries (42 KB per 128-ray block + the stack) is the most that keeps 5 traversal
+// blocks per SM.
 constexpr int K_PASS = FLARE_K_PASS;
 constexpr int COND = FLARE_COND_DIM;           // 96
 constexpr int LUT = FLARE_LUT_SIZE;            // 13154 floats
