@@ -317,46 +317,30 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
         unsigned mask = __ballot_sync(0xffffffffu, want);
         int node = 0, sp = 0;
         const unsigned long long max_visits = 2ull * (unsigned long long)n + 64ull;
+        // The next node's fetch is issued as soon as the box tests decide it, ahead of this node's leaf
+        // tests, so its L2 latency overlaps the primitive-record fetches and hit tests.
+        const float4 *np = reinterpret_cast<const float4 *>(nodes);
+        float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
+        int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
         while (mask) {
             if (++nnode > max_visits) {
                 if (lane == 0) atomicOr(status, ERR_INDEX);
                 break;
             }
             const bool in = (mask >> lane) & 1u;
-            const float4 *np = reinterpret_cast<const float4 *>(nodes + node);
-            const float4 a = __ldg(np), b = __ldg(np + 1), c = __ldg(np + 2);
-            const int4 d = __ldg(reinterpret_cast<const int4 *>(np + 3));
             const float bk = fminf(kb.rt, tcap);
             const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
             float t0 = 0.0f, t1 = 0.0f;
-            bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
-            bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
-            if (d.x < 0) {  // warp-uniform: leaf child 0
-                if (h0) {
-                    float t;
-                    ++nprim;
-                    if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
-                        const int pid = __ldg(ids + ~d.x);
-                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
-                    }
-                }
-                h0 = false;
-            }
-            if (d.y < 0) {
-                if (h1) {
-                    float t;
-                    ++nprim;
-                    if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
-                        const int pid = __ldg(ids + ~d.y);
-                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
-                    }
-                }
-                h1 = false;
-            }
-            const unsigned m0 = __ballot_sync(0xffffffffu, h0), m1 = __ballot_sync(0xffffffffu, h1);
+            const bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
+            const bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
+            const bool leaf0 = d.x < 0, leaf1 = d.y < 0;  // warp-uniform
+            const bool i0 = h0 && !leaf0, i1 = h1 && !leaf1;
+            const unsigned m0 = __ballot_sync(0xffffffffu, i0), m1 = __ballot_sync(0xffffffffu, i1);
+            int next = -1;
+            unsigned nmask = 0;
             if (m0 && m1) {
                 // nearer child first by lane vote (lanes that hit only one child vote for it)
-                const unsigned v0 = __ballot_sync(0xffffffffu, h0 && (!h1 || t0 <= t1));
+                const unsigned v0 = __ballot_sync(0xffffffffu, i0 && (!i1 || t0 <= t1));
                 const bool first0 = __popc(v0) * 2 >= __popc(m0 | m1);
                 if (sp < TRACE_STACK) {
                     if (lane == 0) {
@@ -367,18 +351,55 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
                 } else if (lane == 0) {
                     atomicOr(status, ERR_STACK);
                 }
-                node = first0 ? d.x : d.y;
-                mask = first0 ? m0 : m1;
+                next = first0 ? d.x : d.y;
+                nmask = first0 ? m0 : m1;
+            } else if (m0) {
+                next = d.x;
+                nmask = m0;
+            } else if (m1) {
+                next = d.y;
+                nmask = m1;
+            } else {
                 __syncwarp();
-                continue;
+                if (sp > 0) {
+                    --sp;
+                    next = s_node[wib][sp];
+                    nmask = s_mask[wib][sp];
+                }
             }
-            if (m0) { node = d.x; mask = m0; continue; }
-            if (m1) { node = d.y; mask = m1; continue; }
+            float4 na = a, nb = b, nc = c;
+            int4 nd = d;
+            if (next >= 0) {
+                const float4 *nq = reinterpret_cast<const float4 *>(nodes + next);
+                na = __ldg(nq);
+                nb = __ldg(nq + 1);
+                nc = __ldg(nq + 2);
+                nd = __ldg(reinterpret_cast<const int4 *>(nq + 3));
+            }
+            if (leaf0 && h0) {
+                float t;
+                ++nprim;
+                if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
+                    const int pid = __ldg(ids + ~d.x);
+                    if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                }
+            }
+            if (leaf1 && h1) {
+                float t;
+                ++nprim;
+                if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
+                    const int pid = __ldg(ids + ~d.y);
+                    if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                }
+            }
             __syncwarp();
-            if (sp == 0) break;
-            --sp;
-            node = s_node[wib][sp];
-            mask = s_mask[wib][sp];
+            if (next < 0) break;
+            node = next;
+            mask = nmask;
+            a = na;
+            b = nb;
+            c = nc;
+            d = nd;
         }
     }
     if (live) {  // heap sort: the largest key leaves first, into the last slot
