@@ -173,8 +173,8 @@ __device__ __forceinline__ int delta(const unsigned *codes, int n, int i, int j)
     return __clz(a ^ b);
 }
 
-__global__ void karras_kernel(const unsigned *__restrict__ codes, int n, Node *__restrict__ nodes,
-                              int *__restrict__ parent) {
+__global__ void karras_kernel(const unsigned *__restrict__ codes, const int *__restrict__ ids_sorted, int n,
+                              Node *__restrict__ nodes, int *__restrict__ parent) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n - 1) return;
     int d = (delta(codes, n, i, i + 1) - delta(codes, n, i, i - 1)) >= 0 ? 1 : -1;
@@ -196,7 +196,8 @@ __global__ void karras_kernel(const unsigned *__restrict__ codes, int n, Node *_
     int lo = min(i, j), hi = max(i, j);
     int c0 = (lo == gamma) ? ~gamma : gamma;
     int c1 = (hi == gamma + 1) ? ~(gamma + 1) : gamma + 1;
-    nodes[i].d = make_int4(c0, c1, 0, 0);
+    // links, then the original index of each leaf child (the traversal reads it with the node)
+    nodes[i].d = make_int4(c0, c1, c0 < 0 ? ids_sorted[gamma] : -1, c1 < 0 ? ids_sorted[gamma + 1] : -1);
     if (c0 >= 0) parent[c0] = i; else parent[(n - 1) + gamma] = i;
     if (c1 >= 0) parent[c1] = i; else parent[(n - 1) + gamma + 1] = i;
 }
@@ -300,7 +301,7 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
     } else {
         if (n > 1) {
             FLARE_CUDA_TRY(cudaMemsetAsync(r->refit_flag, 0, (size_t)(n - 1) * sizeof(unsigned), st));
-            karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(r->morton_sorted, n, r->nodes, r->parent);
+            karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(r->morton_sorted, r->ids_sorted, n, r->nodes, r->parent);
         }
         refit_kernel<<<G, B, 0, st>>>(n, r->ids_sorted, r->aabb, r->nodes, r->parent, r->refit_flag, r->rec,
                                       r->frames, r->dstatus);
@@ -324,7 +325,7 @@ int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, c
                                                    0, MORTON_END_BIT, st));
     if (n > 1) {
         FLARE_CUDA_TRY(cudaMemsetAsync(g.refit_flag, 0, (size_t)(n - 1) * sizeof(unsigned), st));
-        karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(g.morton_sorted, n, g.nodes, g.parent);
+        karras_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(g.morton_sorted, g.ids_sorted, n, g.nodes, g.parent);
     }
     refit_kernel<<<G, B, 0, st>>>(n, g.ids_sorted, g.aabb, g.nodes, g.parent, g.refit_flag, g.rec, g.frames, g.status);
     FLARE_CUDA_TRY(cudaGetLastError());

@@ -47,7 +47,7 @@ struct __align__(16) Node {
     float4 a;  // lo0.x lo0.y lo0.z hi0.x
     float4 b;  // hi0.y hi0.z lo1.x lo1.y
     float4 c;  // lo1.z hi1.x hi1.y hi1.z
-    int4 d;    // c0 c1 - -
+    int4 d;    // c0 c1 (internal >= 0, leaf = ~sorted position), pid0 pid1 (original index of a leaf child)
 };
 
 // Polygon edge constants for the hit test (host computes them once per renderer).

@@ -97,7 +97,7 @@ __global__ void ploc_merge_kernel(int m, int n, int created, const int *__restri
                                   const unsigned long long *__restrict__ flags,
                                   const unsigned long long *__restrict__ scan, const float *__restrict__ cbox,
                                   const int *__restrict__ cid, float *__restrict__ cbox_out, int *__restrict__ cid_out,
-                                  Node *__restrict__ nodes) {
+                                  Node *__restrict__ nodes, const int *__restrict__ ids_sorted) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= m) return;
     const unsigned long long f = flags[i];
@@ -112,7 +112,8 @@ __global__ void ploc_merge_kernel(int m, int n, int created, const int *__restri
         float *nf = reinterpret_cast<float *>(nodes + node);
         nf[0] = b.lx; nf[1] = b.ly; nf[2] = b.lz; nf[3] = b.hx; nf[4] = b.hy; nf[5] = b.hz;
         nf[6] = o.lx; nf[7] = o.ly; nf[8] = o.lz; nf[9] = o.hx; nf[10] = o.hy; nf[11] = o.hz;
-        nodes[node].d = make_int4(id, cid[j], 0, 0);
+        const int cj = cid[j];
+        nodes[node].d = make_int4(id, cj, id < 0 ? ids_sorted[~id] : -1, cj < 0 ? ids_sorted[~cj] : -1);
         b = Box6{fminf(b.lx, o.lx), fminf(b.ly, o.ly), fminf(b.lz, o.lz),
                  fmaxf(b.hx, o.hx), fmaxf(b.hy, o.hy), fmaxf(b.hz, o.hz)};
         id = node;
@@ -180,7 +181,7 @@ int build_hierarchy_ploc(int n, const int *ids_sorted, const float *aabb, const 
         size_t t = scan_tmp;
         FLARE_CUDA_TRY(cub::DeviceScan::ExclusiveSum(tmp, t, flags, scan, m, st));
         ploc_merge_kernel<<<G, B, 0, st>>>(m, n, created, nn, flags, scan, cbox[cur], cid[cur], cbox[cur ^ 1],
-                                           cid[cur ^ 1], nodes);
+                                           cid[cur ^ 1], nodes, ids_sorted);
         // totals = last exclusive prefix + last flag
         FLARE_CUDA_TRY(cudaMemcpyAsync(h_total, scan + (m - 1), sizeof(unsigned long long), cudaMemcpyDeviceToHost, st));
         FLARE_CUDA_TRY(cudaMemcpyAsync(h_total + 1, flags + (m - 1), sizeof(unsigned long long),

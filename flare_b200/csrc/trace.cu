@@ -49,16 +49,15 @@ __device__ __forceinline__ void kbuf_insert(KBuf<K> &b, float t, int id) {
     b.i[0] = lt_k ? id : b.i[0];
 }
 
-// Exact hit test on the record of sorted primitive p (same operation order as the oracle).
-__device__ __forceinline__ bool hit_prim(const float4 *__restrict__ rec, int p, float3 O, float3 v, float t_min,
-                                         const PolyConst &c_poly, float &t_out, float t_max = INFINITY) {
-    float4 r0 = __ldg(rec + 3 * (size_t)p), r1 = __ldg(rec + 3 * (size_t)p + 1), r2 = __ldg(rec + 3 * (size_t)p + 2);
+// Exact hit test against one 48-byte primitive record (same operation order as the oracle).
+__device__ __forceinline__ bool hit_rec(float4 r0, float4 r1, float4 r2, float3 O, float3 v, float t_min,
+                                        const PolyConst &c_poly, float &t_out, float t_max = INFINITY) {
     // r0 = m.xyz N.x, r1 = N.yz Ua.xy, r2 = Ua.z Va.xyz
     float dx = __fsub_rn(r0.x, O.x), dy = __fsub_rn(r0.y, O.y), dz = __fsub_rn(r0.z, O.z);
     float num = __fmaf_rn(r0.w, dx, __fmaf_rn(r1.x, dy, __fmul_rn(r1.y, dz)));
     float den = __fmaf_rn(r0.w, v.x, __fmaf_rn(r1.x, v.y, __fmul_rn(r1.y, v.z)));
     float t = __fdiv_rn(num, den);
-    if (!(t >= t_min) || t > t_max) return false;  // beyond the 16th hit: cannot enter the buffer
+    if (!(t >= t_min) || t > t_max) return false;  // beyond the K-th buffered hit: cannot enter the buffer
     float ex = __fsub_rn(__fmaf_rn(v.x, t, O.x), r0.x);
     float ey = __fsub_rn(__fmaf_rn(v.y, t, O.y), r0.y);
     float ez = __fsub_rn(__fmaf_rn(v.z, t, O.z), r0.z);
@@ -73,6 +72,13 @@ __device__ __forceinline__ bool hit_prim(const float4 *__restrict__ rec, int p, 
     }
     t_out = t;
     return true;
+}
+
+// Exact hit test on the record of sorted primitive p.
+__device__ __forceinline__ bool hit_prim(const float4 *__restrict__ rec, int p, float3 O, float3 v, float t_min,
+                                         const PolyConst &c_poly, float &t_out, float t_max = INFINITY) {
+    return hit_rec(__ldg(rec + 3 * (size_t)p), __ldg(rec + 3 * (size_t)p + 1), __ldg(rec + 3 * (size_t)p + 2), O, v,
+                   t_min, c_poly, t_out, t_max);
 }
 
 __device__ __forceinline__ bool slab(float lx, float ly, float lz, float hx, float hy, float hz, float3 O, float3 iv,
@@ -154,7 +160,7 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
                     float t;
                     ++nprim;
                     if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
-                        const int pid = __ldg(ids + ~d.x);
+                        const int pid = d.z;
                         if (t < kb.t[K - 1] || (t == kb.t[K - 1] && pid < kb.i[K - 1]))
                             kbuf_insert(kb, t, pid);
                     }
@@ -166,7 +172,7 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
                     float t;
                     ++nprim;
                     if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
-                        const int pid = __ldg(ids + ~d.y);
+                        const int pid = d.w;
                         if (t < kb.t[K - 1] || (t == kb.t[K - 1] && pid < kb.i[K - 1]))
                             kbuf_insert(kb, t, pid);
                     }
@@ -271,7 +277,7 @@ __device__ __forceinline__ void heap_insert(HeapBuf<K> &h, float t, int id) {
 }
 
 template <bool STATS, int K>
-__global__ void __launch_bounds__(128) trace_heap_kernel(
+__global__ void __launch_bounds__(128, 5) trace_heap_kernel(
     const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
@@ -328,12 +334,12 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
                 break;
             }
             const bool in = (mask >> lane) & 1u;
+            const bool leaf0 = d.x < 0, leaf1 = d.y < 0;  // warp-uniform
             const float bk = fminf(kb.rt, tcap);
             const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
             float t0 = 0.0f, t1 = 0.0f;
             const bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
             const bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
-            const bool leaf0 = d.x < 0, leaf1 = d.y < 0;  // warp-uniform
             const bool i0 = h0 && !leaf0, i1 = h1 && !leaf1;
             const unsigned m0 = __ballot_sync(0xffffffffu, i0), m1 = __ballot_sync(0xffffffffu, i1);
             int next = -1;
@@ -380,7 +386,7 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
                 float t;
                 ++nprim;
                 if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
-                    const int pid = __ldg(ids + ~d.x);
+                    const int pid = d.z;
                     if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
                 }
             }
@@ -388,7 +394,7 @@ __global__ void __launch_bounds__(128) trace_heap_kernel(
                 float t;
                 ++nprim;
                 if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
-                    const int pid = __ldg(ids + ~d.y);
+                    const int pid = d.w;
                     if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
                 }
             }
@@ -511,7 +517,7 @@ __global__ void __launch_bounds__(128) trace_group_kernel(
                         float t;
                         ++nprim;
                         if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bound)) {
-                            const int pid = __ldg(ids + ~d.x);
+                            const int pid = d.z;
                             if (key_less(t, pid, kb.t[K - 1], kb.i[K - 1])) kbuf_insert(kb, t, pid);
                         }
                     }
@@ -522,7 +528,7 @@ __global__ void __launch_bounds__(128) trace_group_kernel(
                         float t;
                         ++nprim;
                         if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bound)) {
-                            const int pid = __ldg(ids + ~d.y);
+                            const int pid = d.w;
                             if (key_less(t, pid, kb.t[K - 1], kb.i[K - 1])) kbuf_insert(kb, t, pid);
                         }
                     }
