@@ -721,7 +721,7 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
     if (count <= 0) return FLARE_OK;
     const int B = 128;
     // Sparse passes: G lanes per ray, G chosen so the pass still spreads over the whole GPU
-    static const int g32_max = getenv_int("FLARE_TRACE_G32_MAX", 4096);
+    static const int g32_max = getenv_int("FLARE_TRACE_G32_MAX", 16384);
     static const int g16_max = getenv_int("FLARE_TRACE_G16_MAX", 0);
     static const int g8_max = getenv_int("FLARE_TRACE_G8_MAX", 0);
     if (k == K_PASS && K_PASS != K_HITS && (count <= g32_max || count <= g16_max || count <= g8_max)) {
