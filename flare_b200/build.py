@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libflare_b200.so")
-SOURCES = ["api.cu", "bvh.cu", "ploc.cu", "trace.cu", "shade.cu", "viewer.cu", "optim.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "bvh.cu", "bvh4.cu", "ploc.cu", "trace.cu", "shade.cu", "viewer.cu", "optim.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "renderer.cuh", "umma.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

@@ -125,6 +125,17 @@ __device__ __forceinline__ unsigned expand_bits10(unsigned v) {
 // Hierarchy builder: the Karras radix tree (default), or locally-ordered clustering (ploc.cu) when the
 // environment sets FLARE_BVH=ploc -- a slightly better tree for a ~3x longer build (config 3: traversal
 // -3.5 %, build +5 ms; config 2: no net gain).
+// 4-wide traversal hierarchy (collapsed from the binary one after every build) with FLARE_BVH4=1.  Off by
+// default: on the 6M-primitive workload its traversal measured 569 ms per step against 512 ms for the
+// binary one (same hits), so the dependent node-fetch chain it halves is not what bounds the traversal.
+static bool use_bvh4() {
+    static const bool on = [] {
+        const char *e = getenv("FLARE_BVH4");
+        return e && strcmp(e, "1") == 0;
+    }();
+    return on;
+}
+
 static bool use_ploc() {
     static const bool on = [] {
         const char *e = getenv("FLARE_BVH");
@@ -256,6 +267,10 @@ static int grow(flare_renderer *r, int n, cudaStream_t st) {
     cudaFree(r->sort_tmp);
     cudaFree(r->ploc_scratch);
     r->ploc_scratch = nullptr;
+    cudaFree(r->nodes4);
+    cudaFree(r->bvh4_scratch);
+    r->nodes4 = nullptr;
+    r->bvh4_scratch = nullptr;
     r->frames = nullptr; r->rec = nullptr; r->aabb = nullptr; r->morton = r->morton_sorted = nullptr;
     r->ids = r->ids_sorted = nullptr; r->nodes = nullptr; r->parent = nullptr; r->refit_flag = nullptr;
     r->sort_tmp = nullptr; r->cap_n = 0;
@@ -274,6 +289,10 @@ static int grow(flare_renderer *r, int n, cudaStream_t st) {
     cub::DeviceRadixSort::SortPairs(nullptr, tmp, r->morton, r->morton_sorted, r->ids, r->ids_sorted, n, 0, MORTON_END_BIT, st);
     FLARE_CUDA_TRY(cudaMalloc(&r->sort_tmp, tmp));
     if (use_ploc()) FLARE_CUDA_TRY(cudaMalloc(&r->ploc_scratch, ploc_scratch_bytes(n)));
+    if (use_bvh4()) {
+        FLARE_CUDA_TRY(cudaMalloc(&r->nodes4, (N > 1 ? N - 1 : 1) * sizeof(Node4)));
+        FLARE_CUDA_TRY(cudaMalloc(&r->bvh4_scratch, bvh4_scratch_bytes(n)));
+    }
     r->sort_tmp_bytes = tmp;
     r->cap_n = n;
     return FLARE_OK;
@@ -305,6 +324,10 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
         }
         refit_kernel<<<G, B, 0, st>>>(n, r->ids_sorted, r->aabb, r->nodes, r->parent, r->refit_flag, r->rec,
                                       r->frames, r->dstatus);
+    }
+    if (r->nodes4) {
+        e = build_bvh4(r->nodes, n, r->nodes4, r->bvh4_scratch, r->dstatus, st);
+        if (e) return e;
     }
     FLARE_CUDA_TRY(cudaGetLastError());
     r->n = n;

@@ -50,6 +50,14 @@ struct __align__(16) Node {
     int4 d;    // c0 c1 (internal >= 0, leaf = ~sorted position), pid0 pid1 (original index of a leaf child)
 };
 
+// 4-wide node (bvh4.cu): child boxes as structure of arrays, links (internal >= 0: 4-wide node index,
+// leaf: ~sorted position) and each leaf child's original index; 128 bytes, one line per visit.
+constexpr int NODE4_EMPTY = (int)0x80000000;  // link of an unused child slot (never ~position, positions < n)
+struct __align__(128) Node4 {
+    float4 lox, loy, loz, hix, hiy, hiz;
+    int4 link, pid;
+};
+
 // Polygon edge constants for the hit test (host computes them once per renderer).
 struct PolyConst {
     int n;

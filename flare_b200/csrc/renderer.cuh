@@ -24,6 +24,8 @@ struct flare_renderer {
     float *bounds = nullptr;                    // 6 floats (scene centre bounds, ordered-int encoded)
     void *sort_tmp = nullptr;
     void *ploc_scratch = nullptr;               // clustering build scratch (ploc.cu)
+    flare::Node4 *nodes4 = nullptr;             // 4-wide collapse of nodes (bvh4.cu), null when not used
+    void *bvh4_scratch = nullptr;
     size_t sort_tmp_bytes = 0;
 
     // ---- per-ray scratch, sized max_rays ----
@@ -104,6 +106,8 @@ int build_geometry_into(const GeomBufs &g, const float *m, const float *scale, c
                         const float *kappa, int n, cudaStream_t st);
 size_t geometry_sort_temp_bytes(int n);
 size_t ploc_scratch_bytes(int n);
+size_t bvh4_scratch_bytes(int n);
+int build_bvh4(const Node *nodes, int n, Node4 *nodes4, void *scratch, int *status, cudaStream_t st);
 int build_hierarchy_ploc(int n, const int *ids_sorted, const float *aabb, const float *frames, Node *nodes,
                          float4 *rec, void *scratch, unsigned long long *h_total, cudaStream_t st);
 int launch_trace_geom(const Node *nodes, const float4 *rec, const int *ids_sorted, int n, const PolyConst &poly,

@@ -428,6 +428,177 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
 }
 
 
+// The heap traversal over the 4-wide hierarchy: one 128-byte line per visit, four box tests per lane;
+// entered internal children are visited nearest first (by the warp's nearest entry distance), the
+// others pushed; the next node's fetch is issued before this node's leaf tests.  The stack holds node
+// indices only: a popped node is tested by every lane still tracing (a lane that missed its box misses
+// its children too, the children's boxes lying inside it).
+__device__ __forceinline__ bool slab4(float lx, float ly, float lz, float hx, float hy, float hz, float3 O, float3 iv,
+                                      float tlo, float thi, float &tnear) {
+    return slab(lx, ly, lz, hx, hy, hz, O, iv, tlo, thi, tnear);
+}
+
+template <bool STATS, int K>
+__global__ void __launch_bounds__(128, 5) trace_heap4_kernel(
+    const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
+    const int *__restrict__ ray_ids, int count, const Node4 *__restrict__ nodes, const float4 *__restrict__ rec,
+    const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
+    const float *__restrict__ tmax_ = nullptr) {
+    constexpr int STACK4 = 128;
+    __shared__ int s_node[4][STACK4];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = j < count;
+    unsigned long long nprim = 0, nnode = 0;
+    int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
+    float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+    float t_min = INFINITY, tcap = INFINITY;
+    if (live) {
+        O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
+        v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
+        t_min = tmin_[ray];
+        if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
+    }
+    extern __shared__ __align__(16) unsigned char heap_smem[];
+    HeapBuf<K> kb;
+    kb.t = reinterpret_cast<float *>(heap_smem);
+    kb.i = reinterpret_cast<int *>(heap_smem + (size_t)K * 128 * sizeof(float));
+    for (int k = 0; k < K; ++k) {
+        kb.t[k * 128 + threadIdx.x] = INFINITY;
+        kb.i[k * 128 + threadIdx.x] = 0x7fffffff;
+    }
+    kb.rt = INFINITY;
+    kb.ri = 0x7fffffff;
+    const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
+                                  1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
+                                  1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
+    const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);
+    const bool want = live && t_min < INFINITY;
+    if (n == 1) {
+        float t;
+        if (want) {
+            ++nprim;
+            if (hit_prim(rec, 0, O, v, t_min, poly, t, tcap)) heap_insert(kb, t, ids[0]);
+        }
+    } else if (n > 1) {
+        const unsigned all = __ballot_sync(0xffffffffu, want);
+        unsigned mask = all;
+        int sp = 0;
+        const unsigned long long max_visits = 2ull * (unsigned long long)n + 64ull;
+        const float4 *np = reinterpret_cast<const float4 *>(nodes);
+        float4 lx = __ldg(np), ly = __ldg(np + 1), lz = __ldg(np + 2), hx = __ldg(np + 3), hy = __ldg(np + 4),
+               hz = __ldg(np + 5);
+        int4 ln = __ldg(reinterpret_cast<const int4 *>(np + 6)), pd = __ldg(reinterpret_cast<const int4 *>(np + 7));
+        while (mask) {
+            if (++nnode > max_visits) {
+                if (lane == 0) atomicOr(status, ERR_INDEX);
+                break;
+            }
+            const bool in = (mask >> lane) & 1u;
+            const float bk = fminf(kb.rt, tcap);
+            const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
+            const float clx[4] = {lx.x, lx.y, lx.z, lx.w}, cly[4] = {ly.x, ly.y, ly.z, ly.w},
+                        clz[4] = {lz.x, lz.y, lz.z, lz.w}, chx[4] = {hx.x, hx.y, hx.z, hx.w},
+                        chy[4] = {hy.x, hy.y, hy.z, hy.w}, chz[4] = {hz.x, hz.y, hz.z, hz.w};
+            const int link[4] = {ln.x, ln.y, ln.z, ln.w};
+            bool h[4];
+            unsigned key[4], im[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float tn = 0.0f;
+                h[c] = in && link[c] != NODE4_EMPTY && slab4(clx[c], cly[c], clz[c], chx[c], chy[c], chz[c], O, iv, tlo, thi, tn);
+                const bool ic = h[c] && link[c] >= 0;  // empty slots never have h set
+                im[c] = __ballot_sync(0xffffffffu, ic);
+                // nearest entry among the lanes entering the child (entries are >= 0 here, so their bit
+                // patterns order like the values)
+                key[c] = im[c] ? __reduce_min_sync(0xffffffffu, ic ? __float_as_uint(fmaxf(tn, 0.0f)) : 0xffffffffu)
+                               : 0xffffffffu;
+            }
+            // order the entered internal children by key: push all but the nearest, farthest first
+            int order[4] = {0, 1, 2, 3};
+#pragma unroll
+            for (int a = 0; a < 3; ++a)
+#pragma unroll
+                for (int b = 0; b < 3 - a; ++b)
+                    if (key[order[b]] < key[order[b + 1]]) {  // descending: farthest first
+                        const int tmp = order[b];
+                        order[b] = order[b + 1];
+                        order[b + 1] = tmp;
+                    }
+            int next = -1;
+            unsigned nmask = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int c = order[q];
+                if (!im[c]) continue;
+                if (next >= 0) {  // the previous nearer candidate goes to the stack
+                    if (sp < STACK4) {
+                        if (lane == 0) s_node[wib][sp] = next;
+                        ++sp;
+                    } else if (lane == 0) {
+                        atomicOr(status, ERR_STACK);
+                    }
+                }
+                next = link[c];
+                nmask = im[c];
+            }
+            if (next < 0) {
+                __syncwarp();
+                if (sp > 0) {
+                    --sp;
+                    next = s_node[wib][sp];
+                    nmask = all;
+                }
+            }
+            const int4 pid = pd;
+            float4 nlx = lx, nly = ly, nlz = lz, nhx = hx, nhy = hy, nhz = hz;
+            int4 nln = ln, npd = pd;
+            if (next >= 0) {
+                const float4 *q = reinterpret_cast<const float4 *>(nodes + next);
+                nlx = __ldg(q); nly = __ldg(q + 1); nlz = __ldg(q + 2);
+                nhx = __ldg(q + 3); nhy = __ldg(q + 4); nhz = __ldg(q + 5);
+                nln = __ldg(reinterpret_cast<const int4 *>(q + 6));
+                npd = __ldg(reinterpret_cast<const int4 *>(q + 7));
+            }
+            const int pids[4] = {pid.x, pid.y, pid.z, pid.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (link[c] < 0 && h[c]) {
+                    float t;
+                    ++nprim;
+                    if (hit_prim(rec, ~link[c], O, v, t_min, poly, t, bk)) {
+                        const int p = pids[c];
+                        if (t < kb.rt || (t == kb.rt && p < kb.ri)) heap_insert(kb, t, p);
+                    }
+                }
+            }
+            __syncwarp();
+            if (next < 0) break;
+            mask = nmask;
+            lx = nlx; ly = nly; lz = nlz; hx = nhx; hy = nhy; hz = nhz;
+            ln = nln; pd = npd;
+        }
+    }
+    if (live) {  // heap sort: the largest key leaves first, into the last slot
+        for (int k = K - 1; k >= 0; --k) {
+            const float tk = kb.t[threadIdx.x];
+            const int ik = kb.i[threadIdx.x];
+            const bool valid = ik != 0x7fffffff;
+            t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
+            idx_out[(size_t)k * stride + j] = valid ? ik : -1;
+            if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
+        }
+    }
+    if (STATS) {
+        for (int o = 16; o > 0; o >>= 1) nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
+        if (lane == 0 && (nprim | nnode)) {
+            atomicAdd(stats + ST_PRIM_TESTS, nprim);
+            atomicAdd(stats + ST_NODES, nnode);
+        }
+    }
+}
+
 // Group-per-ray traversal for sparse late passes: once few rays remain, a pass lasts as long as its
 // longest single walk, so G lanes (a quarter, half or whole warp) split one ray's walk.  Each step the
 // group pops up to G nodes of its shared stack, tests their children and pushes the entered internal
@@ -743,6 +914,16 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
     // Internal passes keep each ray's K_PASS-entry buffer as a shared-memory heap (FLARE_TRACE_HEAP=0: the
     // sorted register buffer of the packet kernel).
     static const bool heap = getenv_int("FLARE_TRACE_HEAP", 1) != 0;
+    if (k == K_PASS && K_PASS != K_HITS && heap && r->nodes4) {
+        const size_t smem = (size_t)K_PASS * 128 * 8;
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap4_kernel<true, K_PASS>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        trace_heap4_kernel<true, K_PASS><<<(count + B - 1) / B, B, smem, st>>>(
+            O, v, t_min, ray_ids, count, r->nodes4, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+            r->dstatus, r->dstats, t_max);
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    }
     if (k == K_PASS && K_PASS != K_HITS && heap) {
         const size_t smem = (size_t)K_PASS * 128 * 8;
         FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap_kernel<true, K_PASS>,

@@ -390,3 +390,42 @@ print("OK")
     env = dict(os.environ, FLARE_BVH="ploc", PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
     out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and "OK" in out.stdout, out.stdout[-2000:] + out.stderr[-2000:]
+
+
+@pytest.mark.parametrize("bvh4", ["1", "0"])
+def test_training_passes_heap_traversal(bvh4):
+    """Training passes through the block-wide heap traversal (4-wide or binary hierarchy), which full-size
+    passes use: FLARE_TRACE_G32_MAX=0 turns off the warp-per-ray kernel that passes of <= 16384 rays take.
+    Both environment switches are read once per process, hence the child process."""
+    import subprocess
+    import sys
+    code = r"""
+import numpy as np, torch
+from flare_b200.renderer import CPyOptiXFLARERenderer
+from flare_b200.scene import camera_rays, make_scene
+from oracle import oracle
+sc = make_scene(200000, 1)
+O, v = camera_rays(48, 48, 40.0, eye=(0.0, 0.0, 1.8))
+R = O.shape[0]
+r = CPyOptiXFLARERenderer(8, 11.3449, R)
+g = sc.to("cuda")
+geo = (g.m, g.s, g.q, g.RGBA, g.k)
+r.SetGeometry(*[t.contiguous() for t in g.activated()])
+csr = oracle.hit_lists(r.frames().cpu().numpy(), O, v)
+ta, tb = 0.1, 1000.0
+ra, rb = -(ta * tb) / (tb - ta), tb / (tb - ta)
+ref = oracle.forward(sc, O, v, csr, "training", base=True, bg=(0.1, 0.2, 0.3), T_thr=1e-4, reg_a=ra, reg_b=rb)
+z = lambda *s: torch.zeros(*s, device="cuda")
+bitmap, dacc, nacc, dai = z(R, 3), z(R, 4), z(R, 4), z(R, 2)
+r.Forward_training_base(O.cuda(), v.cuda(), bitmap, 0.1, 0.2, 0.3, *geo, 1e-4, dacc, ra, rb, dai, z(R, 3), nacc)
+st = r.stats()
+assert st["passes"] >= 2, st
+assert st["hits_composited"] == ref["total_hits"], (st, ref["total_hits"])
+assert np.abs(bitmap.cpu().numpy() - ref["rgb"]).max() < 1e-3
+print("OK")
+"""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, FLARE_BVH4=bvh4, FLARE_TRACE_G32_MAX="0",
+               PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0 and "OK" in out.stdout, out.stdout[-2000:] + out.stderr[-2000:]
