@@ -26,6 +26,7 @@ constexpr int TRACE_STACK = 64;
 constexpr int LUT_PRIV_FLOATS = 26368;  // 4 * 13154 / 2 = 26308, rounded up to 128 floats
 // Packed per-primitive gradient of the decoder backward: dm 3, ds 2, dq 4, dRGB 3, dA 1, dk 1, 2 pad.
 constexpr int PGRAD_FLOATS = 16;
+constexpr int PROW_FLOATS = PGRAD_FLOATS + 64;  // decoder backward row per primitive: packed gradients | layer-1 deltas
 constexpr float LUT_SCALE = 0.29689279887990428378374198030042f;  // 1/sqrt(11.3449)
 
 // Internal forward mode of the secondary-ray (viewer) path: colour of a shadowed hit times the shadow

@@ -49,7 +49,7 @@ struct flare_renderer {
     float *dw = nullptr;      // dense weight-gradient accumulators (see shade.cu)
     float *gscale = nullptr;  // backward gradient scale (1 float)
     float *dfeat_priv = nullptr;  // per-CTA LUT gradient copies (2 * num_sms * LUT_PRIV_FLOATS floats)
-    float *pgrad = nullptr;       // packed per-primitive gradients of the decoder backward (PGRAD_FLOATS each)
+    float *pgrad = nullptr;       // per-primitive rows of the decoder backward (PROW_FLOATS each)
     size_t pgrad_cap = 0;         // primitives pgrad holds
     void *vw_buf = nullptr;       // secondary-ray path: ray sets and per-generation scratch (viewer.cu)
     int vw_sets = 0;

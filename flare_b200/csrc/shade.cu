@@ -120,7 +120,7 @@ struct BwdIO {
     const float *surface_normal;
     float lambda_depth, reg_a, reg_b, lambda_normal;
     const float *gscale;  // [0] = scale applied to delta3 operands
-    int vec4;             // dq and dcond are 16-byte aligned: use vector reductions
+    int vec4;             // dq is 16-byte aligned: use vector reductions
 };
 
 // dst[0..3] += (a, b, c, d): one vector reduction when 16-byte aligned, else four scalar atomics.
@@ -758,11 +758,12 @@ __device__ __forceinline__ void bulk_red_add_f32(float *gdst, const float *ssrc,
 __device__ __forceinline__ void wait_bulk_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void wait_bulk_done() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Per-lane staging rows: 96 descriptor-gradient floats then the PGRAD_FLOATS packed primitive gradients
+// Per-lane staging rows: the PGRAD_FLOATS packed primitive gradients then the 64 layer-1 deltas
 // (row stride an odd number of 16-byte chunks so the lanes' vector stores hit distinct banks); warps 0-1
 // use the X tile, 2-3 the H1-H2 tiles, which are free between the last tensor-core stage of a slot and the
 // next slot's X row.
-constexpr int DC_ROW = 116;
+constexpr int DC_ROW = 84;
+static_assert(DC_ROW >= PROW_FLOATS && (DC_ROW / 4) % 2 == 1, "staging row");
 static_assert(2 * 32 * DC_ROW * 4 <= 32768, "two warps' rows fit the X tile and the H1-H2 tiles");
 
 template <bool DEC>
@@ -1037,7 +1038,10 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     tmem_ld16(mm.tmem + lane + 16 * cb, gv);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) gv[e] *= hd1[16 * cb + e];
+                    for (int e = 0; e < 16; ++e) {
+                        gv[e] *= hd1[16 * cb + e];
+                        hd1[16 * cb + e] = gv[e];  // delta1, kept for the per-primitive row
+                    }
                     write_row16_split(h1t, h2t, tid, 2 * cb, gv);
                 }
                 fence_async_smem();
@@ -1045,23 +1049,16 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 __syncthreads();
                 if (tid == 0) {
                     tc_fence_after();
-                    // dX[:, 0:16) = d1 W1[:, 0:16) ; dX[:, 32:128) -> TMEM columns [16, 112)
+                    // dX[:, 0:16) = d1 W1[:, 0:16) (hi and lo parts of d1).  The descriptor columns of dX
+                    // are not formed per hit: dX[:, 32:128) = d1 W1[:, 32:128) is linear in d1, so each
+                    // primitive's sum of d1 is reduced instead and multiplied by W1 once per primitive.
                     for (int ks = 0; ks < 4; ++ks)
                         mma_f16_ss(mm.tmem, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
                                    sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1),
                                    ks > 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        mma_f16_ss(mm.tmem + 16, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
-                                   sdesc(smem_u32(smem + SM_W1) + 4 * 1024 + ks * 256, 128, 1024),
-                                   idesc_f16(128, 96, 0, 1), ks > 0);
-                    // + the lo part of delta1
-                    for (int ks = 0; ks < 4; ++ks)
                         mma_f16_ss(mm.tmem, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
                                    sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1), 1);
-                    for (int ks = 0; ks < 4; ++ks)
-                        mma_f16_ss(mm.tmem + 16, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
-                                   sdesc(smem_u32(smem + SM_W1) + 4 * 1024 + ks * 256, 128, 1024),
-                                   idesc_f16(128, 96, 0, 1), 1);
                     // dW1 += d1^T X : M=64, N=128, K=128 hits (hi and lo parts of d1)
                     for (int ks = 0; ks < 8; ++ks)
                         mma_f16_ss(dwreg, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
@@ -1082,32 +1079,8 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     mma_commit(mm.mbar);
                 }
                 mma_wait(mm);
-                // descriptor gradient: dX[32:128) at TMEM columns [16, 112) -> this lane's staging row ->
-                // one bulk reduction into the primitive's row (vector reductions when not 16-byte aligned)
-                float *dc = bo.dcond + (size_t)idc * 96;
                 const int wid = tid >> 5;
                 float *dcrow = reinterpret_cast<float *>(wid < 2 ? xt : h1t) + ((wid & 1) * 32 + (tid & 31)) * DC_ROW;
-#pragma unroll
-                for (int b = 0; b < 6; ++b) {
-                    float v16[16];
-                    tmem_ld16(mm.tmem + lane + 16 + 16 * b, v16);
-                    tmem_wait_ld();
-                    if (valid) {
-#pragma unroll
-                        for (int e = 0; e < 16; e += 4) {
-                            if (bo.vec4)
-                                *reinterpret_cast<float4 *>(dcrow + 16 * b + e) =
-                                    make_float4(v16[e] * ginv, v16[e + 1] * ginv, v16[e + 2] * ginv, v16[e + 3] * ginv);
-                            else
-                                red_add4(dc + 16 * b + e, false, v16[e] * ginv, v16[e + 1] * ginv, v16[e + 2] * ginv,
-                                         v16[e + 3] * ginv);
-                        }
-                    }
-                }
-                if (valid && bo.vec4) {
-                    fence_async_smem();
-                    bulk_red_add_f32(dc, dcrow, 96 * 4);
-                }
                 float dx16[16];
                 tmem_ld16(mm.tmem + lane, dx16);
                 tmem_wait_ld();
@@ -1137,18 +1110,21 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 gw += dxw;
                 if (valid) {
                     geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
-                    if (bo.vec4) {  // the packed row rides behind the descriptor row in the staging row
+                    // this hit's row [packed primitive gradients | delta1] -> one bulk reduction
 #pragma unroll
-                        for (int e = 0; e < PG_N; e += 2)
-                            *reinterpret_cast<float2 *>(dcrow + 96 + e) = make_float2(pg[e], pg[e + 1]);
-                        *reinterpret_cast<float2 *>(dcrow + 96 + PG_N) = make_float2(0.0f, 0.0f);
-                        fence_async_smem();
-                        bulk_red_add_f32(bo.pgrad + (size_t)ind * PGRAD_FLOATS, dcrow + 96, PGRAD_FLOATS * 4);
-                    } else {
-                        flush_prim_direct(bo, ind, pg);
-                    }
+                    for (int e = 0; e < PG_N; e += 2)
+                        *reinterpret_cast<float2 *>(dcrow + e) = make_float2(pg[e], pg[e + 1]);
+#pragma unroll
+                    for (int e = PG_N; e < PGRAD_FLOATS; e += 2)
+                        *reinterpret_cast<float2 *>(dcrow + e) = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int e = 0; e < 64; e += 4)
+                        *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + e) =
+                            make_float4(hd1[e] * ginv, hd1[e + 1] * ginv, hd1[e + 2] * ginv, hd1[e + 3] * ginv);
+                    fence_async_smem();
+                    bulk_red_add_f32(bo.pgrad + (size_t)ind * PROW_FLOATS, dcrow, PROW_FLOATS * 4);
                 }
-                if (valid && bo.vec4) wait_bulk_read();  // the staging rows are overwritten next slot
+                if (valid) wait_bulk_read();  // the staging rows are overwritten next slot
                 tc_fence_before();
                 __syncthreads();
                 if (tid == 0) s_first = 0;
@@ -1269,21 +1245,54 @@ __global__ void reduce_lut_kernel(const float *__restrict__ priv, int copies, fl
     dfeat[i] += acc;
 }
 
-// Adds the packed per-primitive gradients of the decoder backward into the caller's arrays.
-__global__ void scatter_pgrad_kernel(const float4 *__restrict__ pg, int n, float *dm, float *ds, float *dq, float *dRGB,
-                                     float *dA, float *dk) {
-    int p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= n) return;
-    const float4 a = pg[4 * (size_t)p], b = pg[4 * (size_t)p + 1], c = pg[4 * (size_t)p + 2], d = pg[4 * (size_t)p + 3];
-    if (a.x == 0.0f && a.y == 0.0f && a.z == 0.0f && a.w == 0.0f && b.x == 0.0f && b.y == 0.0f && b.z == 0.0f &&
-        b.w == 0.0f && c.x == 0.0f && c.y == 0.0f && c.z == 0.0f && c.w == 0.0f && d.x == 0.0f && d.y == 0.0f)
-        return;  // not hit
-    dm[3 * (size_t)p] += a.x; dm[3 * (size_t)p + 1] += a.y; dm[3 * (size_t)p + 2] += a.z;
-    ds[2 * (size_t)p] += a.w; ds[2 * (size_t)p + 1] += b.x;
-    dq[4 * (size_t)p] += b.y; dq[4 * (size_t)p + 1] += b.z; dq[4 * (size_t)p + 2] += b.w; dq[4 * (size_t)p + 3] += c.x;
-    dRGB[3 * (size_t)p] += c.y; dRGB[3 * (size_t)p + 1] += c.z; dRGB[3 * (size_t)p + 2] += c.w;
-    dA[p] += d.x;
-    dk[p] += d.y;
+// Adds the per-primitive rows of the decoder backward into the caller's arrays, one warp per primitive:
+// the packed gradients (layout PG_*) directly, and the descriptor gradient dcond = W1[:, 32:128)^T d1,
+// d1 being the primitive's summed layer-1 deltas (W1 (64, 128) f16, row = output).
+__global__ void __launch_bounds__(256) scatter_prow_kernel(const float *__restrict__ prow, int n,
+                                                           const __half *__restrict__ A1, float *dm, float *ds,
+                                                           float *dq, float *dRGB, float *dA, float *dk,
+                                                           float *dcond) {
+    __shared__ float w[64 * 96];  // w[k * 96 + j] = W1[k][32 + j]
+    __shared__ float rows[8][64];
+    for (int i = threadIdx.x; i < 64 * 96; i += blockDim.x)
+        w[i] = __half2float(A1[(i / 96) * 128 + 32 + i % 96]);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int nw = gridDim.x * 8;
+    for (int p = blockIdx.x * 8 + wib; p < n; p += nw) {
+        const float *r = prow + (size_t)p * PROW_FLOATS;
+        const float a = r[lane], b = r[32 + lane], c = lane < 16 ? r[64 + lane] : 0.0f;
+        if (!__any_sync(0xffffffffu, a != 0.0f || b != 0.0f || c != 0.0f)) continue;  // not hit
+        if (lane < PG_N) {
+            float *dst;
+            if (lane < PG_S) dst = dm + 3 * (size_t)p + lane;
+            else if (lane < PG_Q) dst = ds + 2 * (size_t)p + (lane - PG_S);
+            else if (lane < PG_RGB) dst = dq + 4 * (size_t)p + (lane - PG_Q);
+            else if (lane < PG_A) dst = dRGB + 3 * (size_t)p + (lane - PG_RGB);
+            else if (lane == PG_A) dst = dA + p;
+            else dst = dk + p;
+            *dst += a;
+        }
+        if (dcond) {
+            if (lane >= PGRAD_FLOATS) rows[wib][lane - PGRAD_FLOATS] = a;
+            rows[wib][16 + lane] = b;
+            if (lane < 16) rows[wib][48 + lane] = c;
+            __syncwarp();
+            float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f;
+#pragma unroll 8
+            for (int k = 0; k < 64; ++k) {
+                const float d = rows[wib][k];
+                o0 = __fmaf_rn(w[k * 96 + lane], d, o0);
+                o1 = __fmaf_rn(w[k * 96 + 32 + lane], d, o1);
+                o2 = __fmaf_rn(w[k * 96 + 64 + lane], d, o2);
+            }
+            __syncwarp();
+            float *dc = dcond + (size_t)p * 96;
+            dc[lane] += o0;
+            dc[32 + lane] += o1;
+            dc[64 + lane] += o2;
+        }
+    }
 }
 
 // Adds the dense MLP gradients into row 0 of the reference's fragment-layout buffers
@@ -1623,11 +1632,11 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         cudaFree(r->pgrad);
         r->pgrad = nullptr;
         r->pgrad_cap = 0;
-        FLARE_CUDA_TRY(cudaMalloc(&r->pgrad, (size_t)sc->n * PGRAD_FLOATS * sizeof(float)));
+        FLARE_CUDA_TRY(cudaMalloc(&r->pgrad, (size_t)sc->n * PROW_FLOATS * sizeof(float)));
         r->pgrad_cap = sc->n;
     }
     bo.pgrad = r->pgrad;
-    bo.vec4 = ((reinterpret_cast<uintptr_t>(a->dL_dq) | reinterpret_cast<uintptr_t>(dec ? a->dL_dcond : a->dL_dq)) & 15) == 0;
+    bo.vec4 = (reinterpret_cast<uintptr_t>(a->dL_dq) & 15) == 0;
     init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
     {
@@ -1641,7 +1650,7 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
                                                                              r->gscale);
         grad_scale_finish_kernel<<<1, 1, 0, st>>>(r->gscale);
         FLARE_CUDA_TRY(cudaMemsetAsync(r->dfeat_priv, 0, (size_t)r->num_sms * 2 * LUT_PRIV_STRIDE * sizeof(float), st));
-        if (sc->n > 0) FLARE_CUDA_TRY(cudaMemsetAsync(r->pgrad, 0, (size_t)sc->n * PGRAD_FLOATS * sizeof(float), st));
+        if (sc->n > 0) FLARE_CUDA_TRY(cudaMemsetAsync(r->pgrad, 0, (size_t)sc->n * PROW_FLOATS * sizeof(float), st));
         FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             SM_BWD_BYTES));
     }
@@ -1696,9 +1705,9 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         pack_dw_kernel<<<32, 256, 0, st>>>(r->dw, a->dL_dw1, a->dL_db1, a->dL_dw2, a->dL_db2, a->dL_dw3, a->dL_db3);
         reduce_lut_kernel<<<(LUT + 255) / 256, 256, 0, st>>>(r->dfeat_priv, r->num_sms * 2, a->dL_dfeatures);
         if (sc->n > 0)
-            scatter_pgrad_kernel<<<(sc->n + 255) / 256, 256, 0, st>>>(reinterpret_cast<const float4 *>(r->pgrad), sc->n,
-                                                                      a->dL_dm, a->dL_ds, a->dL_dq, a->dL_dRGB,
-                                                                      a->dL_dA, a->dL_dk);
+            scatter_prow_kernel<<<std::min((sc->n + 7) / 8, r->num_sms * 8), 256, 0, st>>>(
+                r->pgrad, sc->n, static_cast<const __half *>(sc->A1), a->dL_dm, a->dL_ds, a->dL_dq, a->dL_dRGB,
+                a->dL_dA, a->dL_dk, a->dL_dcond);
         FLARE_CUDA_TRY(cudaGetLastError());
     }
     return FLARE_OK;
