@@ -47,10 +47,11 @@ B_HIT_FWD = 56 + 192             # primitive record + fp16 descriptor row
 B_HIT_BWD = 56 + 192 + 440       # re-read + gradient writes (14 geometry + 96 descriptor fp32)
 B_RAY_FWD, B_RAY_BWD = 44, 24
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per traversal launch, measured with a one-pass
-# ncu capture of the config-3 bench command (mean of six launches: passes 0, 1 and 2 of two views).  Most
-# of it is the 48-slot (t, index) hit lists each pass writes (8 B per slot); node and record fetches are
+# ncu capture of the config-3 bench command (mean of the eight traversal launches captured: passes 0-3 of
+# one view, block-wide heap kernel for passes 0-2 and the warp-per-ray kernel for pass 3, twice).  Most of
+# it is the 42-slot (t, index) hit lists each pass writes (8 B per slot); node and record fetches are
 # mostly L2 hits.  Only valid for the config-3 workload; other workloads report null.
-TRACE_DRAM_BYTES_PER_LAUNCH = {3: 585.2e6}
+TRACE_DRAM_BYTES_PER_LAUNCH = {3: 398.4e6}
 FLOP_HIT_FWD = 2 * (128 * 64 + 64 * 64 + 64 * 4)
 
 
