@@ -122,11 +122,11 @@ def dist_setup(args):
     return world, rank, local
 
 
-def build_workload(cfg, world, rank, device, seed=0):
+def build_workload(cfg, world, rank, device, seed=0, decoder="lut_pe"):
     from flare_b200.dp import Shard, shard_rays
     from flare_b200.scene import camera_rays, make_scene, sphere_eye
     c = CONFIGS[cfg]
-    scene = make_scene(c["n_prims"], seed).to(device)
+    scene = make_scene(c["n_prims"], seed, decoder=decoder).to(device)
     W, H, V = c["width"], c["height"], c["views"]
     host = []
     for view, lo, cnt in shard_rays(V, W * H, world, rank):
@@ -301,10 +301,11 @@ def measure_viewer(cfg, scene, sh, steps, warmup, device, world):
                 kernels={k: dict(ms=v[0], launches=v[1]) for k, v in kt.items() if v[1]})
 
 
-def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
+def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True, decoder="lut_pe"):
     from flare_b200.dp import TrainStep
     from flare_b200.renderer import CPyOptiXFLARERenderer
-    scene, shards, host, total_rays = build_workload(cfg, world, rank, device)
+    scene, shards, host, total_rays = build_workload(cfg, world, rank, device, decoder=decoder)
+    tag = "" if decoder == "lut_pe" else f", {decoder} decoder"
     if CONFIGS[cfg]["mode"] == "viewer":
         return measure_viewer(cfg, scene, shards[0], steps, warmup, device, world)
     max_rays = max(s.O.shape[0] for s in shards)
@@ -349,7 +350,7 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     traversals = kt.get("trace", (0.0, 0))[1] / max(step.fwd_passes, 1)  # 1.0 when the backward replays
     dom, per = kernel_roofline(kt, hits, my_rays, hbm, traversals)
     step_bytes = hits * (2 * B_HIT_TRACE + B_HIT_FWD + B_HIT_BWD) + my_rays * (B_RAY_FWD + B_RAY_BWD)
-    out = dict(workload=f"config {cfg} training step", ms_per_step=ms, value=total_rays / (ms * 1e-3) / 1e6,
+    out = dict(workload=f"config {cfg} training step{tag}", ms_per_step=ms, value=total_rays / (ms * 1e-3) / 1e6,
                hits_per_ray=hits / max(my_rays, 1), hits=hits, kernels=per, dominant=dom, step_algo_bytes=step_bytes,
                traversals_per_step=traversals,
                kernel_times={k: v for k, v in kt.items()}, grad_allreduce_bytes=step.grads.nbytes)
@@ -365,6 +366,10 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     out["e2e"] = dict(value=total_rays / (ms_e2e * 1e-3) / 1e6, unit="Mrays/s",
                       h2d_bytes_per_step=sum(sum(t.numel() * t.element_size() for t in h) for h in host),
                       d2h_bytes_per_step=4)
+    out["_r"] = r
+    out["shards"] = [(s.O.shape[0]) for s in shards]
+    if decoder != "lut_pe":  # the reference's optimizer groups describe its own decoder's W1 blocks
+        return out
     # the optimizer step after the backward (reference train.py:833-953): one fused Adam launch over the
     # 16 parameter groups; not part of the headline step (the reference's metric is fwd + bwd)
     from flare_b200.optim import ModelOptimizer
@@ -382,8 +387,6 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True):
     obytes = elems * 28 + half * 2  # p, m, v read + write, g read; fp16 mirrors written
     out["optimizer_step"] = dict(ms=ms_opt, elements=elems, algo_bytes=obytes,
                                  achieved_gbs=obytes / (ms_opt * 1e-3) / 1e9)
-    out["_r"] = r
-    out["shards"] = [(s.O.shape[0]) for s in shards]
     return out
 
 
@@ -414,12 +417,14 @@ def main():
     clocks = cs.summary()
     extras = {}
     if world == 1 and not args.no_extra:
-        for c in ([2] if main_cfg == 3 else []) + [1, 4]:
-            e = measure_config(c, 1, 0, max(2, args.steps), 2, device, hbm)
+        runs = [(2, "lut_pe")] if main_cfg == 3 else []
+        runs += [(1, "lut_pe"), (4, "lut_pe"), (2, "grid_sh")]
+        for c, dk in runs:
+            e = measure_config(c, 1, 0, max(2, args.steps), 2, device, hbm, decoder=dk)
             e.pop("_r", None)
-            extras[f"config{c}"] = {k: v for k, v in e.items() if k in ("workload", "ms_per_step", "value",
-                                                                          "hits_per_ray", "dominant", "kernels",
-                                                                          "traversal_passes", "optimizer_step")}
+            extras[f"config{c}" + ("" if dk == "lut_pe" else f"_{dk}")] = {
+                k: v for k, v in e.items() if k in ("workload", "ms_per_step", "value", "hits_per_ray", "dominant",
+                                                    "kernels", "traversal_passes", "optimizer_step")}
     if rank != 0:
         dist.destroy_process_group()
         return

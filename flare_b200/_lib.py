@@ -20,7 +20,7 @@ FWD_TRAINING, FWD_INFERENCE, FWD_INFERENCE_GEOMETRY, FWD_PCA, FWD_MEDIAN = range
 class Scene(ctypes.Structure):
     _fields_ = [("m", vp), ("s", vp), ("q", vp), ("RGBA", vp), ("k", vp), ("n", ctypes.c_int),
                 ("cond", vp), ("features", vp), ("A1", vp), ("A2", vp), ("A3", vp),
-                ("b1", vp), ("b2", vp), ("b3", vp)]
+                ("b1", vp), ("b2", vp), ("b3", vp), ("decoder", ctypes.c_int)]
 
 
 class ForwardArgs(ctypes.Structure):

@@ -248,6 +248,8 @@ static int check_scene(flare_renderer *r, const flare_scene *sc, const char *who
     CHECK_ARG(sc, "%s: scene is NULL", who);
     CHECK_ARG(sc->n == r->n, "%s: scene has %d primitives but the last SetGeometry had %d", who, sc->n, r->n);
     CHECK_ARG(sc->n == 0 || (sc->m && sc->s && sc->q && sc->RGBA && sc->k), "%s: NULL primitive tensor", who);
+    CHECK_ARG(sc->decoder == FLARE_DECODER_LUT_PE || sc->decoder == FLARE_DECODER_GRID_SH,
+              "%s: unknown decoder kind %d", who, sc->decoder);
     if (sc->cond)
         CHECK_ARG(sc->features && sc->A1 && sc->A2 && sc->A3 && sc->b1 && sc->b2 && sc->b3,
                   "%s: decoder tensors missing", who);

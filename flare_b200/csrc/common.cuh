@@ -23,7 +23,10 @@ constexpr int MAX_SIDES = 64;
 constexpr int TRACE_STACK = 64;
 // Per-CTA LUT-gradient copy in the backward, "pair-major": 4 floats per cell hold the (x, y) gradient of
 // the cell and of its right neighbour, so the two corners of a bilinear row are one 16-byte reduction.
-constexpr int LUT_PRIV_FLOATS = 26368;  // 4 * 13154 / 2 = 26308, rounded up to 128 floats
+constexpr int GRID_FEATS = FLARE_GRID_SIZE;   // 16502 floats (decoder 1's dense 8-level grid)
+// per-CTA pair-major feature-gradient copy: 4 floats per cell of the larger table (4 * 16502 / 2 = 33004),
+// rounded up to 128 floats
+constexpr int LUT_PRIV_FLOATS = 33024;
 // Packed per-primitive gradient of the decoder backward: dm 3, ds 2, dq 4, dRGB 3, dA 1, dk 1, 2 pad.
 constexpr int PGRAD_FLOATS = 16;
 constexpr int PROW_FLOATS = PGRAD_FLOATS + 64;  // decoder backward row per primitive: packed gradients | layer-1 deltas

@@ -140,11 +140,23 @@ struct Geo {
     float r2, pk, r2k, G;    // r^2, (r^2)^(kappa-1), (r^2)^kappa, exp(-r2k / (2 kappa))
 };
 
+template <int DK>
+struct Dec;
+template <>
+struct Dec<0> {
+    static constexpr int LEVELS = 4, COND = 96, COND_CHUNKS = 12, FEATS = LUT;
+};
+template <>
+struct Dec<1> {
+    static constexpr int LEVELS = 8, COND = 32, COND_CHUNKS = 4, FEATS = GRID_FEATS;
+};
+
 __device__ __forceinline__ void prefetch_l2(const void *p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // Pulls the per-primitive rows the next hit slot reads into L2 while the current slot's tiles run.
+template <int DK = 0>
 __device__ __forceinline__ void prefetch_hit(const SceneP &sc, int idx) {
     if (idx < 0) return;
     prefetch_l2(sc.m + 3 * (size_t)idx);
@@ -152,10 +164,10 @@ __device__ __forceinline__ void prefetch_hit(const SceneP &sc, int idx) {
     prefetch_l2(sc.q + 4 * (size_t)idx);
     prefetch_l2(sc.k + idx);
     prefetch_l2(sc.RGBA + 4 * (size_t)idx);
-    if (sc.cond) {  // the 192-byte descriptor row spans two 128-byte lines
-        const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)idx * 12);
+    if (sc.cond) {  // the 192-byte descriptor row spans two 128-byte lines (the 64-byte one, one)
+        const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)idx * Dec<DK>::COND_CHUNKS);
         prefetch_l2(c);
-        prefetch_l2(c + 128);
+        if (DK == 0) prefetch_l2(c + 128);
     }
 }
 
@@ -204,18 +216,46 @@ __device__ __forceinline__ float hswish_d(float y) {
 }
 __device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
+// Decoder kinds (flare_scene::decoder).  Both fill the same 128-wide f16 input row and run the same
+// 128->64->64->16 tensor-core tiles; they differ in the row's contents, the hidden activation and the
+// colour head.
+//   0 (FLARE_DECODER_LUT_PE, the reference's compiled decoder, Forward_training.cu:198-373):
+//     [LUT 4 levels x 2 | sin/cos view encoding 24 | descriptor 96], Hardswish, colour = relu(y) * RGB.
+//   1 (FLARE_DECODER_GRID_SH, the BASELINE config-0 encoder): [dense grid 8 levels x 2 | real spherical
+//     harmonics of the view direction, degree 3 (16) | descriptor 32 | zeros 64], ReLU, colour =
+//     sigmoid(y) * RGB.  W1 keeps its (64, 128) shape; columns 64..127 meet zero inputs.
+template <int DK>
+__device__ __forceinline__ float act(float y) {
+    return DK ? fmaxf(y, 0.0f) : hswish(y);
+}
+template <int DK>
+__device__ __forceinline__ float act_d(float y) {
+    return DK ? (y > 0.0f ? 1.0f : 0.0f) : hswish_d(y);
+}
+
 // LUT levels (reference Forward_training.cu:240-263): res {16,25,40,64}, float2 offsets {0,256,881,2481}
 __device__ __forceinline__ int lut_res(int l) { return l == 0 ? 16 : (l == 1 ? 25 : (l == 2 ? 40 : 64)); }
 __device__ __forceinline__ int lut_off(int l) { return l == 0 ? 0 : (l == 1 ? 256 : (l == 2 ? 881 : 2481)); }
+
+// Dense grid levels of decoder 1: resolution floor(4 * 1.5^l) vertices per side, l = 0..7 (every level
+// has fewer than 2^16 vertices, so the multiresolution table addresses them row-major, unhashed), float2
+// offsets = running sums of res^2.
+__device__ __forceinline__ int grid_res(int l) {
+    return l < 4 ? (l == 0 ? 4 : (l == 1 ? 6 : (l == 2 ? 9 : 13))) : (l == 4 ? 20 : (l == 5 ? 30 : (l == 6 ? 45 : 68)));
+}
+__device__ __forceinline__ int grid_off(int l) {
+    return l < 4 ? (l == 0 ? 0 : (l == 1 ? 16 : (l == 2 ? 52 : 133))) : (l == 4 ? 302 : (l == 5 ? 702 : (l == 6 ? 1602 : 3627)));
+}
 
 struct LutCell {
     int i00;        // float2 index of the (x0, y0) corner
     int R;
     float fx, fy;
 };
+template <int DK = 0>
 __device__ __forceinline__ LutCell lut_cell(int l, float cu, float cw) {
     LutCell c;
-    int R = lut_res(l);
+    int R = DK ? grid_res(l) : lut_res(l);
     float xs = __saturatef((cu + 1.0f) * 0.5f), ys = __saturatef((cw + 1.0f) * 0.5f);
     float scale = (float)R - 1.0f;
     float px = xs * scale, py = ys * scale;
@@ -223,12 +263,35 @@ __device__ __forceinline__ LutCell lut_cell(int l, float cu, float cw) {
     c.fx = px - (float)ix;
     c.fy = py - (float)iy;
     c.R = R;
-    c.i00 = lut_off(l) + iy * R + ix;
+    c.i00 = (DK ? grid_off(l) : lut_off(l)) + iy * R + ix;
     return c;
+}
+
+// Real spherical harmonics of a unit direction, degrees 0..3 (16 values, the standard real basis with
+// the Condon-Shortley phase, as the Instant-NGP / 3DGS view encodings use).
+__device__ __forceinline__ void sh_deg3(float x, float y, float z, float out[16]) {
+    const float xx = x * x, yy = y * y, zz = z * z;
+    out[0] = 0.28209479177387814f;
+    out[1] = -0.48860251190291987f * y;
+    out[2] = 0.48860251190291987f * z;
+    out[3] = -0.48860251190291987f * x;
+    out[4] = 1.0925484305920792f * x * y;
+    out[5] = -1.0925484305920792f * y * z;
+    out[6] = 0.94617469575755997f * zz - 0.31539156525251999f;
+    out[7] = -1.0925484305920792f * x * z;
+    out[8] = 0.54627421529603959f * (xx - yy);
+    out[9] = 0.59004358992664352f * y * (-3.0f * xx + yy);
+    out[10] = 2.8906114426405538f * x * y * z;
+    out[11] = 0.45704579946446572f * y * (1.0f - 5.0f * zz);
+    out[12] = 0.3731763325901154f * z * (5.0f * zz - 3.0f);
+    out[13] = 0.45704579946446572f * x * (1.0f - 5.0f * zz);
+    out[14] = 1.4453057213202769f * z * (xx - yy);
+    out[15] = 0.59004358992664352f * x * (-xx + 3.0f * yy);
 }
 
 // Writes one 128-wide f16 decoder input row into a K-major interleaved tile (row r).  Returns the
 // LUT values through lut8 for reuse.
+template <int DK = 0>
 __device__ __forceinline__ void write_x_row(char *tile, int r, const float2 *lut2, const SceneP &sc, int idx,
                                             float cu, float cw, float3 v, bool zero) {
     uint4 *T = reinterpret_cast<uint4 *>(tile);
@@ -237,6 +300,41 @@ __device__ __forceinline__ void write_x_row(char *tile, int r, const float2 *lut
         for (int kc = 0; kc < 16; ++kc) T[kc * 128 + r] = make_uint4(0, 0, 0, 0);
         return;
     }
+    if constexpr (DK == 1) {
+        // chunks 0-1: grid levels 0-7 (level l -> elements 2l, 2l+1); one chunk at a time keeps the
+        // corner loads in flight to 16 float2
+#pragma unroll 1
+        for (int hc = 0; hc < 2; ++hc) {
+            __half2 h[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                LutCell c = lut_cell<1>(4 * hc + q, cu, cw);
+                float2 f00 = lut2[c.i00], f10 = lut2[c.i00 + 1], f01 = lut2[c.i00 + c.R], f11 = lut2[c.i00 + c.R + 1];
+                float ux = c.fx, vx = 1.0f - ux;
+                float r0x = __fmaf_rn(f00.x, vx, f10.x * ux), r0y = __fmaf_rn(f00.y, vx, f10.y * ux);
+                float r1x = __fmaf_rn(f01.x, vx, f11.x * ux), r1y = __fmaf_rn(f01.y, vx, f11.y * ux);
+                float uy = c.fy, vy = 1.0f - uy;
+                h[q] = __floats2half2_rn(__fmaf_rn(r0x, vy, r1x * uy), __fmaf_rn(r0y, vy, r1y * uy));
+            }
+            T[hc * 128 + r] = *reinterpret_cast<uint4 *>(h);
+        }
+        // chunks 2-3: spherical harmonics of v
+        float shv[16];
+        sh_deg3(v.x, v.y, v.z, shv);
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+            __half2 h[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(shv[8 * hc + 2 * q], shv[8 * hc + 2 * q + 1]);
+            T[(2 + hc) * 128 + r] = *reinterpret_cast<uint4 *>(h);
+        }
+        // chunks 4-7: the 32-wide descriptor row; 8-15: zero
+        const uint4 *cr = sc.cond + (size_t)idx * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) T[(4 + j) * 128 + r] = __ldg(cr + j);
+#pragma unroll
+        for (int kc = 8; kc < 16; ++kc) T[kc * 128 + r] = make_uint4(0, 0, 0, 0);
+    } else {
     // chunk 0: LUT (level l -> elements 2l, 2l+1)
     __half2 h[4];
 #pragma unroll
@@ -267,6 +365,7 @@ __device__ __forceinline__ void write_x_row(char *tile, int r, const float2 *lut
     const uint4 *cr = sc.cond + (size_t)idx * 12;
 #pragma unroll
     for (int j = 0; j < 12; ++j) T[(4 + j) * 128 + r] = __ldg(cr + j);
+    }
 }
 
 // Writes 64 f16 values (8 chunks) as row r of a K-major interleaved 128-row tile.
@@ -392,6 +491,7 @@ __device__ __forceinline__ void tmem_row64(uint32_t tmem, int col, float *y) {
 // Leaves h1/h2 in `tile` at the end (h2), returns y[0..3] (+ b3) for this thread's row.
 // If keep_d1 is non-null the layer-1 Hardswish derivatives are stored there (fp32).  Layer 2 accumulates
 // into TMEM columns [y2col, y2col+64): the backward keeps them there to form delta2 exactly.
+template <int DK = 0>
 __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char *h1_tile, char *h2_tile, Mma &mm,
                                                  float *y4, float *keep_d1, int y2col) {
     const float *bias = reinterpret_cast<const float *>(smem + SM_BIAS);
@@ -408,11 +508,11 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
     for (int o = 0; o < 64; o += 2) {
         const float z0 = y[o] + bias[o], z1 = y[o + 1] + bias[o + 1];
         if (keep_d1) {
-            keep_d1[o] = hswish_d(z0);
-            keep_d1[o + 1] = hswish_d(z1);
+            keep_d1[o] = act_d<DK>(z0);
+            keep_d1[o + 1] = act_d<DK>(z1);
         }
-        y[o] = hswish(z0);
-        y[o + 1] = hswish(z1);
+        y[o] = act<DK>(z0);
+        y[o + 1] = act<DK>(z1);
     }
     write_row64(h1_tile, r, y);
     fence_async_smem();
@@ -428,8 +528,8 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
 #pragma unroll
     for (int o = 0; o < 64; o += 2) {
         const float z0 = y[o] + bias[64 + o], z1 = y[o + 1] + bias[64 + o + 1];
-        y[o] = hswish(z0);
-        y[o + 1] = hswish(z1);
+        y[o] = act<DK>(z0);
+        y[o + 1] = act<DK>(z1);
     }
     write_row64(h2_tile, r, y);
     fence_async_smem();
@@ -456,7 +556,7 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
 // ================================================================================================
 // Forward
 // ================================================================================================
-template <bool DEC, int MODE>
+template <bool DEC, int MODE, int DK>
 __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, FwdOut fo) {
     extern __shared__ __align__(1024) char smem[];
     __shared__ int s_abort;
@@ -527,11 +627,11 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             float y4[4] = {0, 0, 0, 0};
             if (DEC) {
                 if (!__syncthreads_or(valid)) continue;  // uniform: no ray of this CTA needs slot h
-                write_x_row(tile, tid, lut2, sc, idc, g.u * LUT_SCALE, g.w * LUT_SCALE, v, !valid);
+                write_x_row<DK>(tile, tid, lut2, sc, idc, g.u * LUT_SCALE, g.w * LUT_SCALE, v, !valid);
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
-                mlp_forward_tile(smem, tile, tile, tile, mm, y4, nullptr, 0);
+                mlp_forward_tile<DK>(smem, tile, tile, tile, mm, y4, nullptr, 0);
                 __syncthreads();
                 if (s_abort) goto done;
             }
@@ -552,9 +652,9 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                 }
                 float c0 = rgba.x, c1 = rgba.y, c2 = rgba.z;
                 if (DEC) {
-                    c0 *= fmaxf(y4[0], 0.0f);
-                    c1 *= fmaxf(y4[1], 0.0f);
-                    c2 *= fmaxf(y4[2], 0.0f);
+                    c0 *= DK ? sigm(y4[0]) : fmaxf(y4[0], 0.0f);
+                    c1 *= DK ? sigm(y4[1]) : fmaxf(y4[1], 0.0f);
+                    c2 *= DK ? sigm(y4[2]) : fmaxf(y4[2], 0.0f);
                 }
                 if (MODE == FWD_VIEWER && fo.shadow[(size_t)h * pp.count + slot]) {
                     c0 *= fo.shadow_mult;
@@ -766,7 +866,7 @@ constexpr int DC_ROW = 84;
 static_assert(DC_ROW >= PROW_FLOATS && (DC_ROW / 4) % 2 == 1, "staging row");
 static_assert(2 * 32 * DC_ROW * 4 <= 32768, "two warps' rows fit the X tile and the H1-H2 tiles");
 
-template <bool DEC>
+template <bool DEC, int DK>
 __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, BwdIO bo) {
     extern __shared__ __align__(1024) char smem[];
     __shared__ int s_abort;
@@ -870,12 +970,12 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             for (int e = 0; e < PG_N; ++e) pg[e] = 0.0f;
             const bool any_valid = DEC ? __syncthreads_or(valid) : false;  // uniform
             if (DEC && any_valid) {
-                write_x_row(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
+                write_x_row<DK>(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
-                mlp_forward_tile(smem, xt, h1t, h2t, mm, y4, hd1, 64);
-                prefetch_hit(sc, ind_next);
+                mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, hd1, 64);
+                prefetch_hit<DK>(sc, ind_next);
                 __syncthreads();
                 if (s_abort) goto done;
             }
@@ -888,8 +988,13 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 if (DEC) {
 #pragma unroll
                     for (int c = 0; c < 3; ++c) {
-                        z3[c] = fmaxf(y4[c], 0.0f);
-                        dz3[c] = y4[c] >= 0.0f ? 1.0f : 0.0f;
+                        if (DK) {
+                            z3[c] = sigm(y4[c]);
+                            dz3[c] = z3[c] * (1.0f - z3[c]);
+                        } else {
+                            z3[c] = fmaxf(y4[c], 0.0f);
+                            dz3[c] = y4[c] >= 0.0f ? 1.0f : 0.0f;
+                        }
                     }
                     sig_y = sigm(y4[3]);
                     dz3[3] = sig_y * (1.0f - sig_y);
@@ -1004,7 +1109,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                         tmem_ld16(mm.tmem + lane + 64 + 16 * cb, yv);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) gv[e] *= hswish_d(yv[e] + b2s[16 * cb + e]);
+                        for (int e = 0; e < 16; ++e) gv[e] *= act_d<DK>(yv[e] + b2s[16 * cb + e]);
                         write_row16(h2t, tid, 2 * cb, gv);
                     }
                 }
@@ -1081,16 +1186,27 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 mma_wait(mm);
                 const int wid = tid >> 5;
                 float *dcrow = reinterpret_cast<float *>(wid < 2 ? xt : h1t) + ((wid & 1) * 32 + (tid & 31)) * DC_ROW;
+                if (valid) {  // delta1 into the staging row now (the tiles are free), ahead of the LUT work
+#pragma unroll
+                    for (int e = 0; e < 64; e += 4)
+                        *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + e) =
+                            make_float4(hd1[e] * ginv, hd1[e + 1] * ginv, hd1[e + 2] * ginv, hd1[e + 3] * ginv);
+                }
                 float dx16[16];
                 tmem_ld16(mm.tmem + lane, dx16);
                 tmem_wait_ld();
                 float dxu = 0.0f, dxw = 0.0f;
                 if (valid) {
                     // LUT: dX element 2l+f -> feature gradients of level l and the coordinate gradient
+                    // groups of four levels, one group at a time (decoder 1 has two)
+#pragma unroll 1
+                    for (int hb = 0; hb < Dec<DK>::LEVELS / 4; ++hb)
 #pragma unroll
-                    for (int l = 0; l < 4; ++l) {
-                        LutCell c = lut_cell(l, cu, cw);
-                        float dx_ = dx16[2 * l] * ginv, dy_ = dx16[2 * l + 1] * ginv;
+                    for (int lq = 0; lq < 4; ++lq) {
+                        const int l = 4 * hb + lq;
+                        LutCell c = lut_cell<DK>(l, cu, cw);
+                        float dx_ = (hb ? dx16[8 + 2 * lq] : dx16[2 * lq]) * ginv,
+                              dy_ = (hb ? dx16[9 + 2 * lq] : dx16[2 * lq + 1]) * ginv;
                         float ux = c.fx, vx = 1.0f - ux, uy = c.fy, vy = 1.0f - uy;
                         float2 f00 = __ldg(lut2 + c.i00), f10 = __ldg(lut2 + c.i00 + 1),
                                f01 = __ldg(lut2 + c.i00 + c.R), f11 = __ldg(lut2 + c.i00 + c.R + 1);
@@ -1117,10 +1233,6 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
 #pragma unroll
                     for (int e = PG_N; e < PGRAD_FLOATS; e += 2)
                         *reinterpret_cast<float2 *>(dcrow + e) = make_float2(0.0f, 0.0f);
-#pragma unroll
-                    for (int e = 0; e < 64; e += 4)
-                        *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + e) =
-                            make_float4(hd1[e] * ginv, hd1[e + 1] * ginv, hd1[e + 2] * ginv, hd1[e + 3] * ginv);
                     fence_async_smem();
                     bulk_red_add_f32(bo.pgrad + (size_t)ind * PROW_FLOATS, dcrow, PROW_FLOATS * 4);
                 }
@@ -1232,9 +1344,9 @@ __global__ void grad_scale_finish_kernel(float *scale) {
 // Sums the per-CTA pair-major copies: feature i of cell c = i / 2 is the cell's own slot plus the
 // right-neighbour slot of cell c - 1 (a bilinear row never spans two rows or levels, so that slot is
 // zero wherever c - 1 is not a left corner of c).
-__global__ void reduce_lut_kernel(const float *__restrict__ priv, int copies, float *__restrict__ dfeat) {
+__global__ void reduce_lut_kernel(const float *__restrict__ priv, int copies, float *__restrict__ dfeat, int nfeat) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= LUT) return;
+    if (i >= nfeat) return;
     const int cell = i >> 1, f = i & 1;
     float acc = 0.0f;
     for (int c = 0; c < copies; ++c) {
@@ -1247,15 +1359,16 @@ __global__ void reduce_lut_kernel(const float *__restrict__ priv, int copies, fl
 
 // Adds the per-primitive rows of the decoder backward into the caller's arrays, one warp per primitive:
 // the packed gradients (layout PG_*) directly, and the descriptor gradient dcond = W1[:, 32:128)^T d1,
-// d1 being the primitive's summed layer-1 deltas (W1 (64, 128) f16, row = output).
+// d1 being the primitive's summed layer-1 deltas (W1 (64, 128) f16, row = output); cdim = the descriptor
+// width (96 or 32).
 __global__ void __launch_bounds__(256) scatter_prow_kernel(const float *__restrict__ prow, int n,
                                                            const __half *__restrict__ A1, float *dm, float *ds,
                                                            float *dq, float *dRGB, float *dA, float *dk,
-                                                           float *dcond) {
-    __shared__ float w[64 * 96];  // w[k * 96 + j] = W1[k][32 + j]
+                                                           float *dcond, int cdim) {
+    __shared__ float w[64 * 96];  // w[k * 96 + j] = W1[k][32 + j], j < cdim
     __shared__ float rows[8][64];
     for (int i = threadIdx.x; i < 64 * 96; i += blockDim.x)
-        w[i] = __half2float(A1[(i / 96) * 128 + 32 + i % 96]);
+        w[i] = (i % 96) < cdim ? __half2float(A1[(i / 96) * 128 + 32 + i % 96]) : 0.0f;
     __syncthreads();
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int nw = gridDim.x * 8;
@@ -1287,10 +1400,12 @@ __global__ void __launch_bounds__(256) scatter_prow_kernel(const float *__restri
                 o2 = __fmaf_rn(w[k * 96 + 64 + lane], d, o2);
             }
             __syncwarp();
-            float *dc = dcond + (size_t)p * 96;
+            float *dc = dcond + (size_t)p * cdim;
             dc[lane] += o0;
-            dc[32 + lane] += o1;
-            dc[64 + lane] += o2;
+            if (cdim == 96) {
+                dc[32 + lane] += o1;
+                dc[64 + lane] += o2;
+            }
         }
     }
 }
@@ -1345,9 +1460,9 @@ static SceneP scene_params(const flare_scene *sc, const float *override_colors) 
     return p;
 }
 
-template <bool DEC, int MODE>
+template <bool DEC, int MODE, int DK = 0>
 static int launch_fwd(flare_renderer *r, const SceneP &sp, const PassP &pp, const FwdOut &fo, cudaStream_t st) {
-    auto kern = shade_fwd_kernel<DEC, MODE>;
+    auto kern = shade_fwd_kernel<DEC, MODE, DK>;
     int smem = DEC ? SM_FWD_BYTES : 0;
     if (DEC) FLARE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int chunks = (pp.count + 127) / 128;
@@ -1357,15 +1472,15 @@ static int launch_fwd(flare_renderer *r, const SceneP &sp, const PassP &pp, cons
     return FLARE_OK;
 }
 
-template <bool DEC>
+template <bool DEC, int DK = 0>
 static int launch_fwd_mode(flare_renderer *r, int mode, const SceneP &sp, const PassP &pp, const FwdOut &fo,
                            cudaStream_t st) {
     switch (mode) {
-        case FLARE_FWD_TRAINING: return launch_fwd<DEC, FLARE_FWD_TRAINING>(r, sp, pp, fo, st);
-        case FLARE_FWD_INFERENCE: return launch_fwd<DEC, FLARE_FWD_INFERENCE>(r, sp, pp, fo, st);
-        case FLARE_FWD_INFERENCE_GEOMETRY: return launch_fwd<DEC, FLARE_FWD_INFERENCE_GEOMETRY>(r, sp, pp, fo, st);
-        case FLARE_FWD_PCA: return launch_fwd<DEC, FLARE_FWD_PCA>(r, sp, pp, fo, st);
-        case FLARE_FWD_MEDIAN: return launch_fwd<DEC, FLARE_FWD_MEDIAN>(r, sp, pp, fo, st);
+        case FLARE_FWD_TRAINING: return launch_fwd<DEC, FLARE_FWD_TRAINING, DK>(r, sp, pp, fo, st);
+        case FLARE_FWD_INFERENCE: return launch_fwd<DEC, FLARE_FWD_INFERENCE, DK>(r, sp, pp, fo, st);
+        case FLARE_FWD_INFERENCE_GEOMETRY: return launch_fwd<DEC, FLARE_FWD_INFERENCE_GEOMETRY, DK>(r, sp, pp, fo, st);
+        case FLARE_FWD_PCA: return launch_fwd<DEC, FLARE_FWD_PCA, DK>(r, sp, pp, fo, st);
+        case FLARE_FWD_MEDIAN: return launch_fwd<DEC, FLARE_FWD_MEDIAN, DK>(r, sp, pp, fo, st);
     }
     set_error("unknown forward mode %d", mode);
     return FLARE_E_INVALID;
@@ -1428,8 +1543,8 @@ static int input_checksum(flare_renderer *r, const flare_scene *sc, const float 
     add(sc->RGBA, n * 16);
     add(sc->k, n * 4);
     if (sc->cond) {
-        add(sc->cond, n * 192);
-        add(sc->features, (size_t)LUT * 4);
+        add(sc->cond, n * (sc->decoder ? Dec<1>::COND : Dec<0>::COND) * 2);
+        add(sc->features, (size_t)(sc->decoder ? Dec<1>::FEATS : Dec<0>::FEATS) * 4);
         add(sc->A1, 64 * 128 * 2);
         add(sc->A2, 64 * 64 * 2);
         add(sc->A3, 16 * 64 * 2);
@@ -1607,8 +1722,9 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
             pp.count = count;
                 pp.hit_t = ht;
             pp.hit_idx = hi;
-            return dec ? launch_fwd_mode<true>(r, a->mode, sp, pp, fo, st)
-                       : launch_fwd_mode<false>(r, a->mode, sp, pp, fo, st);
+            if (!dec) return launch_fwd_mode<false>(r, a->mode, sp, pp, fo, st);
+            return sc->decoder ? launch_fwd_mode<true, 1>(r, a->mode, sp, pp, fo, st)
+                               : launch_fwd_mode<true, 0>(r, a->mode, sp, pp, fo, st);
         },
         cache);
 }
@@ -1651,7 +1767,9 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         grad_scale_finish_kernel<<<1, 1, 0, st>>>(r->gscale);
         FLARE_CUDA_TRY(cudaMemsetAsync(r->dfeat_priv, 0, (size_t)r->num_sms * 2 * LUT_PRIV_STRIDE * sizeof(float), st));
         if (sc->n > 0) FLARE_CUDA_TRY(cudaMemsetAsync(r->pgrad, 0, (size_t)sc->n * PROW_FLOATS * sizeof(float), st));
-        FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            SM_BWD_BYTES));
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             SM_BWD_BYTES));
     }
     PassP base = make_pass(r, a->O, a->v, a->bg[0], a->bg[1], a->bg[2], a->T_threshold);
@@ -1665,9 +1783,12 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         FLARE_CUDA_TRY(cudaMemsetAsync(pp.work, 0, sizeof(int), st));
         if (dec) {
             int grid = std::min(chunks, r->num_sms * 2);
-            shade_bwd_kernel<true><<<grid, 128, SM_BWD_BYTES, st>>>(sp, pp, bo);
+            if (sc->decoder)
+                shade_bwd_kernel<true, 1><<<grid, 128, SM_BWD_BYTES, st>>>(sp, pp, bo);
+            else
+                shade_bwd_kernel<true, 0><<<grid, 128, SM_BWD_BYTES, st>>>(sp, pp, bo);
         } else {
-            shade_bwd_kernel<false><<<chunks, 128, 0, st>>>(sp, pp, bo);
+            shade_bwd_kernel<false, 0><<<chunks, 128, 0, st>>>(sp, pp, bo);
         }
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
@@ -1703,11 +1824,12 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     if (e) return e;
     if (dec) {
         pack_dw_kernel<<<32, 256, 0, st>>>(r->dw, a->dL_dw1, a->dL_db1, a->dL_dw2, a->dL_db2, a->dL_dw3, a->dL_db3);
-        reduce_lut_kernel<<<(LUT + 255) / 256, 256, 0, st>>>(r->dfeat_priv, r->num_sms * 2, a->dL_dfeatures);
+        const int nfeat = sc->decoder ? Dec<1>::FEATS : Dec<0>::FEATS;
+        reduce_lut_kernel<<<(nfeat + 255) / 256, 256, 0, st>>>(r->dfeat_priv, r->num_sms * 2, a->dL_dfeatures, nfeat);
         if (sc->n > 0)
             scatter_prow_kernel<<<std::min((sc->n + 7) / 8, r->num_sms * 8), 256, 0, st>>>(
                 r->pgrad, sc->n, static_cast<const __half *>(sc->A1), a->dL_dm, a->dL_ds, a->dL_dq, a->dL_dRGB,
-                a->dL_dA, a->dL_dk, a->dL_dcond);
+                a->dL_dA, a->dL_dk, a->dL_dcond, sc->decoder ? Dec<1>::COND : Dec<0>::COND);
         FLARE_CUDA_TRY(cudaGetLastError());
     }
     return FLARE_OK;
@@ -1786,7 +1908,9 @@ int launch_shade_viewer(flare_renderer *r, const flare_scene *sc, const float *O
     fo.bitmap = bitmap;
     fo.shadow = shadow;
     fo.shadow_mult = shadow_mult;
-    return sc->cond ? launch_fwd<true, FWD_VIEWER>(r, sp, pp, fo, st) : launch_fwd<false, FWD_VIEWER>(r, sp, pp, fo, st);
+    if (!sc->cond) return launch_fwd<false, FWD_VIEWER>(r, sp, pp, fo, st);
+    return sc->decoder ? launch_fwd<true, FWD_VIEWER, 1>(r, sp, pp, fo, st)
+                       : launch_fwd<true, FWD_VIEWER, 0>(r, sp, pp, fo, st);
 }
 
 }  // namespace flare

@@ -43,10 +43,10 @@ def shard_rays(n_views: int, rays_per_view: int, world: int, rank: int):
 
 
 # gradient tensors of one step, in the order they sit in the flat buffer: name -> shape (N = primitives)
-def grad_layout(n: int, decoder: bool):
+def grad_layout(n: int, decoder: bool, cond_dim: int = 96, n_features: int = 13154):
     lay = [("loss", (1,)), ("RGB", (n, 3)), ("A", (n, 1)), ("k", (n, 1)), ("m", (n, 3)), ("s", (n, 2)), ("q", (n, 4))]
     if decoder:
-        lay += [("cond", (n, 96)), ("features", (13154,)), ("w3", (1, 512)), ("b3", (1, 64)), ("w2", (1, 4096)),
+        lay += [("cond", (n, cond_dim)), ("features", (n_features,)), ("w3", (1, 512)), ("b3", (1, 64)), ("w2", (1, 4096)),
                 ("b2", (1, 512)), ("w1", (1, 8192)), ("b1", (1, 512))]
     return lay
 
@@ -56,8 +56,8 @@ class GradBuffer:
 
     ALIGN = 16  # floats: every segment starts on a 64-byte boundary (the kernels use vector reductions)
 
-    def __init__(self, n: int, decoder: bool, device):
-        self.layout = grad_layout(n, decoder)
+    def __init__(self, n: int, decoder: bool, device, cond_dim: int = 96, n_features: int = 13154):
+        self.layout = grad_layout(n, decoder, cond_dim, n_features)
         offs, off = [], 0
         for _, shape in self.layout:
             offs.append(off)
@@ -106,7 +106,7 @@ class TrainStep:
         self.lambda_normal = lambda_normal
         self.group = group
         dev = scene.m.device
-        self.grads = GradBuffer(scene.n, decoder, dev)
+        self.grads = GradBuffer(scene.n, decoder, dev, scene.cond.shape[1], scene.features.numel())
         self.buf = []
         for sh in shards:
             R = sh.O.shape[0]

@@ -25,6 +25,20 @@ from . import _lib
 
 F32, F16, I32 = torch.float32, torch.float16, torch.int32
 
+# decoder kind -> (descriptor width, feature-table floats): 0 = the reference's LUT / sin-cos / 96-wide
+# decoder, 1 = the dense-grid / spherical-harmonics / 32-wide variant (include/flare_b200.h)
+DECODER_LUT_PE, DECODER_GRID_SH = 0, 1
+DECODERS = {DECODER_LUT_PE: (96, 13154), DECODER_GRID_SH: (32, 16502)}
+
+
+def decoder_kind(cond) -> int:
+    """The decoder a descriptor tensor belongs to, from its width (96: LUT/PE, 32: grid/SH)."""
+    w = cond.shape[1] if cond.dim() == 2 else -1
+    for kind, (cdim, _) in DECODERS.items():
+        if w == cdim:
+            return kind
+    raise ValueError(f"conditioning_variable: shape {tuple(cond.shape)}, expected (N, 96) or (N, 32)")
+
 
 def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
@@ -89,10 +103,13 @@ class CPyOptiXFLARERenderer:
         sc = _lib.Scene(m=_ptr(m), s=_ptr(s), q=_ptr(q), RGBA=_ptr(RGBA), k=_ptr(kappa), n=n)
         if dec is not None:
             cond, feat, A1, b1, A2, b2, A3, b3 = dec
-            _need(cond, "conditioning_variable", F16, (n, 96), dv)
+            kind = decoder_kind(cond)
+            cdim, nfeat = DECODERS[kind]
+            _need(cond, "conditioning_variable", F16, (n, cdim), dv)
             _need(feat, "features", F32, None, dv)
-            if feat.numel() != 13154:
-                raise ValueError(f"features: {feat.numel()} elements, expected 13154")
+            if feat.numel() != nfeat:
+                raise ValueError(f"features: {feat.numel()} elements, expected {nfeat} for a {cdim}-wide descriptor")
+            sc.decoder = kind
             _need(A1, "A1", F16, (64, 128), dv)
             _need(A2, "A2", F16, (64, 64), dv)
             _need(A3, "A3", F16, (16, 64), dv)
@@ -267,10 +284,11 @@ class CPyOptiXFLARERenderer:
                 _need(t, nm, F32, None, dv)
                 if t.dim() != 2 or t.shape[1] != w or t.shape[0] < 1:
                     raise ValueError(f"{nm}: shape {tuple(t.shape)}, expected (rows, {w})")
-            _need(dcond, "dL_d_conditioning", F32, (n, 96), dv)
+            cdim, nfeat = DECODERS[sc.decoder]
+            _need(dcond, "dL_d_conditioning", F32, (n, cdim), dv)
             _need(dfeat, "dL_d_features", F32, None, dv)
-            if dfeat.numel() != 13154:
-                raise ValueError("dL_d_features: expected 13154 elements")
+            if dfeat.numel() != nfeat:
+                raise ValueError(f"dL_d_features: expected {nfeat} elements")
             a.dL_dw1, a.dL_db1, a.dL_dw2, a.dL_db2 = _ptr(dw1), _ptr(db1), _ptr(dw2), _ptr(db2)
             a.dL_dw3, a.dL_db3, a.dL_dcond, a.dL_dfeatures = _ptr(dw3), _ptr(db3), _ptr(dcond), _ptr(dfeat)
         _lib.check(self._lib.flare_backward(self._h, ctypes.byref(sc), ctypes.byref(a), self._stream()), "Backward")

@@ -20,6 +20,11 @@ import torch
 
 LUT_SIZE = 13154
 COND_DIM = 96
+# the dense-grid / spherical-harmonics decoder variant (BASELINE config 0's encoder): 8 grid levels of
+# floor(4 * 1.5^l) vertices per side, 2 features each; 32-wide descriptor
+GRID_RES = tuple(int(4 * 1.5 ** l) for l in range(8))
+GRID_SIZE = 2 * sum(r * r for r in GRID_RES)
+GRID_COND_DIM = 32
 
 
 @dataclass
@@ -56,8 +61,14 @@ def _xavier(gen, fan_out, fan_in):
     return (torch.rand(fan_out, fan_in, generator=gen) * 2 - 1) * bound
 
 
-def make_scene(n: int, seed: int = 0, device="cpu", extent: float = 1.0) -> Scene:
-    """Primitives with the config-0 distributions (BASELINE configs reuse them at larger N)."""
+def make_scene(n: int, seed: int = 0, device="cpu", extent: float = 1.0, decoder: str = "lut_pe") -> Scene:
+    """Primitives with the config-0 distributions (BASELINE configs reuse them at larger N).
+
+    decoder "lut_pe": the reference's decoder (96-wide descriptor, 13154-float LUT, W1 over 128 inputs);
+    "grid_sh": the variant with a 32-wide descriptor, the 16502-float dense grid and W1 over its 64
+    inputs (Xavier over fan-in 64, stored in the left half of a (64, 128) tensor)."""
+    if decoder not in ("lut_pe", "grid_sh"):
+        raise ValueError(f"unknown decoder {decoder!r}")
     g = torch.Generator().manual_seed(seed)
     m = (torch.rand(n, 3, generator=g) * 2 - 1) * extent
     q = torch.randn(n, 4, generator=g)
@@ -68,9 +79,15 @@ def make_scene(n: int, seed: int = 0, device="cpu", extent: float = 1.0) -> Scen
     lo, hi = math.log(0.05 / 0.95), math.log(0.95 / 0.05)
     A = torch.empty(n, 1).uniform_(lo, hi, generator=g)     # sigmoid(A) in [0.05, 0.95]
     RGB = torch.rand(n, 3, generator=g)
-    cond = (torch.randn(n, COND_DIM, generator=g) * 0.1).to(torch.float16)
-    features = torch.empty(LUT_SIZE).uniform_(-0.1, 0.1, generator=g)
-    A1 = _xavier(g, 64, 128).to(torch.float16)
+    grid = decoder == "grid_sh"
+    cond = (torch.randn(n, GRID_COND_DIM if grid else COND_DIM, generator=g) * 0.1).to(torch.float16)
+    features = torch.empty(GRID_SIZE if grid else LUT_SIZE).uniform_(-0.1, 0.1, generator=g)
+    if grid:
+        A1 = torch.zeros(64, 128)
+        A1[:, :64] = _xavier(g, 64, 64)
+        A1 = A1.to(torch.float16)
+    else:
+        A1 = _xavier(g, 64, 128).to(torch.float16)
     A2 = _xavier(g, 64, 64).to(torch.float16)
     A3 = _xavier(g, 16, 64).to(torch.float16)
     z = lambda c: torch.zeros(c)

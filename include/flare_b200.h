@@ -35,6 +35,18 @@ extern "C" {
 #define FLARE_HIT_BUFFER_SIZE 16 /* k of the k-nearest hit buffer (reference constants.h:2) */
 #define FLARE_LUT_SIZE 13154     /* 2 * (16^2 + 25^2 + 40^2 + 64^2), reference Forward_training.cu:608 */
 #define FLARE_COND_DIM 96        /* reference Forward_training.cu:32 */
+#define FLARE_GRID_SIZE 16502    /* decoder 1: 2 * sum over l < 8 of floor(4 * 1.5^l)^2 */
+#define FLARE_GRID_COND_DIM 32   /* decoder 1 descriptor width */
+
+/* Decoder kinds (flare_scene.decoder).  FLARE_DECODER_LUT_PE is the reference's compiled decoder.
+   FLARE_DECODER_GRID_SH is BASELINE config 0's encoder: a dense multiresolution grid of the local (u, v)
+   coordinates (8 levels of floor(4 * 1.5^l) vertices per side, 2 features each, row-major like the
+   reference's MultiResolutionEncoding when a level fits its 2^16-entry table), the degree-3 real
+   spherical harmonics of the view direction, a 32-wide descriptor and ReLU hidden layers; colour =
+   sigmoid(y) * RGB.  Its layouts: cond (N,32) f16, features (16502) f32 (level-major, vertex row-major,
+   2 floats per vertex), A1 (64,128) f16 of which columns 64..127 are unused (their gradient is 0). */
+#define FLARE_DECODER_LUT_PE 0
+#define FLARE_DECODER_GRID_SH 1
 
 typedef struct flare_renderer flare_renderer;
 
@@ -100,6 +112,7 @@ typedef struct flare_scene {
     const float *features;                   /* (13154) f32 LUT */
     const void *A1, *A2, *A3;                /* f16 weights (64,128) (64,64) (16,64) */
     const float *b1, *b2, *b3;               /* f32 biases (64) (64) (16) */
+    int decoder;                             /* FLARE_DECODER_*; 0 unless the grid/SH variant is used */
 } flare_scene;
 
 typedef struct flare_forward_args {

@@ -16,6 +16,11 @@
  *   - inference geometry outputs and override colours                      Forward_inference.cu:866-917
  *   - median depth (last hit while T > 0.5)                                GetMedianDepth.cu:852-867
  *   - base model (constant colour, alpha = sigma(A) G(r))                  Forward_training_base.cu:21-257
+ * and the grid/SH decoder variant (decoder = 1, BASELINE config 0's encoder; no compiled reference code):
+ *   - 8-level dense grid of the same (u, w) coordinates, res floor(4 * 1.5^l), row-major vertices
+ *     (scripts/encoding_2d_benchmark.py:107-163 GridLevel / MultiResolutionEncoding with 2^16 entries)
+ *   - degree-3 real spherical harmonics of v (16), descriptor 32, zeros 64; ReLU hidden layers;
+ *     colour = RGB_base * sigmoid(y[0:3])
  * Transcendentals use libm (expf, logf, powf, sinf, cosf); the reference's fast intrinsics differ by a
  * few ulp, far inside the 1e-3 parity tolerance.
  */
@@ -35,6 +40,7 @@ typedef struct {
     const _Float16 *A1, *A2, *A3;
     const float *b1, *b2, *b3;
     const float *override_colors;
+    int decoder; /* 0: LUT / sin-cos / 96 (reference); 1: grid / SH / 32 */
 } oscene;
 
 typedef struct {
@@ -66,9 +72,14 @@ static inline float hswish(float y) {
 static const int lut_res[4] = {16, 25, 40, 64};
 static const int lut_off[4] = {0, 256, 881, 2481}; /* in float2 units */
 
-static void lut_encode(const float *features, float cu, float cw, float *out8) {
-    for (int l = 0; l < 4; ++l) {
-        int R = lut_res[l];
+static const int grid_res[8] = {4, 6, 9, 13, 20, 30, 45, 68};
+static const int grid_off[8] = {0, 16, 52, 133, 302, 702, 1602, 3627}; /* in float2 units */
+
+/* One bilinear lookup per level: nl levels of resolution res[l] at float2 offset off[l]. */
+static void grid_encode(const float *features, float cu, float cw, int nl, const int *res, const int *off,
+                        float *out) {
+    for (int l = 0; l < nl; ++l) {
+        int R = res[l];
         float xs = sat((cu + 1.0f) * 0.5f), ys = sat((cw + 1.0f) * 0.5f);
         float scale = (float)R - 1.0f;
         float px = xs * scale, py = ys * scale;
@@ -76,40 +87,80 @@ static void lut_encode(const float *features, float cu, float cw, float *out8) {
         if (ix > R - 2) ix = R - 2;
         if (iy > R - 2) iy = R - 2;
         float fx = px - (float)ix, fy = py - (float)iy;
-        const float *F = features + 2 * lut_off[l];
+        const float *F = features + 2 * off[l];
         for (int f = 0; f < 2; ++f) {
             float f00 = F[2 * (iy * R + ix) + f], f10 = F[2 * (iy * R + ix + 1) + f];
             float f01 = F[2 * ((iy + 1) * R + ix) + f], f11 = F[2 * ((iy + 1) * R + ix + 1) + f];
             float r0 = fmaf(f00, 1.0f - fx, f10 * fx);
             float r1 = fmaf(f01, 1.0f - fx, f11 * fx);
-            out8[2 * l + f] = fmaf(r0, 1.0f - fy, r1 * fy);
+            out[2 * l + f] = fmaf(r0, 1.0f - fy, r1 * fy);
         }
     }
 }
 
+static void lut_encode(const float *features, float cu, float cw, float *out8) {
+    grid_encode(features, cu, cw, 4, lut_res, lut_off, out8);
+}
+
+/* Real spherical harmonics of degrees 0..3 of a unit direction (standard real basis, Condon-Shortley
+   phase; the normalisation constants sqrt((2l+1)/(4 pi) (l-|m|)!/(l+|m|)!) times the usual factors). */
+static void sh_deg3(float x, float y, float z, float *o) {
+    float xx = x * x, yy = y * y, zz = z * z;
+    o[0] = 0.28209479177387814f;
+    o[1] = -0.48860251190291987f * y;
+    o[2] = 0.48860251190291987f * z;
+    o[3] = -0.48860251190291987f * x;
+    o[4] = 1.0925484305920792f * x * y;
+    o[5] = -1.0925484305920792f * y * z;
+    o[6] = 0.94617469575755997f * zz - 0.31539156525251999f;
+    o[7] = -1.0925484305920792f * x * z;
+    o[8] = 0.54627421529603959f * (xx - yy);
+    o[9] = 0.59004358992664352f * y * (-3.0f * xx + yy);
+    o[10] = 2.8906114426405538f * x * y * z;
+    o[11] = 0.45704579946446572f * y * (1.0f - 5.0f * zz);
+    o[12] = 0.3731763325901154f * z * (5.0f * zz - 3.0f);
+    o[13] = 0.45704579946446572f * x * (1.0f - 5.0f * zz);
+    o[14] = 1.4453057213202769f * z * (xx - yy);
+    o[15] = 0.59004358992664352f * x * (-xx + 3.0f * yy);
+}
+
+static inline float relu(float y) { return y > 0.0f ? y : 0.0f; }
+
 /* Decoder: returns y[0..3] (pre-activation outputs 0..3 of layer 3). */
 static void decode(const oscene *S, int idx, float cu, float cw, const float *v, float *y4) {
     float x[128];
-    float lut[8];
-    lut_encode(S->features, cu, cw, lut);
-    for (int i = 0; i < 8; ++i) x[i] = (float)(_Float16)lut[i];
-    for (int a = 0; a < 3; ++a)
-        for (int f = 0; f < 4; ++f) {
-            float arg = (float)M_PI * (float)(1 << f) * v[a];
-            x[8 + 8 * a + 2 * f] = (float)(_Float16)sinf(arg);
-            x[9 + 8 * a + 2 * f] = (float)(_Float16)cosf(arg);
+    if (S->decoder == 1) {
+        float enc[16], sh[16];
+        grid_encode(S->features, cu, cw, 8, grid_res, grid_off, enc);
+        sh_deg3(v[0], v[1], v[2], sh);
+        for (int i = 0; i < 16; ++i) {
+            x[i] = (float)(_Float16)enc[i];
+            x[16 + i] = (float)(_Float16)sh[i];
         }
-    for (int j = 0; j < 96; ++j) x[32 + j] = (float)S->cond[(long)idx * 96 + j];
+        for (int j = 0; j < 32; ++j) x[32 + j] = (float)S->cond[(long)idx * 32 + j];
+        for (int j = 64; j < 128; ++j) x[j] = 0.0f;
+    } else {
+        float lut[8];
+        lut_encode(S->features, cu, cw, lut);
+        for (int i = 0; i < 8; ++i) x[i] = (float)(_Float16)lut[i];
+        for (int a = 0; a < 3; ++a)
+            for (int f = 0; f < 4; ++f) {
+                float arg = (float)M_PI * (float)(1 << f) * v[a];
+                x[8 + 8 * a + 2 * f] = (float)(_Float16)sinf(arg);
+                x[9 + 8 * a + 2 * f] = (float)(_Float16)cosf(arg);
+            }
+        for (int j = 0; j < 96; ++j) x[32 + j] = (float)S->cond[(long)idx * 96 + j];
+    }
     float h1[64], h2[64];
     for (int o = 0; o < 64; ++o) {
         float acc = S->b1[o];
         for (int kk = 0; kk < 128; ++kk) acc = fmaf((float)S->A1[o * 128 + kk], x[kk], acc);
-        h1[o] = (float)(_Float16)hswish(acc);
+        h1[o] = (float)(_Float16)(S->decoder == 1 ? relu(acc) : hswish(acc));
     }
     for (int o = 0; o < 64; ++o) {
         float acc = S->b2[o];
         for (int kk = 0; kk < 64; ++kk) acc = fmaf((float)S->A2[o * 64 + kk], h1[kk], acc);
-        h2[o] = (float)(_Float16)hswish(acc);
+        h2[o] = (float)(_Float16)(S->decoder == 1 ? relu(acc) : hswish(acc));
     }
     for (int o = 0; o < 4; ++o) {
         float acc = S->b3[o];
@@ -162,7 +213,8 @@ static int shade_pass(const oscene *S, const oparams *P, const float *O, const f
             float y[4];
             decode(S, idx, u * LUT_SCALE, w * LUT_SCALE, v, y);
             sig_y = 1.0f / (1.0f + expf(-y[3]));
-            for (int c = 0; c < 3; ++c) crgb[c] = rgba[c] * (y[c] > 0.0f ? y[c] : 0.0f);
+            for (int c = 0; c < 3; ++c)
+                crgb[c] = rgba[c] * (S->decoder == 1 ? 1.0f / (1.0f + expf(-y[c])) : (y[c] > 0.0f ? y[c] : 0.0f));
         }
         if (P->mode == M_PCA && S->override_colors)
             for (int c = 0; c < 3; ++c) crgb[c] = S->override_colors[3 * idx + c];
@@ -227,9 +279,9 @@ long oracle_shade_csr(const float *m, const float *s, const float *q, const floa
                       const float *bg, float T_thr, float reg_a, float reg_b, const float *O, const float *v,
                       const float *surface_normal, int R, const long *off, const float *hit_t,
                       const int *hit_idx, float *rgb, float *dacc, float *nacc, float *normal, float *alpha,
-                      float *edn, float *med, float *Tout, int *nhits) {
+                      float *edn, float *med, float *Tout, int *nhits, int decoder) {
     oscene S = {m, s, q, RGBA, k, (const _Float16 *)cond, features, (const _Float16 *)A1, (const _Float16 *)A2,
-                (const _Float16 *)A3, b1, b2, b3, override_colors};
+                (const _Float16 *)A3, b1, b2, b3, override_colors, decoder};
     oparams P;
     P.mode = mode;
     P.bg[0] = bg[0]; P.bg[1] = bg[1]; P.bg[2] = bg[2];
@@ -273,6 +325,16 @@ void oracle_lut(const float *features, const float *cu, const float *cw, int n, 
     for (int i = 0; i < n; ++i) lut_encode(features, cu[i], cw[i], out + 8 * i);
 }
 
+/* The decoder-1 grid encoding alone: out (n, 16). */
+void oracle_grid(const float *features, const float *cu, const float *cw, int n, float *out) {
+    for (int i = 0; i < n; ++i) grid_encode(features, cu[i], cw[i], 8, grid_res, grid_off, out + 16 * i);
+}
+
+/* Degree-3 spherical harmonics of n directions: out (n, 16). */
+void oracle_sh(const float *v, int n, float *out) {
+    for (int i = 0; i < n; ++i) sh_deg3(v[3 * i], v[3 * i + 1], v[3 * i + 2], out + 16 * i);
+}
+
 /*
  * Secondary-ray compositing (viewer path, CPyOptiXFLAREVIEWERRenderer_CUDA_Forward.cu:695-897): the
  * hits of ray ray[j] are hit_t / hit_idx [off[j], off[j+1]) ascending; a shadowed hit (flag != 0)
@@ -284,9 +346,9 @@ long oracle_viewer_composite(const float *m, const float *s, const float *q, con
                              const float *b2, const void *A3, const float *b3, float T_thr, float shadow_mult,
                              const float *O, const float *v, const int *ray, int n, const long *off,
                              const float *hit_t, const int *hit_idx, const unsigned char *shadow, float *T_io,
-                             float *rgb_io) {
+                             float *rgb_io, int decoder) {
     oscene S = {m, s, q, RGBA, k, (const _Float16 *)cond, features, (const _Float16 *)A1, (const _Float16 *)A2,
-                (const _Float16 *)A3, b1, b2, b3, NULL};
+                (const _Float16 *)A3, b1, b2, b3, NULL, decoder};
     long total = 0;
 #pragma omp parallel for schedule(dynamic, 64) reduction(+ : total)
     for (int j = 0; j < n; ++j) {
@@ -323,7 +385,8 @@ long oracle_viewer_composite(const float *m, const float *s, const float *q, con
                 float y[4];
                 decode(&S, idx, u * LUT_SCALE, w * LUT_SCALE, d, y);
                 sig_y = 1.0f / (1.0f + expf(-y[3]));
-                for (int c = 0; c < 3; ++c) crgb[c] = rgba[c] * (y[c] > 0.0f ? y[c] : 0.0f);
+                for (int c = 0; c < 3; ++c)
+                crgb[c] = rgba[c] * (S.decoder == 1 ? 1.0f / (1.0f + expf(-y[c])) : (y[c] > 0.0f ? y[c] : 0.0f));
             }
             if (shadow[h])
                 for (int c = 0; c < 3; ++c) crgb[c] *= shadow_mult;

@@ -29,6 +29,9 @@ import torch
 LUT_SCALE = 0.29689279887990428378374198030042
 LUT_RES = (16, 25, 40, 64)
 LUT_OFF = (0, 256, 881, 2481)
+# grid/SH decoder variant: 8 dense levels of floor(4 * 1.5^l) vertices per side (float2 offsets)
+GRID_RES = (4, 6, 9, 13, 20, 30, 45, 68)
+GRID_OFF = (0, 16, 52, 133, 302, 702, 1602, 3627)
 
 
 def _st16(x):
@@ -39,19 +42,19 @@ def _hswish(y):
     return y * torch.clamp(y + 3.0, 0.0, 6.0) / 6.0
 
 
-def _lut(features, cu, cw):
-    """features (13154,) float64 requiring grad; cu, cw (H,) -> (H, 8)."""
+def _lut(features, cu, cw, res=LUT_RES, offs=LUT_OFF):
+    """features (13154,) float64 requiring grad; cu, cw (H,) -> (H, 2 * levels)."""
     F2 = features.view(-1, 2)
     outs = []
     xs = torch.clamp((cu + 1.0) * 0.5, 0.0, 1.0)
     ys = torch.clamp((cw + 1.0) * 0.5, 0.0, 1.0)
-    for l in range(4):
-        R = LUT_RES[l]
+    for l in range(len(res)):
+        R = res[l]
         px, py = xs * (R - 1), ys * (R - 1)
         ix = torch.clamp(torch.floor(px.detach()), max=R - 2).long()
         iy = torch.clamp(torch.floor(py.detach()), max=R - 2).long()
         fx, fy = px - ix, py - iy
-        base = LUT_OFF[l] + iy * R + ix
+        base = offs[l] + iy * R + ix
         f00, f10 = F2[base], F2[base + 1]
         f01, f11 = F2[base + R], F2[base + R + 1]
         r0 = f00 * (1 - fx)[:, None] + f10 * fx[:, None]
@@ -67,6 +70,20 @@ def _pe(v):
         for f in range(4):
             arg = math.pi * (2 ** f) * v[:, a]
             cols += [torch.sin(arg), torch.cos(arg)]
+    return torch.stack(cols, 1)
+
+
+def _sh(v):
+    """(H,3) unit directions -> (H,16) real spherical harmonics of degrees 0..3."""
+    x, y, z = v[:, 0], v[:, 1], v[:, 2]
+    xx, yy, zz = x * x, y * y, z * z
+    cols = [torch.full_like(x, 0.28209479177387814), -0.48860251190291987 * y, 0.48860251190291987 * z,
+            -0.48860251190291987 * x, 1.0925484305920792 * x * y, -1.0925484305920792 * y * z,
+            0.94617469575755997 * zz - 0.31539156525251999, -1.0925484305920792 * x * z,
+            0.54627421529603959 * (xx - yy), 0.59004358992664352 * y * (-3.0 * xx + yy),
+            2.8906114426405538 * x * y * z, 0.45704579946446572 * y * (1.0 - 5.0 * zz),
+            0.3731763325901154 * z * (5.0 * zz - 3.0), 0.45704579946446572 * x * (1.0 - 5.0 * zz),
+            1.4453057213202769 * z * (xx - yy), 0.59004358992664352 * x * (-xx + 3.0 * yy)]
     return torch.stack(cols, 1)
 
 
@@ -131,12 +148,20 @@ def gradients(scene, O, v, csr, nhits, dL_dI, base=False, bg=(0.0, 0.0, 0.0), re
         col = rgba[:, :3]
         alpha = torch.sigmoid(rgba[:, 3]) * G
     else:
-        x = torch.cat([_st16(_lut(P["features"], u * LUT_SCALE, w * LUT_SCALE)),
-                       _pe(vh).to(torch.float16).to(dt), P["cond"][idx_t]], 1)
-        h1 = _st16(_hswish(x @ P["A1"].T + P["b1"]))
-        h2 = _st16(_hswish(h1 @ P["A2"].T + P["b2"]))
+        grid = P["cond"].shape[1] == 32  # the grid/SH decoder variant
+        if grid:
+            x = torch.cat([_st16(_lut(P["features"], u * LUT_SCALE, w * LUT_SCALE, GRID_RES, GRID_OFF)),
+                           _sh(vh).to(torch.float16).to(dt), P["cond"][idx_t],
+                           torch.zeros(vh.shape[0], 64, dtype=dt)], 1)
+            act = torch.relu
+        else:
+            x = torch.cat([_st16(_lut(P["features"], u * LUT_SCALE, w * LUT_SCALE)),
+                           _pe(vh).to(torch.float16).to(dt), P["cond"][idx_t]], 1)
+            act = _hswish
+        h1 = _st16(act(x @ P["A1"].T + P["b1"]))
+        h2 = _st16(act(h1 @ P["A2"].T + P["b2"]))
         y = h2 @ P["A3"].T + P["b3"]
-        col = rgba[:, :3] * torch.relu(y[:, :3])
+        col = rgba[:, :3] * (torch.sigmoid(y[:, :3]) if grid else torch.relu(y[:, :3]))
         alpha = torch.sigmoid(rgba[:, 3]) * G * torch.sigmoid(y[:, 3])
     Hm = int(nhits.max()) if len(nhits) and nhits.max() > 0 else 1
     pos_t = torch.as_tensor(pos)

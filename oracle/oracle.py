@@ -134,6 +134,12 @@ def scene_arrays(scene):
     return out
 
 
+def decoder_of(S) -> int:
+    """Decoder kind of a scene's arrays: 1 (grid/SH) for a 32-wide descriptor, else 0 (LUT/PE)."""
+    c = S.get("cond")
+    return 1 if c is not None and c.ndim == 2 and c.shape[1] == 32 else 0
+
+
 def forward(scene, O, v, csr, mode="training", base=False, bg=(0.0, 0.0, 0.0), T_thr=1e-4, reg_a=0.0,
             reg_b=0.0, surface_normal=None, override_colors=None):
     """Forward over CSR hit lists.  Returns a dict of numpy outputs (rgb, dacc, nacc, normal, alpha,
@@ -160,7 +166,8 @@ def forward(scene, O, v, csr, mode="training", base=False, bg=(0.0, 0.0, 0.0), T
         G("cond"), G("features"), G("A1"), G("b1"), G("A2"), G("b2"), G("A3"), G("b3"), _p(oc), ctypes.c_int(MODES[mode]), _p(bgv),
         ctypes.c_float(T_thr), ctypes.c_float(reg_a), ctypes.c_float(reg_b), _p(O), _p(v), _p(sn),
         ctypes.c_int(R), _p(off), _p(tt), _p(ii), _p(out["rgb"]), _p(out["dacc"]), _p(out["nacc"]),
-        _p(out["normal"]), _p(out["alpha"]), _p(out["edn"]), _p(out["med"]), _p(out["T"]), _p(out["nhits"]))
+        _p(out["normal"]), _p(out["alpha"]), _p(out["edn"]), _p(out["med"]), _p(out["T"]), _p(out["nhits"]),
+        ctypes.c_int(decoder_of(S)))
     out["total_hits"] = int(total)
     return out
 
@@ -170,4 +177,20 @@ def lut(features, cu, cw):
     features, cu, cw = _f32(_np(features)), _f32(_np(cu)), _f32(_np(cw))
     out = np.zeros((cu.shape[0], 8), np.float32)
     lib().oracle_lut(_p(features), _p(cu), _p(cw), ctypes.c_int(cu.shape[0]), _p(out))
+    return out
+
+
+def grid(features, cu, cw):
+    """The 8-level dense-grid encoding of the grid/SH decoder variant -> (n, 16)."""
+    features, cu, cw = _f32(_np(features)), _f32(_np(cu)), _f32(_np(cw))
+    out = np.zeros((cu.shape[0], 16), np.float32)
+    lib().oracle_grid(_p(features), _p(cu), _p(cw), ctypes.c_int(cu.shape[0]), _p(out))
+    return out
+
+
+def sh(v):
+    """Degree-3 real spherical harmonics of unit directions (n, 3) -> (n, 16)."""
+    v = _f32(_np(v))
+    out = np.zeros((v.shape[0], 16), np.float32)
+    lib().oracle_sh(_p(v), ctypes.c_int(v.shape[0]), _p(out))
     return out

@@ -14,7 +14,7 @@ import ctypes
 
 import numpy as np
 
-from .oracle import K, _f32, _np, _p, lib, scene_arrays
+from .oracle import K, _f32, _np, _p, decoder_of, lib, scene_arrays
 
 
 def _lib():
@@ -113,7 +113,7 @@ def viewer_forward(frames, scene, spheres, materials, lights, O, v, bg=(0.0, 0.0
                 _p(S["m"]), _p(S["s"]), _p(S["q"]), _p(S["RGBA"]), _p(S["k"]), G("cond"), G("features"), G("A1"),
                 G("b1"), G("A2"), G("b2"), G("A3"), G("b3"), ctypes.c_float(T_thr), ctypes.c_float(shadow_mult),
                 _p(cur["O"]), _p(cur["v"]), _p(lst), ctypes.c_int(n0), _p(off), _p(tt), _p(ii), _p(flags),
-                _p(cur["T"]), _p(bitmap))
+                _p(cur["T"]), _p(bitmap), ctypes.c_int(decoder_of(S)))
             tsf = np.full(R, np.inf, np.float32)
             sidf = np.full(R, -1, np.int32)
             tsf[lst] = t_sph

@@ -159,3 +159,47 @@ def test_grad_oracle_finite_difference():
 
     fd = (loss(eps) - loss(-eps)) / (2 * eps)
     assert fd == pytest.approx(float(gr["m"][p, 0]), rel=2e-3, abs=1e-7)
+
+
+# ------------------------------------------------------------------ grid / spherical-harmonics decoder variant
+def test_grid_matches_reference_multiresolution_encoding():
+    """The variant's 8-level grid against the reference's MultiResolutionEncoding (golden vectors)."""
+    z = np.load(os.path.join(GOLD, "grid_multires.npz"))
+    from flare_b200.scene import GRID_RES, GRID_SIZE
+    assert tuple(z["resolutions"]) == GRID_RES and z["features"].size == GRID_SIZE
+    got = oracle.grid(z["features"], z["cu"], z["cw"])
+    # float32 coordinates against the reference's float64: the same < 1e-6 bound as the LUT pin
+    np.testing.assert_allclose(got, z["expected"], rtol=0, atol=1e-6)
+
+
+def test_sh_addition_theorem():
+    """Degree-l band of the real spherical harmonics: sum_m Y_lm(v)^2 = (2l+1)/(4 pi) for unit v, which
+    pins every normalisation constant; and Y_00, Y_1m against their closed forms."""
+    v = torch.nn.functional.normalize(torch.randn(257, 3, generator=torch.Generator().manual_seed(2)), dim=1)
+    Y = oracle.sh(v.numpy())
+    for l in range(4):
+        band = Y[:, l * l:(l + 1) * (l + 1)]
+        np.testing.assert_allclose((band.astype(np.float64) ** 2).sum(1), (2 * l + 1) / (4 * math.pi), rtol=2e-6)
+    c1 = math.sqrt(3.0 / (4.0 * math.pi))
+    np.testing.assert_allclose(Y[:, 0], 0.5 / math.sqrt(math.pi), rtol=1e-7)
+    np.testing.assert_allclose(Y[:, 1:4], c1 * torch.stack([-v[:, 1], v[:, 2], -v[:, 0]], 1).numpy(), rtol=1e-6, atol=1e-7)
+    # the autograd oracle's basis is the same
+    np.testing.assert_allclose(grad_oracle._sh(v.double()).numpy(), Y, rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("base", [False])
+def test_grid_sh_grad_oracle_forward_matches_c_oracle(base):
+    sc = make_scene(3000, 1, decoder="grid_sh")
+    assert sc.cond.shape == (3000, 32) and sc.features.numel() == 16502
+    O, v = camera_rays(24, 24, 60.0, eye=(0.0, 0.0, 3.0))
+    fr = oracle.prep_frames(*sc.activated())
+    csr = oracle.hit_lists(fr, O, v)
+    ref = oracle.forward(sc, O, v, csr, "training", base=base)
+    assert ref["total_hits"] > 100
+    d = np.zeros((576, 3), np.float32)
+    gr = grad_oracle.gradients(sc, O, v, csr, ref["nhits"], d, base=base)
+    np.testing.assert_allclose(gr["C"].numpy(), ref["rgb"], atol=2e-4)
+    # the variant really decodes differently from the reference decoder on the same geometry
+    sc0 = make_scene(3000, 1)
+    ref0 = oracle.forward(sc0, O, v, csr, "training")
+    assert np.abs(ref0["rgb"] - ref["rgb"]).max() > 1e-3
