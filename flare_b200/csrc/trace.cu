@@ -276,19 +276,30 @@ __device__ __forceinline__ void heap_insert(HeapBuf<K> &h, float t, int id) {
     h.ri = h.i[threadIdx.x];
 }
 
-template <bool STATS, int K>
+template <bool STATS, int K, bool PERSIST>
 __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
     const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
     const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
-    const float *__restrict__ tmax_ = nullptr) {
+    const float *__restrict__ tmax_ = nullptr, int *__restrict__ chunk_ctr = nullptr) {
     __shared__ int s_node[4][TRACE_STACK];
     __shared__ unsigned s_mask[4][TRACE_STACK];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    const bool live = j < count;
     unsigned long long nprim = 0, nnode = 0;
+    // PERSIST: the grid holds as many blocks as fit at once and every warp claims the next 32 rays of
+    // the list until it is exhausted, so a warp slot frees as soon as its rays are done instead of
+    // when the slowest warp of its block is (dense and sparse rays share blocks).
+    int base = blockIdx.x * blockDim.x + (threadIdx.x & ~31);
+    while (true) {
+    if (PERSIST) {
+        int b = 0;
+        if (lane == 0) b = atomicAdd(chunk_ctr, 32);
+        base = __shfl_sync(0xffffffffu, b, 0);
+        if (base >= count) break;
+    }
+    const int j = base + lane;
+    const bool live = j < count;
     int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
     float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
     float t_min = INFINITY, tcap = INFINITY;
@@ -417,6 +428,9 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
             idx_out[(size_t)k * stride + j] = valid ? ik : -1;
             if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
         }
+    }
+    __syncwarp();
+    if (!PERSIST) break;
     }
     if (STATS) {
         for (int o = 16; o > 0; o >>= 1) nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
@@ -924,11 +938,27 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
         FLARE_CUDA_TRY(cudaGetLastError());
         return FLARE_OK;
     }
+    static const bool persist = getenv_int("FLARE_TRACE_PERSIST", 1) != 0;
+    if (k == K_PASS && K_PASS != K_HITS && heap && persist) {
+        const size_t smem = (size_t)K_PASS * 128 * 8;
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap_kernel<true, K_PASS, true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        int per_sm = 0;
+        FLARE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trace_heap_kernel<true, K_PASS, true>, B,
+                                                                     smem));
+        const int grid = std::max(1, std::min((count + B - 1) / B, r->num_sms * std::max(per_sm, 1)));
+        FLARE_CUDA_TRY(cudaMemsetAsync(r->counters + 2, 0, sizeof(int), st));
+        trace_heap_kernel<true, K_PASS, true><<<grid, B, smem, st>>>(
+            O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+            r->dstatus, r->dstats, t_max, r->counters + 2);
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    }
     if (k == K_PASS && K_PASS != K_HITS && heap) {
         const size_t smem = (size_t)K_PASS * 128 * 8;
-        FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap_kernel<true, K_PASS>,
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap_kernel<true, K_PASS, false>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        trace_heap_kernel<true, K_PASS><<<(count + B - 1) / B, B, smem, st>>>(
+        trace_heap_kernel<true, K_PASS, false><<<(count + B - 1) / B, B, smem, st>>>(
             O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
             r->dstatus, r->dstats, t_max);
         FLARE_CUDA_TRY(cudaGetLastError());
