@@ -483,3 +483,36 @@ def test_grid_sh_backward_matches_autograd(case_grid, reg):
     assert not bad, f"relative L2 above {GRAD_TOL}: {bad}"
     assert float(np.abs(G["A1"][:, 64:].cpu().numpy()).max()) == 0.0  # unused W1 columns: zero gradient
 
+
+
+# ------------------------------------------------------------------ known-answer scenes
+def _kat_renderer(sc):
+    from kat_scenes import activated
+    r = _renderer(64)
+    r.SetGeometry(*[t.cuda().contiguous() for t in activated(sc)])
+    return r
+
+
+@pytest.mark.parametrize("name", ["coplanar", "grazing"])
+def test_kat_hits_bit_exact(name):
+    import kat_scenes
+    sc, O, v = getattr(kat_scenes, name)()
+    r = _kat_renderer(sc)
+    t, idx = r.Render(O.cuda(), v.cuda(), z(64), 64)
+    fr = r.frames().cpu().numpy()
+    to, io = oracle.hits(fr, O.numpy(), v.numpy(), np.zeros(64, np.float32))
+    assert np.array_equal(idx.cpu().numpy(), io)
+    assert np.array_equal(t.cpu().numpy(), to)
+    assert not torch.isnan(t).any()
+
+
+def test_kat_termination_inside_a_pass():
+    from kat_scenes import expected_stack_image, stack
+    sc, O, v = stack()
+    r = _kat_renderer(sc)
+    g = {k: x.cuda() for k, x in sc.items()}
+    img = z(64, 3)
+    r.Forward_inference_base(O.cuda(), v.cuda(), img, 0.0, 0.0, 0.0, g["m"], g["s"], g["q"], g["RGBA"], g["k"], 1e-4)
+    rgb, j = expected_stack_image(sc)
+    assert r.stats()["hits_composited"] == 64 * j
+    np.testing.assert_allclose(img.cpu().numpy(), np.tile(rgb, (64, 1)), atol=1e-5)
