@@ -74,7 +74,8 @@ class GatherTensor(ctypes.Structure):
 
 class Stats(ctypes.Structure):
     _fields_ = [("rays", ctypes.c_longlong), ("passes", ctypes.c_longlong), ("hits_composited", ctypes.c_longlong),
-                ("prim_tests", ctypes.c_longlong), ("node_visits", ctypes.c_longlong)]
+                ("prim_tests", ctypes.c_longlong), ("node_visits", ctypes.c_longlong),
+                ("decoder_tiles", ctypes.c_longlong)]
 
 
 class KernelTimes(ctypes.Structure):

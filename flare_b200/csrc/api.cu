@@ -371,6 +371,7 @@ int flare_get_stats(flare_renderer *r, flare_stats *out) {
     out->passes = (long long)h[ST_PASSES];
     out->hits_composited = (long long)h[ST_HITS];
     out->prim_tests = (long long)h[ST_PRIM_TESTS];
+    out->decoder_tiles = (long long)h[ST_TILES];
     out->node_visits = (long long)h[ST_NODES];
     out->rays = 0;
     return FLARE_OK;

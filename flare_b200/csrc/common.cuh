@@ -44,7 +44,7 @@ enum : int {
 };
 
 // Counters in renderer->dstats (unsigned long long each).
-enum { ST_PASSES = 0, ST_HITS = 1, ST_PRIM_TESTS = 2, ST_NODES = 3, ST_NSTATS = 8 };
+enum { ST_PASSES = 0, ST_HITS = 1, ST_PRIM_TESTS = 2, ST_NODES = 3, ST_TILES = 4, ST_NSTATS = 8 };
 
 // BVH2 node: both child boxes plus child links; a negative link ~p is a leaf holding sorted primitive p.
 struct __align__(16) Node {

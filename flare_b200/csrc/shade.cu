@@ -582,7 +582,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
     const float2 *lut2 = FLARE_FWD_LUT_SMEM ? reinterpret_cast<const float2 *>(smem + SM_FWD_LUT)
                                             : reinterpret_cast<const float2 *>(sc.features);
     char *tile = smem + SM_FWD_TILE;
-    unsigned long long nhits = 0;
+    unsigned long long nhits = 0, ntiles = 0;
     const int nchunks = (pp.count + 127) / 128;
     for (int chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
         const int slot = chunk * 128 + tid;
@@ -627,6 +627,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             float y4[4] = {0, 0, 0, 0};
             if (DEC) {
                 if (!__syncthreads_or(valid)) continue;  // uniform: no ray of this CTA needs slot h
+                ++ntiles;
                 write_x_row<DK>(tile, tid, lut2, sc, idc, g.u * LUT_SCALE, g.w * LUT_SCALE, v, !valid);
                 fence_async_smem();
                 tc_fence_before();
@@ -725,6 +726,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
 done:
     for (int o = 16; o > 0; o >>= 1) nhits += __shfl_xor_sync(0xffffffffu, nhits, o);
     if ((tid & 31) == 0 && nhits) atomicAdd(pp.stats + ST_HITS, nhits);
+    if (tid == 0 && ntiles) atomicAdd(pp.stats + ST_TILES, ntiles);
     if (DEC) {
         if (s_abort && tid == 0) atomicOr(pp.status, ERR_MBAR);
         tc_fence_before();
@@ -916,6 +918,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     bool nvalid = false;
     int ind = -1, ind_next = -1;
     float t_hit = 0.0f;
+    unsigned long long ntiles = 0;
     while (true) {
         {   // rows without a ray claim the next ones (one atomic per warp)
             const bool need = !have && !exhausted;
@@ -969,6 +972,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
 #pragma unroll
             for (int e = 0; e < PG_N; ++e) pg[e] = 0.0f;
             const bool any_valid = DEC ? __syncthreads_or(valid) : false;  // uniform
+            if (any_valid && tid == 0) ++ntiles;
             if (DEC && any_valid) {
                 write_x_row<DK>(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
                 fence_async_smem();
@@ -1261,6 +1265,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
         }
     }
 done:
+    if (tid == 0 && ntiles) atomicAdd(pp.stats + ST_TILES, ntiles);
     if (DEC) {
         wait_bulk_done();
         if (s_abort && tid == 0) atomicOr(pp.status, ERR_MBAR);

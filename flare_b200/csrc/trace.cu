@@ -49,6 +49,10 @@ __device__ __forceinline__ void kbuf_insert(KBuf<K> &b, float t, int id) {
     b.i[0] = lt_k ? id : b.i[0];
 }
 
+#ifdef FLARE_TRACE_WHY
+__device__ unsigned long long g_why[4];  // diagnostic build only: why primitive tests fail
+#endif
+
 // Exact hit test against one 48-byte primitive record (same operation order as the oracle).
 __device__ __forceinline__ bool hit_rec(float4 r0, float4 r1, float4 r2, float3 O, float3 v, float t_min,
                                         const PolyConst &c_poly, float &t_out, float t_max = INFINITY) {
@@ -57,7 +61,12 @@ __device__ __forceinline__ bool hit_rec(float4 r0, float4 r1, float4 r2, float3 
     float num = __fmaf_rn(r0.w, dx, __fmaf_rn(r1.x, dy, __fmul_rn(r1.y, dz)));
     float den = __fmaf_rn(r0.w, v.x, __fmaf_rn(r1.x, v.y, __fmul_rn(r1.y, v.z)));
     float t = __fdiv_rn(num, den);
-    if (!(t >= t_min) || t > t_max) return false;  // beyond the K-th buffered hit: cannot enter the buffer
+    if (!(t >= t_min) || t > t_max) {  // beyond the K-th buffered hit: cannot enter the buffer
+#ifdef FLARE_TRACE_WHY
+        atomicAdd(g_why + (t >= t_min ? 1 : 0), 1ull);  // 0: before t_min, 1: beyond the K-th hit
+#endif
+        return false;
+    }
     float ex = __fsub_rn(__fmaf_rn(v.x, t, O.x), r0.x);
     float ey = __fsub_rn(__fmaf_rn(v.y, t, O.y), r0.y);
     float ez = __fsub_rn(__fmaf_rn(v.z, t, O.z), r0.z);
@@ -65,7 +74,12 @@ __device__ __forceinline__ bool hit_rec(float4 r0, float4 r1, float4 r2, float3 
     float b = __fmaf_rn(r2.y, ex, __fmaf_rn(r2.z, ey, __fmul_rn(r2.w, ez)));
     if (c_poly.half) {
         for (int j = 0; j < c_poly.half; ++j)
-            if (!(fabsf(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b))) <= 1.0f)) return false;
+            if (!(fabsf(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b))) <= 1.0f)) {
+#ifdef FLARE_TRACE_WHY
+                atomicAdd(g_why + 2, 1ull);  // outside the polygon
+#endif
+                return false;
+            }
     } else {
         for (int j = 0; j < c_poly.n; ++j)
             if (!(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b)) <= 1.0f)) return false;
@@ -993,3 +1007,17 @@ int launch_trace_geom(const Node *nodes, const float4 *rec, const int *ids_sorte
 
 }  // namespace flare
 
+
+#ifdef FLARE_TRACE_WHY
+// Diagnostic build only (-DFLARE_TRACE_WHY): failed primitive tests by reason since the last reset:
+// [0] t before t_min, [1] t beyond the current K-th hit, [2] outside the polygon.
+extern "C" int flare_debug_why(unsigned long long *out, int reset) {
+    FLARE_CUDA_TRY(cudaDeviceSynchronize());
+    FLARE_CUDA_TRY(cudaMemcpyFromSymbol(out, flare::g_why, 3 * sizeof(unsigned long long)));
+    if (reset) {
+        unsigned long long z[4] = {0, 0, 0, 0};
+        FLARE_CUDA_TRY(cudaMemcpyToSymbol(flare::g_why, z, sizeof(z)));
+    }
+    return 0;
+}
+#endif

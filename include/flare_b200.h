@@ -252,6 +252,8 @@ int flare_gather_rows(const flare_gather_tensor *tensors, int n_tensors, const i
    stream of that call): rays, passes, composited hits, primitive tests, BVH node visits. */
 typedef struct flare_stats {
     long long rays, passes, hits_composited, prim_tests, node_visits;
+    long long decoder_tiles;  /* 128-row tensor-core tiles the decoder kernels ran (forward + backward);
+                                 hits_composited / (128 * decoder_tiles) is their row utilisation */
 } flare_stats;
 int flare_get_stats(flare_renderer *r, flare_stats *out);
 
