@@ -114,6 +114,8 @@ def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":  # the CPU arm: rank 0 alone works, no device and no process group needed
+        return world, rank, local
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
@@ -403,8 +405,6 @@ def main():
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         run_reference(args, world, rank)
-        if world > 1:
-            dist.destroy_process_group()
         return
     device = torch.device(f"cuda:{torch.cuda.current_device()}")
     hbm, tflops, tflops_sus, peak_kind = peaks()
