@@ -626,15 +626,17 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             else g = Geo{};
             float y4[4] = {0, 0, 0, 0};
             if (DEC) {
-                if (!__syncthreads_or(valid)) continue;  // uniform: no ray of this CTA needs slot h
+                // this barrier also closes the previous slot: its TMEM reads are done before the next
+                // layer-1 MMA is issued, and an abort raised in its waits is seen by every thread here
+                const bool any = __syncthreads_or(valid);
+                if (s_abort) goto done;
+                if (!any) continue;  // uniform: no ray of this CTA needs slot h
                 ++ntiles;
                 write_x_row<DK>(tile, tid, lut2, sc, idc, g.u * LUT_SCALE, g.w * LUT_SCALE, v, !valid);
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
                 mlp_forward_tile<DK>(smem, tile, tile, tile, mm, y4, nullptr, 0);
-                __syncthreads();
-                if (s_abort) goto done;
             }
             if (!valid) continue;
             {
@@ -955,7 +957,12 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 }
             }
         }
-        if (!__syncthreads_or(have)) break;
+        // this barrier also closes the previous slot: its staging rows have been read by the bulk
+        // reductions (the issuing threads waited) before the X and H1 tiles are written again, and an
+        // abort raised in its waits is seen by every thread here
+        const bool more = __syncthreads_or(have);
+        if (DEC && s_abort) goto done;
+        if (!more) break;
         {
             ind = have ? ind_next : -1;
             t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
@@ -1242,9 +1249,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 }
                 if (valid) wait_bulk_read();  // the staging rows are overwritten next slot
                 tc_fence_before();
-                __syncthreads();
                 if (tid == 0) s_first = 0;
-                if (s_abort) goto done;
             }
             if (!DEC && valid) {  // decoder-free path: straight into the caller's arrays
                 geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
