@@ -957,12 +957,6 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 }
             }
         }
-        // this barrier also closes the previous slot: its staging rows have been read by the bulk
-        // reductions (the issuing threads waited) before the X and H1 tiles are written again, and an
-        // abort raised in its waits is seen by every thread here
-        const bool more = __syncthreads_or(have);
-        if (DEC && s_abort) goto done;
-        if (!more) break;
         {
             ind = have ? ind_next : -1;
             t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
@@ -978,7 +972,13 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             float pg[PG_N];  // this hit's per-primitive gradients (layout PG_*)
 #pragma unroll
             for (int e = 0; e < PG_N; ++e) pg[e] = 0.0f;
+            // The slot's first barrier.  It also closes the previous slot: that slot's staging rows have
+            // been read by its bulk reductions (the issuing threads waited) before the X and H1 tiles are
+            // written again, and an abort raised in its waits is seen by every thread here.  A valid row
+            // has a ray, so whether any row still has one is asked only when no row composites.
             const bool any_valid = DEC ? __syncthreads_or(valid) : false;  // uniform
+            if (DEC && s_abort) goto done;
+            if (!any_valid && !__syncthreads_or(have)) break;
             if (any_valid && tid == 0) ++ntiles;
             if (DEC && any_valid) {
                 write_x_row<DK>(xt, tid, lut2, sc, idc, cu, cw, v, !valid);
