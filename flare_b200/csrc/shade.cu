@@ -921,6 +921,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     int ind = -1, ind_next = -1;
     float t_hit = 0.0f;
     unsigned long long ntiles = 0;
+    bool bulk_pending = false;  // this thread's last bulk reduction may still be reading its staging row
     while (true) {
         {   // rows without a ray claim the next ones (one atomic per warp)
             const bool need = !have && !exhausted;
@@ -976,6 +977,10 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             // been read by its bulk reductions (the issuing threads waited) before the X and H1 tiles are
             // written again, and an abort raised in its waits is seen by every thread here.  A valid row
             // has a ray, so whether any row still has one is asked only when no row composites.
+            if (DEC && bulk_pending) {  // the staging rows are overwritten after this barrier
+                wait_bulk_read();
+                bulk_pending = false;
+            }
             const bool any_valid = DEC ? __syncthreads_or(valid) : false;  // uniform
             if (DEC && s_abort) goto done;
             if (!any_valid && !__syncthreads_or(have)) break;
@@ -987,8 +992,6 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 __syncthreads();
                 mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, hd1, 64);
                 prefetch_hit<DK>(sc, ind_next);
-                __syncthreads();
-                if (s_abort) goto done;
             }
             // ---- compositing gradient (restates Backward.cu:1700-1900) ----
             float gu = 0.0f, gw = 0.0f, dLdt_depth = 0.0f, ow = 0.0f, sgn = 1.0f;
@@ -1089,6 +1092,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
+                if (s_abort) goto done;  // raised in the forward tile's waits
                 const uint32_t acc0 = s_first ? 0u : 1u;
                 const uint32_t dwreg = mm.tmem + TM_DW;
                 const uint32_t half1 = 16u << 16;
@@ -1247,7 +1251,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     fence_async_smem();
                     bulk_red_add_f32(bo.pgrad + (size_t)ind * PROW_FLOATS, dcrow, PROW_FLOATS * 4);
                 }
-                if (valid) wait_bulk_read();  // the staging rows are overwritten next slot
+                bulk_pending = valid;  // its staging row is read before the next slot's first barrier
                 tc_fence_before();
                 if (tid == 0) s_first = 0;
             }
