@@ -749,28 +749,10 @@ __device__ __forceinline__ void red_add_v4(float *addr, float a, float b, float 
 
 // scalar gradient accumulation into global memory
 __device__ __forceinline__ void gadd(float *dst, float v) {
-#ifdef FLARE_EXPERIMENT_NO_ATOMICS
-    if (v == 12345.678f) dst[0] = v;
-    return;
-#endif
     atomicAdd(dst, v);
 }
 
-// LUT feature gradient accumulation: the (x, y) features of one cell are adjacent, so one 8-byte
-// vector reduction adds both (dst is 8-byte aligned: per-CTA copies start at even float offsets).
-__device__ __forceinline__ void lut_add2(float *dst, float a, float b) {
-#ifdef FLARE_EXPERIMENT_NO_LUT_ATOMICS
-    if (a == 12345.678f) dst[0] = b;
-    return;
-#endif
-    asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(dst), "f"(a), "f"(b) : "memory");
-}
-
 __device__ __forceinline__ void red_add4(float *dst, bool vec, float a, float b, float c, float d) {
-#ifdef FLARE_EXPERIMENT_NO_ATOMICS
-    if (a == 12345.678f) dst[0] = b + c + d;
-    return;
-#endif
     if (vec) {
         red_add_v4(dst, a, b, c, d);
     } else {
