@@ -516,3 +516,27 @@ def test_kat_termination_inside_a_pass():
     rgb, j = expected_stack_image(sc)
     assert r.stats()["hits_composited"] == 64 * j
     np.testing.assert_allclose(img.cpu().numpy(), np.tile(rgb, (64, 1)), atol=1e-5)
+
+
+# ------------------------------------------------------------------ BASELINE config 0 at its own size
+@pytest.mark.parametrize("decoder", ["lut_pe", "grid_sh"])
+def test_config0_forward_backward(decoder):
+    """Config 0 (10k primitives, one 64x64 camera on the radius-3 sphere, forward + backward); with the
+    grid/SH decoder this is BASELINE's literal config-0 model."""
+    c = Case(10000, 64, seed=0, decoder=decoder)
+    R = c.R
+    ref = _fwd_oracle(c, "training", False, (0.0, 0.0, 0.0))
+    bitmap, dacc, nacc, dai = z(R, 3), z(R, 4), z(R, 4), z(R, 2)
+    c.r.Forward_training(*c.dec(), c.Og, c.vg, bitmap, 0.0, 0.0, 0.0, *c.geo(), 1e-4, dacc, REG_A, REG_B, dai,
+                         z(R, 3), nacc)
+    assert c.r.stats()["hits_composited"] == ref["total_hits"] > 1000
+    assert np.abs(bitmap.cpu().numpy() - ref["rgb"]).max() < RGB_TOL
+    G, gr = _run_backward(c, False, 0.0, 0.0, seed=17)
+    kink = RELU_KINK_GRADS if decoder == "grid_sh" else ()
+    bad = {}
+    for k in ["RGB", "A", "k", "m", "s", "q", "cond", "features", "A1", "b1", "A2", "b2", "A3", "b3"]:
+        got = G[k].cpu().numpy() if torch.is_tensor(G[k]) else G[k]
+        e = grad_oracle.rel_l2(got, gr[k].numpy())
+        if not e < (GRAD_TOL_RELU_KINK if k in kink else GRAD_TOL):
+            bad[k] = e
+    assert not bad, f"relative L2 above the bar: {bad}"
