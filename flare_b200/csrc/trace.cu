@@ -72,7 +72,16 @@ __device__ __forceinline__ bool hit_rec(float4 r0, float4 r1, float4 r2, float3 
     float ez = __fsub_rn(__fmaf_rn(v.z, t, O.z), r0.z);
     float a = __fmaf_rn(r1.z, ex, __fmaf_rn(r1.w, ey, __fmul_rn(r2.x, ez)));
     float b = __fmaf_rn(r2.y, ex, __fmaf_rn(r2.z, ey, __fmul_rn(r2.w, ez)));
-    if (c_poly.half) {
+    if (c_poly.half == 4) {  // octagon (the renderer's default): the same tests, unrolled
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (!(fabsf(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b))) <= 1.0f)) {
+#ifdef FLARE_TRACE_WHY
+                atomicAdd(g_why + 2, 1ull);  // outside the polygon
+#endif
+                return false;
+            }
+    } else if (c_poly.half) {
         for (int j = 0; j < c_poly.half; ++j)
             if (!(fabsf(__fmaf_rn(c_poly.c[j], a, __fmul_rn(c_poly.s[j], b))) <= 1.0f)) {
 #ifdef FLARE_TRACE_WHY
