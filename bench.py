@@ -46,12 +46,13 @@ B_HIT_TRACE = 64                 # one 64-B node per composited hit
 B_HIT_FWD = 56 + 192             # primitive record + fp16 descriptor row
 B_HIT_BWD = 56 + 192 + 440       # re-read + gradient writes (14 geometry + 96 descriptor fp32)
 B_RAY_FWD, B_RAY_BWD = 44, 24
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per traversal launch, measured with a one-pass
-# ncu capture of the config-3 bench command (mean of the eight traversal launches captured: passes 0-3 of
-# one view, block-wide heap kernel for passes 0-2 and the warp-per-ray kernel for pass 3, twice).  Most of
-# it is the 42-slot (t, index) hit lists each pass writes (8 B per slot); node and record fetches are
-# mostly L2 hits.  Only valid for the config-3 workload; other workloads report null.
-TRACE_DRAM_BYTES_PER_LAUNCH = {3: 398.4e6}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each timed kernel, measured with
+# a one-pass ncu capture of the config-3 bench command (mean over the launches captured: passes 0-3 of one
+# view, profiles/trace_shade_dram_config3_training_step.md).  Traversal: mostly the 42-slot (t, index) hit
+# lists each pass writes (8 B per slot), node and record fetches being mostly L2 hits; shading: descriptor
+# rows, primitive parameters and hit lists read, per-primitive gradient rows written.  Only valid for the
+# config-3 workload; other workloads report null.
+DRAM_BYTES_PER_LAUNCH = {"trace": {3: 398.4e6}, "shade_forward": {3: 594.7e6}, "shade_backward": {3: 648.3e6}}
 FLOP_HIT_FWD = 2 * (128 * 64 + 64 * 64 + 64 * 4)
 
 
@@ -433,7 +434,7 @@ def main():
     d = per[dom]
     roof = {"bound": "hbm", "kernel": dom, "achieved": d["achieved_gbs"], "peak": hbm, "unit": "GB/s",
             "frac": d["achieved_gbs"] / hbm,
-            "traffic": TRACE_DRAM_BYTES_PER_LAUNCH.get(main_cfg) if dom == "trace" else None,
+            "traffic": DRAM_BYTES_PER_LAUNCH.get(dom, {}).get(main_cfg),
             "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
             if peak_kind == "measured" else "fallback 6.65 TB/s",
             "algo_bytes_per_launch": d["algo_bytes"] / max(d["launches"], 1),
