@@ -99,10 +99,10 @@ def _worker(rank, world, port, out, mode):
 
 
 def _run(world, mode):
-    mgr = mp.Manager()
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
     out = mgr.dict()
     port = _free_port()
-    ctx = mp.get_context("spawn")
     ps = [ctx.Process(target=_worker, args=(r, world, port, out, mode)) for r in range(world)]
     for p in ps:
         p.start()
