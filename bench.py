@@ -48,7 +48,7 @@ B_HIT_BWD = 56 + 192 + 440       # re-read + gradient writes (14 geometry + 96 d
 B_RAY_FWD, B_RAY_BWD = 44, 24
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each timed kernel, measured with
 # a one-pass ncu capture of the config-3 bench command (mean over the launches captured: passes 0-3 of one
-# view, profiles/trace_shade_dram_config3_training_step.md).  Traversal: mostly the 42-slot (t, index) hit
+# view).  Traversal: mostly the 42-slot (t, index) hit
 # lists each pass writes (8 B per slot), node and record fetches being mostly L2 hits; shading: descriptor
 # rows, primitive parameters and hit lists read, per-primitive gradient rows written.  Only valid for the
 # config-3 workload; other workloads report null.

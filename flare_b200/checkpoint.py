@@ -77,12 +77,18 @@ def restore_optimizer(opt, tensors: dict):
         return
     state = sd.get("state", {})
     segs = {s.name: i for i, s in enumerate(opt.adam.segments)}
+    # the 17-entry form has no RGB parameter, so its optimizer has no RGB group: group g is segment g + 1
+    names = GROUP_SEGMENTS if "RGB" in tensors else GROUP_SEGMENTS[1:]
     step = 0
-    for g, name in enumerate(GROUP_SEGMENTS):
+    for g, name in enumerate(names):
         st = state.get(g)
         if not st:
             continue
         m, v = opt.adam.state[segs[name]]
+        for key, dst in (("exp_avg", m), ("exp_avg_sq", v)):
+            if st[key].numel() != dst.numel():
+                raise ValueError(f"optimizer group {g} ({name}): {key} has {st[key].numel()} values, the "
+                                 f"parameter has {dst.numel()}")
         m.copy_(st["exp_avg"].reshape(m.shape))
         v.copy_(st["exp_avg_sq"].reshape(v.shape))
         step = max(step, int(float(st.get("step", 0))))

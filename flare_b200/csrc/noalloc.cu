@@ -1,17 +1,17 @@
 // noalloc.cu -- flare_render_hits_noalloc: the proxy-hierarchy build and the 16-nearest-hit query of
 // flare_set_geometry + flare_render_hits in one call that allocates no device memory.
 //
-// Who needs it: callers that cannot allocate device memory when they call in -- code running while a
-// CUDA stream is being captured (cudaMalloc is not allowed there), hosts that hand this library a fixed
-// device-memory budget and forbid it to grow, and plugins loaded into processes whose own allocator owns
-// every device byte.  The renderer object allocates its scratch in flare_create and grows it in
+// Who needs it: callers that cannot allocate device memory when they call in -- hosts that hand this
+// library a fixed device-memory budget and forbid it to grow, and plugins loaded into processes whose own
+// allocator owns every device byte.  The renderer object allocates its scratch in flare_create and grows it in
 // flare_set_geometry; this entry point instead keeps all scratch -- polygon frames, boxes, Morton keys,
 // the radix-sort workspace, the hierarchy and the traversal records -- in one file-scope static device
 // array sized for at most FLARE_NOALLOC_MAX_PRIMS primitives.  The caller passes inputs and outputs.
 //
 // Set-up: the first call on a device resolves the array's device address with cudaGetSymbolAddress
-// (that device current) and checks the sort workspace fits; make that first call before any stream
-// capture.  Later calls on the device reuse the address.  The array keeps the last call's contents; each
+// (that device current) and checks the sort workspace fits; a failed resolution is not cached, so the
+// next call retries it.  Later calls on the device reuse the address.  Each call synchronises `stream`
+// to read the status word.  The array keeps the last call's contents; each
 // call clears what must start at zero (status word, refit flags).  Calls that overlap on the GPU (two
 // streams, or two host threads on one device) share the array and race: serialise them.
 #include <cmath>
@@ -52,7 +52,6 @@ namespace {
 struct DeviceSetup {
     bool done = false;
     unsigned char *ptr = nullptr;
-    cudaError_t err = cudaSuccess;
 };
 std::mutex g_setup_mu;
 DeviceSetup g_setup[64];
@@ -114,15 +113,20 @@ extern "C" int flare_render_hits_noalloc(int number_of_sides, const float *m, co
         std::lock_guard<std::mutex> lk(g_setup_mu);
         DeviceSetup &s = g_setup[dev];
         if (!s.done) {  // once per device, with that device current
+            if (geometry_sort_temp_bytes(MAX_P) > SORT_BYTES) {  // deterministic: a build-time sizing fault
+                set_error("flare_render_hits_noalloc: the radix-sort workspace does not fit its %zu-byte region",
+                          SORT_BYTES);
+                return FLARE_E_STATE;
+            }
             void *p = nullptr;
-            s.err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (err != cudaSuccess || !p) {  // not cached: a later call retries the resolution
+                cudaGetLastError();
+                set_error("flare_render_hits_noalloc: set-up on device %d failed: %s", dev, cudaGetErrorString(err));
+                return FLARE_E_CUDA;
+            }
             s.ptr = static_cast<unsigned char *>(p);
-            if (s.err == cudaSuccess && geometry_sort_temp_bytes(MAX_P) > SORT_BYTES) s.err = cudaErrorInvalidValue;
             s.done = true;
-        }
-        if (s.err != cudaSuccess || !s.ptr) {
-            set_error("flare_render_hits_noalloc: set-up on device %d failed: %s", dev, cudaGetErrorString(s.err));
-            return FLARE_E_CUDA;
         }
         base = s.ptr;
     }

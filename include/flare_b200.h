@@ -280,12 +280,13 @@ int flare_get_frames(flare_renderer *r, float *frames_out, void *stream);
 /*
  * Allocation-free 16-nearest-hit query.  No counterpart in the reference, whose renderer allocates its
  * scratch in the constructor and in SetGeometry.  For callers that cannot allocate device memory when
- * they call (during a CUDA stream capture, under a fixed device-memory budget, or as a plugin in a
- * process whose allocator owns the device): builds the proxy hierarchy for n_prims <=
+ * they call (under a fixed device-memory budget, or as a plugin in a process whose allocator owns the
+ * device): builds the proxy hierarchy for n_prims <=
  * FLARE_NOALLOC_MAX_PRIMS primitives from SetGeometry's activated inputs and writes the same (16, n_rays)
  * t / idx as flare_set_geometry + flare_render_hits, with all scratch (about 11 MB) in a static device
  * array that every GPU loading the library holds until exit.  Larger scenes return FLARE_E_INVALID.
- * The first call on a device resolves the array's address; make it before any stream capture.  Calls
+ * The first call on a device resolves the array's address (a failed resolution is retried by the next
+ * call).  Calls
  * share the array, so calls that overlap on the GPU race and must be serialised by the caller.  The
  * call synchronises `stream` to read its status word.
  */

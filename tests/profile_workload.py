@@ -1,6 +1,6 @@
 """Small fixed workload for kernel profiling (ncu) of the render path.
 
-    python -m flare_b200.profile_driver [n_primitives=1000000] [width=400]
+    python tests/profile_workload.py [n_primitives=1000000] [width=400]
 
 Renders a seeded scene (BASELINE config-0 distributions) with Forward_training + Backward twice through
 CPyOptiXFLARERenderer, so each kernel launches several times; pick launches with ncu -k / -s / -c.

@@ -62,3 +62,38 @@ def test_optimizer_state_round_trip(tmp_path):
     for (m1, v1), (m2, v2) in zip(opt.adam.state, opt2.adam.state):
         assert torch.equal(m1.reshape(-1), m2.reshape(-1)) and torch.equal(v1.reshape(-1), v2.reshape(-1))
     assert torch.equal(opt2.W1, opt.W1) and torch.equal(opt2.cond32, opt.cond32)
+
+
+def test_legacy_optimizer_state_skips_the_rgb_segment():
+    """A 17-entry checkpoint's optimizer has no RGB group: its group 0 holds A's moments."""
+    from flare_b200 import optim
+    from flare_b200.dp import GradBuffer
+    n = 50
+    t = list(_reference_tuple(n, legacy=True))
+    params = t[:15]
+    state = {g: {"step": torch.tensor(5.0), "exp_avg": torch.full_like(p, float(g + 1)),
+                 "exp_avg_sq": torch.full_like(p, float(g + 101))} for g, p in enumerate(params)}
+    t[15] = {"state": state, "param_groups": []}
+    tens = checkpoint.tensors_from_tuple(tuple(t))
+    sc = checkpoint.scene_from_tensors(tens)
+    opt = optim.ModelOptimizer(sc, GradBuffer(n, True, "cpu"))
+    checkpoint.restore_optimizer(opt, tens)
+    segs = {s.name: i for i, s in enumerate(opt.adam.segments)}
+    assert opt.adam.t == 5
+    for g, name in enumerate(checkpoint.GROUP_SEGMENTS[1:]):
+        m, v = opt.adam.state[segs[name]]
+        assert torch.all(m == g + 1) and torch.all(v == g + 101), name
+    m_rgb, _ = opt.adam.state[segs["RGB"]]
+    assert torch.all(m_rgb == 0)
+
+
+def test_optimizer_state_of_the_wrong_size_is_rejected():
+    from flare_b200 import optim
+    from flare_b200.dp import GradBuffer
+    t = list(_reference_tuple(50))
+    t[16] = {"state": {0: {"step": torch.tensor(1.0), "exp_avg": torch.zeros(49, 3), "exp_avg_sq": torch.zeros(49, 3)}},
+             "param_groups": []}
+    tens = checkpoint.tensors_from_tuple(tuple(t))
+    opt = optim.ModelOptimizer(checkpoint.scene_from_tensors(tens), GradBuffer(50, True, "cpu"))
+    with pytest.raises(ValueError):
+        checkpoint.restore_optimizer(opt, tens)
