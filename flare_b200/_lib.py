@@ -102,6 +102,7 @@ EXPORTS = {
                                          ctypes.c_int, vp]),
     "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
     "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
+    "flare_get_pass_hits": (ctypes.c_int, [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int), vp, vp, vp, vp]),
     "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),
     "flare_get_kernel_times": (ctypes.c_int, [vp, ctypes.POINTER(KernelTimes)]),
     "flare_selftest_mlp": (ctypes.c_int, [vp, ctypes.c_int, vp, vp, vp, vp, vp, vp, vp, vp]),

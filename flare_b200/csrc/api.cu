@@ -420,6 +420,36 @@ int flare_get_frames(flare_renderer *r, float *frames_out, void *stream) {
     return FLARE_OK;
 }
 
+static_assert(K_PASS == FLARE_PASS_SLOTS, "the header's pass size must match the build's");
+
+int flare_get_pass_hits(flare_renderer *r, int pass, int *count, int *ray_ids, float *t_out, int *idx_out,
+                        void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(r && count, "flare_get_pass_hits: NULL argument");
+    if (!r->hc_valid) {
+        set_error("flare_get_pass_hits: no cached Forward_training passes (the first Forward_training on a "
+                  "renderer only sizes the cache; the cache was dropped, or a Backward consumed it)");
+        return FLARE_E_STATE;
+    }
+    if (pass < 0) {
+        *count = r->hc_npass;
+        return FLARE_OK;
+    }
+    CHECK_ARG(pass < r->hc_npass, "flare_get_pass_hits: pass out of range");
+    *count = r->hc_cnt[pass];
+    if (!ray_ids && !t_out && !idx_out) return FLARE_OK;
+    CHECK_ARG(ray_ids && t_out && idx_out, "flare_get_pass_hits: NULL output");
+    DeviceGuard dg(r->device);
+    const size_t off = r->hc_off[pass], c = (size_t)r->hc_cnt[pass];
+    FLARE_CUDA_TRY(cudaMemcpyAsync(ray_ids, r->hc_list + off, c * sizeof(int), cudaMemcpyDeviceToDevice, S(stream)));
+    FLARE_CUDA_TRY(cudaMemcpyAsync(t_out, r->hc_t + (size_t)K_PASS * off, c * K_PASS * sizeof(float),
+                                   cudaMemcpyDeviceToDevice, S(stream)));
+    FLARE_CUDA_TRY(cudaMemcpyAsync(idx_out, r->hc_idx + (size_t)K_PASS * off, c * K_PASS * sizeof(int),
+                                   cudaMemcpyDeviceToDevice, S(stream)));
+    FLARE_CUDA_TRY(cudaStreamSynchronize(S(stream)));
+    return FLARE_OK;
+}
+
 int flare_selftest_mlp(const void *X, int rows, const void *A1, const float *b1, const void *A2, const float *b2,
                        const void *A3, const float *b3, float *Y, void *stream) {
     g_err[0] = 0;

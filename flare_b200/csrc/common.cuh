@@ -10,7 +10,7 @@ namespace flare {
 
 constexpr int K_HITS = FLARE_HIT_BUFFER_SIZE;  // 16: hits per Render call (the reference's k-buffer)
 #ifndef FLARE_K_PASS
-#define FLARE_K_PASS 42
+#define FLARE_K_PASS FLARE_PASS_SLOTS
 #endif
 // Hits gathered per pass inside Forward / Backward.  The composited result does not depend on it (hits
 // are consumed in (t, index) order either way); it trades traversal restarts against the per-ray heap in

@@ -799,15 +799,20 @@ __device__ __forceinline__ void geom_grads(const Geo &g, float3 v, float gu, flo
             // dL/dR for R = [U V N]: G_U = gu e^-sx (P-m), G_V = gw e^-sy (P-m),
             // G_N = -dL/dt (P-m)/(N.v) - lambda_n o sgn N_target (the normal regulariser's opacity is held)
             float ln = nvalid ? lambda_normal * (-ow * sgn) : 0.0f;
+            const float a = g.q[0], b = g.q[1], c = g.q[2], d = g.q[3], S = g.S;
+            // The reference forms the depth regulariser's share of dL/dq from a dt/dq that lacks the factor
+            // S = 2/|q|^2 (Backward.cu:2096-2110, Backward_base.cu:496-510: dt_dq is built from (dN/dq) / S
+            // and, unlike du_dq and dv_dq, never scaled by S), so that share is (exact share) / S; it is
+            // reproduced here.  dm and the other shares of dq are exact.
+            const float kq = __fmaf_rn(dLdt_depth * inv_ndv, __fdiv_rn(1.0f, S) - 1.0f, kt);
             float Gm[3][3];
 #pragma unroll
             for (int i = 0; i < 3; ++i) {
                 Gm[i][0] = su * g.d[i];
                 Gm[i][1] = sw * g.d[i];
-                Gm[i][2] = -kt * g.d[i] + ln * Nm[i];
+                Gm[i][2] = -kq * g.d[i] + ln * Nm[i];
             }
             // R = I + S M(q) with S = 2/|q|^2; dR/dq_k = S (dM/dq_k - S q_k M)
-            const float a = g.q[0], b = g.q[1], c = g.q[2], d = g.q[3], S = g.S;
             float GM = Gm[0][0] * (-(c * c + d * d)) + Gm[0][1] * (b * c - a * d) + Gm[0][2] * (b * d + a * c) +
                        Gm[1][0] * (b * c + a * d) + Gm[1][1] * (-(b * b + d * d)) + Gm[1][2] * (c * d - a * b) +
                        Gm[2][0] * (b * d - a * c) + Gm[2][1] * (c * d + a * b) + Gm[2][2] * (-(b * b + c * c));

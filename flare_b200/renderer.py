@@ -24,6 +24,7 @@ import torch
 from . import _lib
 
 F32, F16, I32 = torch.float32, torch.float16, torch.int32
+PASS_SLOTS = 42  # FLARE_PASS_SLOTS: hit slots of an internal traversal pass
 
 # decoder kind -> (descriptor width, feature-table floats): 0 = the reference's LUT / sin-cos / 96-wide
 # decoder, 1 = the dense-grid / spherical-harmonics / 32-wide variant (include/flare_b200.h)
@@ -308,6 +309,26 @@ class CPyOptiXFLARERenderer:
         kt = _lib.KernelTimes()
         _lib.check(self._lib.flare_get_kernel_times(self._h, ctypes.byref(kt)), "kernel_times")
         return {n: (kt.ms[i], kt.launches[i]) for i, n in enumerate(_lib.KERNEL_NAMES)}
+
+    def pass_hits(self):
+        """The traversal passes of the last Forward_training (valid from the second call on this
+        renderer): a list of (ray_ids (count,), t (42, count), idx (42, count)) device tensors."""
+        cnt = ctypes.c_int(0)
+        _lib.check(self._lib.flare_get_pass_hits(self._h, -1, ctypes.byref(cnt), None, None, None, self._stream()),
+                   "pass_hits")
+        out = []
+        dev = f"cuda:{self.device}"
+        for p in range(cnt.value):
+            c = ctypes.c_int(0)
+            _lib.check(self._lib.flare_get_pass_hits(self._h, p, ctypes.byref(c), None, None, None, self._stream()),
+                       "pass_hits")
+            ids = torch.empty(c.value, dtype=torch.int32, device=dev)
+            t = torch.empty((PASS_SLOTS, c.value), dtype=F32, device=dev)
+            idx = torch.empty((PASS_SLOTS, c.value), dtype=torch.int32, device=dev)
+            _lib.check(self._lib.flare_get_pass_hits(self._h, p, ctypes.byref(c), _ptr(ids), _ptr(t), _ptr(idx),
+                                                     self._stream()), "pass_hits")
+            out.append((ids, t, idx))
+        return out
 
     def frames(self):
         """Per-primitive proxy frames (N,12) of the last SetGeometry (used by the hit-list parity test)."""

@@ -278,6 +278,22 @@ int flare_get_kernel_times(flare_renderer *r, flare_kernel_times *out);
 int flare_get_frames(flare_renderer *r, float *frames_out, void *stream);
 
 /*
+ * Diagnostic read-out of the traversal passes of the last Forward_training (the hit cache a following
+ * Backward replays; valid from the second Forward_training on a renderer, which the first one sizes).
+ * pass < 0: *count = number of cached passes.  Otherwise *count = rays of that pass and, when the
+ * outputs are non-NULL, ray_ids (count) receives the pass's ray ids and t_out / idx_out
+ * (FLARE_PASS_SLOTS, count) slot-major its hit lists, ascending by (t, index), +inf / -1 padded.
+ * Device pointers; synchronous on `stream`.  Used by the full-size hit-list parity tests.  No
+ * reference counterpart (the reference's per-pass buffers are private to its pass loop,
+ * CPyOptiXFLARERenderer_CUDA_Forward_training.cu:1004-1131).
+ */
+#ifndef FLARE_PASS_SLOTS
+#define FLARE_PASS_SLOTS 42 /* hits per internal pass; a build with another FLARE_K_PASS sets it too */
+#endif
+int flare_get_pass_hits(flare_renderer *r, int pass, int *count, int *ray_ids, float *t_out, int *idx_out,
+                        void *stream);
+
+/*
  * Allocation-free 16-nearest-hit query.  No counterpart in the reference, whose renderer allocates its
  * scratch in the constructor and in SetGeometry.  For callers that cannot allocate device memory when
  * they call (under a fixed device-memory budget, or as a plugin in a process whose allocator owns the

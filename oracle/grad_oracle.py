@@ -175,7 +175,17 @@ def gradients(scene, O, v, csr, nhits, dL_dI, base=False, bg=(0.0, 0.0, 0.0), re
     C = (W[:, :, None] * Cc).sum(1) + Tincl[:, -1:] * bgv[None, :]
     loss = (dLdI * C).sum()
     if lambda_depth != 0.0:
-        tt = torch.zeros(R, Hm, dtype=dt).index_put((ray_t, pos_t), torch.clamp(reg_a / t + reg_b, 0.0, 1.0))
+        # The reference's depth-regulariser share of dL/dq uses dt/dq without the factor S = 2/|q|^2
+        # (Backward.cu:2096-2110, Backward_base.cu:496-510): the depth term's explicit t is given a
+        # q-gradient scaled by 1/S (values and every other gradient unchanged).
+        q_d = P["q"][idx_t]
+        q_d = q_d.detach() + (q_d - q_d.detach()) / S.detach()[:, None]
+        S_d = 2.0 / (q_d * q_d).sum(1)
+        a_, b_, c_, d_ = q_d[:, 0], q_d[:, 1], q_d[:, 2], q_d[:, 3]
+        N_d = torch.stack([S_d * (b_ * d_ + a_ * c_), S_d * (c_ * d_ - a_ * b_), 1 - S_d * (b_ * b_ + c_ * c_)], 1)
+        t_rd = (N_d * (m - Oh)).sum(1) / (N_d * vh).sum(1)
+        t_d = t_trav + (t_rd - t_rd.detach()) if not exact_t else t_rd
+        tt = torch.zeros(R, Hm, dtype=dt).index_put((ray_t, pos_t), torch.clamp(reg_a / t_d + reg_b, 0.0, 1.0))
         Wb = torch.cumsum(W, 1) - W
         TWb = torch.cumsum(W * tt, 1) - W * tt
         Ld = (4.0 * W * (tt * Wb - TWb)).sum()

@@ -194,3 +194,50 @@ def sh(v):
     out = np.zeros((v.shape[0], 16), np.float32)
     lib().oracle_sh(_p(v), ctypes.c_int(v.shape[0]), _p(out))
     return out
+
+
+def all_hits(frames, O, v, t_min=None, nsides=8, cap=4096):
+    """Every hit of each ray (t >= t_min, default 0) ascending by (t, index), from one brute-force sweep
+    per ray: a list of (t, idx) numpy arrays.  For full-size parity on a few hundred sampled rays."""
+    frames, O, v = _f32(_np(frames)), _f32(_np(O)), _f32(_np(v))
+    R = O.shape[0]
+    t_min = np.zeros(R, np.float32) if t_min is None else _f32(_np(t_min))
+    counts = np.zeros(R, np.int32)
+    t = np.zeros((R, cap), np.float32)
+    idx = np.zeros((R, cap), np.int32)
+    worst = lib().oracle_all_hits(_p(frames), ctypes.c_int(frames.shape[0]), _p(O), _p(v), _p(t_min),
+                                  ctypes.c_int(R), ctypes.c_int(nsides), ctypes.c_int(cap), _p(counts), _p(t), _p(idx))
+    if worst > cap:
+        return all_hits(frames, O, v, t_min, nsides, cap=int(worst) + 64)
+    return [(t[r, :counts[r]].copy(), idx[r, :counts[r]].copy()) for r in range(R)]
+
+
+def restart_passes(t, idx, k):
+    """Splits one ray's sorted hit sequence into the passes of a k-slot buffer that restarts at
+    nextafter(t_k) (Forward_training.cu:929): a pass holds the next k hits at or beyond t_min; hits tied
+    with t_k but later in (t, index) order are skipped by the restart, as the reference's k-buffer skips
+    them.  Returns a list of (t, idx) arrays, the last one shorter than k (possibly empty)."""
+    out = []
+    pos = 0
+    n = len(t)
+    while True:
+        chunk_t, chunk_i = t[pos:pos + k], idx[pos:pos + k]
+        out.append((chunk_t, chunk_i))
+        if len(chunk_t) < k:
+            return out
+        t_next = np.nextafter(chunk_t[-1], np.float32(np.inf), dtype=np.float32)
+        pos += k
+        while pos < n and t[pos] < t_next:
+            pos += 1
+
+
+def csr_from_passes(per_ray_passes):
+    """CSR (off, t, idx) of the concatenated pass lists of every ray (the form forward() and
+    grad_oracle.gradients() read)."""
+    lists_t = [np.concatenate([p[0] for p in ps]) if ps else np.zeros(0, np.float32) for ps in per_ray_passes]
+    lists_i = [np.concatenate([p[1] for p in ps]) if ps else np.zeros(0, np.int32) for ps in per_ray_passes]
+    off = np.zeros(len(lists_t) + 1, np.int64)
+    off[1:] = np.cumsum([len(x) for x in lists_t])
+    tt = np.concatenate(lists_t).astype(np.float32) if lists_t else np.zeros(0, np.float32)
+    ii = np.concatenate(lists_i).astype(np.int32) if lists_i else np.zeros(0, np.int32)
+    return off, tt, ii

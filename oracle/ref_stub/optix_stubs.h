@@ -1,0 +1,2 @@
+#pragma once
+#include "optix_host.h"

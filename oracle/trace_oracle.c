@@ -24,6 +24,8 @@
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
+#include <stdlib.h>
+#include <omp.h>
 
 #define K_HITS 16
 
@@ -199,4 +201,70 @@ void oracle_hits_tmax(const float *frames, int n, const float *O, const float *v
             idx_out[(long)k * R + r] = valid ? ib[k] : -1;
         }
     }
+}
+
+/* Every hit of each ray with t >= t_min[r], ascending by (t, index): the whole sequence the multi-pass
+   k-buffer restarts walk through (shaders.cu:166-188 per pass, Forward_training.cu:929 between passes),
+   found in one brute-force sweep per ray for the full-size parity tests (a few hundred rays).  Ray r's
+   hits go to t_out / idx_out [r * cap, r * cap + counts[r]); returns the largest count, which exceeds
+   cap (and truncates that ray's list) when cap was too small. */
+static int cmp_hit(const void *pa, const void *pb) {
+    const float ta = ((const float *)pa)[0], tb = ((const float *)pb)[0];
+    if (ta < tb) return -1;
+    if (ta > tb) return 1;
+    const int ia = ((const int *)pa)[1], ib = ((const int *)pb)[1];
+    return (ia > ib) - (ia < ib);
+}
+
+int oracle_all_hits(const float *frames, int n, const float *O, const float *v, const float *t_min, int R,
+                    int nsides, int cap, int *counts, float *t_out, int *idx_out) {
+    float pc[64], ps[64];
+    oracle_polygon_constants(nsides, pc, ps);
+    const int nthr = omp_get_max_threads() < 64 ? omp_get_max_threads() : 64;
+    const size_t slice = (size_t)2 * cap;  /* floats per thread slice: (t, index bits) pairs */
+    float *buf = (float *)malloc(sizeof(float) * slice * nthr);
+    float *all = (float *)malloc(sizeof(float) * slice * nthr);
+    int worst = 0;
+    /* few rays, many primitives: the primitives are split over the threads, each appends to its own
+       slice; the slices are concatenated and sorted */
+    for (int r = 0; r < R; ++r) {
+        const float *o = O + 3 * r, *d = v + 3 * r;
+        int cnt_thr[64] = {0};
+#pragma omp parallel num_threads(nthr)
+        {
+            const int tid = omp_get_thread_num();
+            float *mine = buf + slice * tid;
+            int c = 0;
+#pragma omp for schedule(static)
+            for (int i = 0; i < n; ++i) {
+                float t;
+                if (hit_test(frames + 12 * (long)i, o, d, t_min[r], nsides, pc, ps, &t)) {
+                    if (c < cap) {
+                        mine[2 * c] = t;
+                        memcpy(mine + 2 * c + 1, &i, sizeof(int));
+                    }
+                    ++c;
+                }
+            }
+            cnt_thr[tid] = c;
+        }
+        int total = 0, kept = 0;
+        for (int th = 0; th < nthr; ++th) {
+            const int c = cnt_thr[th] < cap ? cnt_thr[th] : cap;
+            memcpy(all + 2 * (size_t)kept, buf + slice * th, sizeof(float) * 2 * c);
+            kept += c;
+            total += cnt_thr[th];
+        }
+        qsort(all, kept, 2 * sizeof(float), cmp_hit);
+        const int keep = kept < cap ? kept : cap;
+        for (int k = 0; k < keep; ++k) {
+            t_out[(long)r * cap + k] = all[2 * k];
+            memcpy(idx_out + (long)r * cap + k, all + 2 * k + 1, sizeof(int));
+        }
+        counts[r] = keep;
+        if (total > worst) worst = total;
+    }
+    free(all);
+    free(buf);
+    return worst;
 }
