@@ -186,3 +186,38 @@ def test_backward_on_sample(full):
         if not e < GRAD_TOL:
             bad[k] = e
     assert not bad, f"config {f.cfg} relative L2 above {GRAD_TOL}: {bad}"
+
+
+def test_config4_secondary_rays_on_sample():
+    """BASELINE config 4 (1M primitives + mirror / glass spheres, 1024 x 1024, recursion depth 3): the whole
+    image on the GPU, 128 sampled primary rays (each with its own tree of reflected / refracted rays)
+    through the oracle's viewer restatement."""
+    from flare_b200.scene import viewer_lights, viewer_spheres
+    from flare_b200.viewer import CPyFlareViewerRenderer
+    from oracle import viewer_oracle
+    W = 1024
+    sc = make_scene(1_000_000, 0)
+    g = sc.to("cuda")
+    O, v = camera_rays(W, W, 60.0, eye=(0.0, 0.0, 3.0))
+    R = W * W
+    r = CPyFlareViewerRenderer(8, 11.3449, R, 3)
+    sph, mat = viewer_spheres()
+    lts = viewer_lights()
+    r.SetGeometry(*[t.contiguous() for t in g.activated()], sph)
+    bm = z(R, 3)
+    r.Forward(g.cond, g.features, g.RGBA[:, :3].contiguous(), g.A1, g.b1, g.A2, g.b2, g.A3, g.b3, O.cuda(), v.cuda(),
+              bm, 0.0, 0.0, 0.0, g.m, g.s, g.q, g.RGBA[:, 3].contiguous(), g.k, 0.01, mat, lts, 1e-4, 0.55, 0.06, 0.06,
+              0.07)
+    frames = r.frames().cpu().numpy()
+    # 64 rays through the spheres' screen region (centre-left / centre-right / upper centre) + 64 random
+    rs = np.random.RandomState(11)
+    ys = np.concatenate([rs.randint(400, 624, 64), rs.randint(0, W, 64)])
+    xs = np.concatenate([rs.randint(250, 774, 64), rs.randint(0, W, 64)])
+    S = np.unique(ys * W + xs)
+    ref, st = viewer_oracle.viewer_forward(frames, sc.__dict__, sph.numpy(), mat.numpy(), lts.numpy(), O[S], v[S],
+                                           bg=(0.0, 0.0, 0.0), T_thr=0.01, eps=1e-4, shadow_mult=0.55,
+                                           Ia=(0.06, 0.06, 0.07), max_depth=3)
+    got = bm[S].cpu().numpy()
+    err = np.abs(got - ref).max(axis=1)
+    assert st["generations"] > 3
+    assert err.max() < RGB_TOL, ((err > RGB_TOL).sum(), err.max())
