@@ -39,7 +39,7 @@ class BackwardArgs(ctypes.Structure):
                 ("dL_dw1", vp), ("dL_db1", vp), ("dL_dw2", vp), ("dL_db2", vp), ("dL_dw3", vp), ("dL_db3", vp),
                 ("depth_reg_accums", vp), ("depth_normal_reg_prefix_sums", vp), ("lambda_depth", ctypes.c_float),
                 ("reg_a", ctypes.c_float), ("reg_b", ctypes.c_float), ("surface_normal", vp),
-                ("lambda_normal", ctypes.c_float)]
+                ("lambda_normal", ctypes.c_float), ("prim_rows", vp)]
 
 
 class ViewerArgs(ctypes.Structure):
@@ -102,6 +102,7 @@ EXPORTS = {
                                          ctypes.c_int, vp]),
     "flare_get_stats": (ctypes.c_int, [vp, ctypes.POINTER(Stats)]),
     "flare_get_frames": (ctypes.c_int, [vp, vp, vp]),
+    "flare_scatter_prim_rows": (ctypes.c_int, [vp, ctypes.c_int, vp, ctypes.c_int] + [vp] * 8),
     "flare_get_pass_hits": (ctypes.c_int, [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int), vp, vp, vp, vp]),
     "flare_profile": (ctypes.c_int, [vp, ctypes.c_int]),
     "flare_get_kernel_times": (ctypes.c_int, [vp, ctypes.POINTER(KernelTimes)]),

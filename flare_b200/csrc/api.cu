@@ -191,7 +191,8 @@ int flare_destroy(flare_renderer *r) {
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
                     r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->T, r->list[0], r->list[1],
-                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->pgrad, r->vw_buf, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats};
+                    r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->pgrad, r->vw_buf, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats,
+                    r->ploc_scratch, r->nodes4, r->bvh4_scratch, r->nodesL};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (r->h_count) cudaFreeHost(r->h_count);
@@ -353,12 +354,28 @@ int flare_backward(flare_renderer *r, const flare_scene *sc, const flare_backwar
               "flare_backward: NULL regulariser buffer");
     if (sc->cond)
         CHECK_ARG(a->dL_dcond && a->dL_dfeatures, "flare_backward: NULL decoder gradient");
+    CHECK_ARG(!a->prim_rows || (reinterpret_cast<uintptr_t>(a->prim_rows) & 15) == 0,
+              "flare_backward: prim_rows must be 16-byte aligned");
     DeviceGuard dg(r->device);
     FLARE_CUDA_TRY(cudaMemsetAsync(r->dstats, 0, ST_NSTATS * sizeof(unsigned long long), S(stream)));
     r->last_stream = S(stream);
     e = run_backward(r, sc, a, S(stream));
     if (e) return e;
     return check_status(r, S(stream), "flare_backward");
+}
+
+static_assert(PROW_FLOATS == FLARE_PRIM_ROW_FLOATS, "the header's row width must match the build's");
+
+int flare_scatter_prim_rows(const float *rows, int n, const void *A1, int decoder, float *dL_dRGB, float *dL_dA,
+                            float *dL_dk, float *dL_dm, float *dL_ds, float *dL_dq, float *dL_dcond, void *stream) {
+    g_err[0] = 0;
+    CHECK_ARG(n >= 0, "flare_scatter_prim_rows: n < 0");
+    CHECK_ARG(decoder == FLARE_DECODER_LUT_PE || decoder == FLARE_DECODER_GRID_SH,
+              "flare_scatter_prim_rows: unknown decoder %d", decoder);
+    if (n == 0) return FLARE_OK;
+    CHECK_ARG(rows && A1 && dL_dRGB && dL_dA && dL_dk && dL_dm && dL_ds && dL_dq && dL_dcond,
+              "flare_scatter_prim_rows: NULL argument");
+    return run_scatter_rows(rows, n, A1, decoder, dL_dRGB, dL_dA, dL_dk, dL_dm, dL_ds, dL_dq, dL_dcond, S(stream));
 }
 
 int flare_get_stats(flare_renderer *r, flare_stats *out) {

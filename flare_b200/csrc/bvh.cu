@@ -136,6 +136,44 @@ static bool use_bvh4() {
     return on;
 }
 
+// Traversal nodes with inline leaf records (NodeL), built after every hierarchy build; FLARE_TRACE_INLINE=0
+// keeps the 64-byte nodes with separate records only.
+bool use_inline_leaves() {
+    static const bool on = [] {
+        const char *e = getenv("FLARE_TRACE_INLINE");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    return on;
+}
+
+// Node i of the binary hierarchy with each leaf child's record copied in (layout: NodeL).
+__global__ void pack_inline_kernel(const Node *__restrict__ nodes, const float4 *__restrict__ rec, int n_internal,
+                                   NodeL *__restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_internal) return;
+    const Node nd = nodes[i];
+    float4 c[8];
+    const int link[2] = {nd.d.x, nd.d.y}, pid[2] = {nd.d.z, nd.d.w};
+    const float box[2][6] = {{nd.a.x, nd.a.y, nd.a.z, nd.a.w, nd.b.x, nd.b.y},
+                             {nd.b.z, nd.b.w, nd.c.x, nd.c.y, nd.c.z, nd.c.w}};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        if (link[j] < 0) {
+            const size_t p = (size_t)(~link[j]);
+            c[4 * j] = rec[3 * p];
+            c[4 * j + 1] = rec[3 * p + 1];
+            c[4 * j + 2] = rec[3 * p + 2];
+        } else {
+            c[4 * j] = make_float4(box[j][0], box[j][1], box[j][2], box[j][3]);
+            c[4 * j + 1] = make_float4(box[j][4], box[j][5], 0.0f, 0.0f);
+            c[4 * j + 2] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        c[4 * j + 3] = make_float4(__int_as_float(link[j]), __int_as_float(pid[j]), 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[i].c[k] = c[k];
+}
+
 static bool use_ploc() {
     static const bool on = [] {
         const char *e = getenv("FLARE_BVH");
@@ -289,6 +327,9 @@ static int grow(flare_renderer *r, int n, cudaStream_t st) {
     cub::DeviceRadixSort::SortPairs(nullptr, tmp, r->morton, r->morton_sorted, r->ids, r->ids_sorted, n, 0, MORTON_END_BIT, st);
     FLARE_CUDA_TRY(cudaMalloc(&r->sort_tmp, tmp));
     if (use_ploc()) FLARE_CUDA_TRY(cudaMalloc(&r->ploc_scratch, ploc_scratch_bytes(n)));
+    cudaFree(r->nodesL);
+    r->nodesL = nullptr;
+    if (use_inline_leaves()) FLARE_CUDA_TRY(cudaMalloc(&r->nodesL, (N > 1 ? N - 1 : 1) * sizeof(NodeL)));
     if (use_bvh4()) {
         FLARE_CUDA_TRY(cudaMalloc(&r->nodes4, (N > 1 ? N - 1 : 1) * sizeof(Node4)));
         FLARE_CUDA_TRY(cudaMalloc(&r->bvh4_scratch, bvh4_scratch_bytes(n)));
@@ -325,6 +366,8 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
         refit_kernel<<<G, B, 0, st>>>(n, r->ids_sorted, r->aabb, r->nodes, r->parent, r->refit_flag, r->rec,
                                       r->frames, r->dstatus);
     }
+    if (r->nodesL && n > 1)
+        pack_inline_kernel<<<(n - 1 + B - 1) / B, B, 0, st>>>(r->nodes, r->rec, n - 1, r->nodesL);
     if (r->nodes4) {
         e = build_bvh4(r->nodes, n, r->nodes4, r->bvh4_scratch, r->dstatus, st);
         if (e) return e;

@@ -62,6 +62,15 @@ struct __align__(128) Node4 {
     int4 link, pid;
 };
 
+// Traversal node with inline leaves (128 bytes, one cache line per visit): child j owns c[4j .. 4j+3].
+// Internal child: c[4j] = (lo.xyz, hi.x), c[4j+1] = (hi.y, hi.z, -, -), c[4j+3].x = link (>= 0).
+// Leaf child: c[4j .. 4j+2] = the primitive's 48-byte traversal record (m, N, U/(e^sx rho), V/(e^sy rho)),
+// c[4j+3] = (link = ~sorted position, original index, -, -).  A leaf is tested straight from the node:
+// no second, dependent fetch of its record.
+struct __align__(128) NodeL {
+    float4 c[8];
+};
+
 // Polygon edge constants for the hit test (host computes them once per renderer).
 struct PolyConst {
     int n;

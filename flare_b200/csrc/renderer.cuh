@@ -25,6 +25,7 @@ struct flare_renderer {
     void *sort_tmp = nullptr;
     void *ploc_scratch = nullptr;               // clustering build scratch (ploc.cu)
     flare::Node4 *nodes4 = nullptr;             // 4-wide collapse of nodes (bvh4.cu), null when not used
+    flare::NodeL *nodesL = nullptr;             // nodes with inline leaf records (bvh.cu), null when not used
     void *bvh4_scratch = nullptr;
     size_t sort_tmp_bytes = 0;
 
@@ -133,6 +134,8 @@ size_t select_temp_bytes(int max_rays);
 int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_args *a, cudaStream_t st);
 int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_args *a, cudaStream_t st);
 int run_viewer_forward(flare_renderer *r, const flare_scene *sc, const flare_viewer_args *a, cudaStream_t st);
+int run_scatter_rows(const float *rows, int n, const void *A1, int decoder, float *dRGB, float *dA, float *dk,
+                     float *dm, float *ds, float *dq, float *dcond, cudaStream_t st);
 int run_adam(const flare_adam_args *a, cudaStream_t st);
 int run_gather_rows(const flare_gather_tensor *t, int n_tensors, const int *src_row, int n_out, int alt_begin,
                     int alt_end, cudaStream_t st);

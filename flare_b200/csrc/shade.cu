@@ -1745,14 +1745,15 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     bo.lambda_depth = a->lambda_depth; bo.reg_a = a->reg_a; bo.reg_b = a->reg_b; bo.lambda_normal = a->lambda_normal;
     bo.gscale = r->gscale;
     bo.dfeat_priv = r->dfeat_priv;
-    if (dec && (size_t)sc->n > r->pgrad_cap) {
+    const bool rows_out = dec && a->prim_rows != nullptr;  // caller-owned rows, scattered by the caller
+    if (dec && !rows_out && (size_t)sc->n > r->pgrad_cap) {
         cudaFree(r->pgrad);
         r->pgrad = nullptr;
         r->pgrad_cap = 0;
         FLARE_CUDA_TRY(cudaMalloc(&r->pgrad, (size_t)sc->n * PROW_FLOATS * sizeof(float)));
         r->pgrad_cap = sc->n;
     }
-    bo.pgrad = r->pgrad;
+    bo.pgrad = rows_out ? a->prim_rows : r->pgrad;
     bo.vec4 = (reinterpret_cast<uintptr_t>(a->dL_dq) & 15) == 0;
     init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
@@ -1767,7 +1768,8 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
                                                                              r->gscale);
         grad_scale_finish_kernel<<<1, 1, 0, st>>>(r->gscale);
         FLARE_CUDA_TRY(cudaMemsetAsync(r->dfeat_priv, 0, (size_t)r->num_sms * 2 * LUT_PRIV_STRIDE * sizeof(float), st));
-        if (sc->n > 0) FLARE_CUDA_TRY(cudaMemsetAsync(r->pgrad, 0, (size_t)sc->n * PROW_FLOATS * sizeof(float), st));
+        if (sc->n > 0 && !rows_out)
+            FLARE_CUDA_TRY(cudaMemsetAsync(r->pgrad, 0, (size_t)sc->n * PROW_FLOATS * sizeof(float), st));
         FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             SM_BWD_BYTES));
         FLARE_CUDA_TRY(cudaFuncSetAttribute(shade_bwd_kernel<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1827,12 +1829,24 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         pack_dw_kernel<<<32, 256, 0, st>>>(r->dw, a->dL_dw1, a->dL_db1, a->dL_dw2, a->dL_db2, a->dL_dw3, a->dL_db3);
         const int nfeat = sc->decoder ? Dec<1>::FEATS : Dec<0>::FEATS;
         reduce_lut_kernel<<<(nfeat + 255) / 256, 256, 0, st>>>(r->dfeat_priv, r->num_sms * 2, a->dL_dfeatures, nfeat);
-        if (sc->n > 0)
+        if (sc->n > 0 && !rows_out)
             scatter_prow_kernel<<<std::min((sc->n + 7) / 8, r->num_sms * 8), 256, 0, st>>>(
                 r->pgrad, sc->n, static_cast<const __half *>(sc->A1), a->dL_dm, a->dL_ds, a->dL_dq, a->dL_dRGB,
                 a->dL_dA, a->dL_dk, a->dL_dcond, sc->decoder ? Dec<1>::COND : Dec<0>::COND);
         FLARE_CUDA_TRY(cudaGetLastError());
     }
+    return FLARE_OK;
+}
+
+int run_scatter_rows(const float *rows, int n, const void *A1, int decoder, float *dRGB, float *dA, float *dk,
+                     float *dm, float *ds, float *dq, float *dcond, cudaStream_t st) {
+    if (n <= 0) return FLARE_OK;
+    int dev = 0, sms = 148;
+    FLARE_CUDA_TRY(cudaGetDevice(&dev));
+    FLARE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    scatter_prow_kernel<<<std::min((n + 7) / 8, sms * 8), 256, 0, st>>>(
+        rows, n, static_cast<const __half *>(A1), dm, ds, dq, dRGB, dA, dk, dcond, decoder ? Dec<1>::COND : Dec<0>::COND);
+    FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
 }
 

@@ -465,6 +465,167 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
 }
 
 
+// The persistent heap traversal over nodes with inline leaf records (NodeL): one 128-byte line per visit
+// carries both child boxes or, for a leaf child, the primitive's whole record, so the exact hit test of a
+// leaf needs no further fetch.  A leaf child is tested by every lane still tracing the node (the exact
+// test rejects on t and on the polygon, so it subsumes the leaf box the 64-byte layout tests first); the
+// next node's fetch is issued before the leaf tests.  Same hits, same order as trace_heap_kernel.
+template <bool STATS, int K>
+__global__ void __launch_bounds__(128, 5) trace_heapL_kernel(
+    const float *__restrict__ O_, const float *__restrict__ v_, const float *__restrict__ tmin_,
+    const int *__restrict__ ray_ids, int count, const NodeL *__restrict__ nodes, const float4 *__restrict__ rec,
+    const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
+    const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
+    const float *__restrict__ tmax_, int *__restrict__ chunk_ctr) {
+    __shared__ int s_node[4][TRACE_STACK];
+    __shared__ unsigned s_mask[4][TRACE_STACK];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    unsigned long long nprim = 0, nnode = 0;
+    extern __shared__ __align__(16) unsigned char heap_smem[];
+    while (true) {
+        int b0 = 0;
+        if (lane == 0) b0 = atomicAdd(chunk_ctr, 32);
+        const int base = __shfl_sync(0xffffffffu, b0, 0);
+        if (base >= count) break;
+        const int j = base + lane;
+        const bool live = j < count;
+        int ray = live ? (ray_ids ? ray_ids[j] : j) : 0;
+        float3 O = make_float3(0, 0, 0), v = make_float3(0, 0, 1);
+        float t_min = INFINITY, tcap = INFINITY;
+        if (live) {
+            O = make_float3(O_[3 * (size_t)ray], O_[3 * (size_t)ray + 1], O_[3 * (size_t)ray + 2]);
+            v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
+            t_min = tmin_[ray];
+            if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
+        }
+        HeapBuf<K> kb;
+        kb.t = reinterpret_cast<float *>(heap_smem);
+        kb.i = reinterpret_cast<int *>(heap_smem + (size_t)K * 128 * sizeof(float));
+        for (int k = 0; k < K; ++k) {
+            kb.t[k * 128 + threadIdx.x] = INFINITY;
+            kb.i[k * 128 + threadIdx.x] = 0x7fffffff;
+        }
+        kb.rt = INFINITY;
+        kb.ri = 0x7fffffff;
+        const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
+                                      1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
+                                      1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
+        const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);
+        const bool want = live && t_min < INFINITY;
+        if (n == 1) {
+            float t;
+            if (want) {
+                ++nprim;
+                if (hit_prim(rec, 0, O, v, t_min, poly, t, tcap)) heap_insert(kb, t, ids[0]);
+            }
+        } else if (n > 1) {
+            unsigned mask = __ballot_sync(0xffffffffu, want);
+            int sp = 0;
+            const unsigned long long max_visits = 2ull * (unsigned long long)n + 64ull;
+            float4 c[8];
+            {
+                const float4 *np = nodes[0].c;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) c[k] = __ldg(np + k);
+            }
+            while (mask) {
+                if (++nnode > max_visits) {
+                    if (lane == 0) atomicOr(status, ERR_INDEX);
+                    break;
+                }
+                const bool in = (mask >> lane) & 1u;
+                const int link0 = __float_as_int(c[3].x), link1 = __float_as_int(c[7].x);
+                const bool leaf0 = link0 < 0, leaf1 = link1 < 0;  // warp-uniform
+                const float bk = fminf(kb.rt, tcap);
+                const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
+                float t0 = 0.0f, t1 = 0.0f;
+                const bool i0 = in && !leaf0 && slab(c[0].x, c[0].y, c[0].z, c[0].w, c[1].x, c[1].y, O, iv, tlo, thi, t0);
+                const bool i1 = in && !leaf1 && slab(c[4].x, c[4].y, c[4].z, c[4].w, c[5].x, c[5].y, O, iv, tlo, thi, t1);
+                const unsigned m0 = __ballot_sync(0xffffffffu, i0), m1 = __ballot_sync(0xffffffffu, i1);
+                int next = -1;
+                unsigned nmask = 0;
+                if (m0 && m1) {
+                    const unsigned v0 = __ballot_sync(0xffffffffu, i0 && (!i1 || t0 <= t1));
+                    const bool first0 = __popc(v0) * 2 >= __popc(m0 | m1);
+                    if (sp < TRACE_STACK) {
+                        if (lane == 0) {
+                            s_node[wib][sp] = first0 ? link1 : link0;
+                            s_mask[wib][sp] = first0 ? m1 : m0;
+                        }
+                        ++sp;
+                    } else if (lane == 0) {
+                        atomicOr(status, ERR_STACK);
+                    }
+                    next = first0 ? link0 : link1;
+                    nmask = first0 ? m0 : m1;
+                } else if (m0) {
+                    next = link0;
+                    nmask = m0;
+                } else if (m1) {
+                    next = link1;
+                    nmask = m1;
+                } else {
+                    __syncwarp();
+                    if (sp > 0) {
+                        --sp;
+                        next = s_node[wib][sp];
+                        nmask = s_mask[wib][sp];
+                    }
+                }
+                float4 nc[8];
+                if (next >= 0) {
+                    const float4 *nq = nodes[next].c;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) nc[k] = __ldg(nq + k);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) nc[k] = c[k];
+                }
+                if (leaf0 && in) {
+                    float t;
+                    ++nprim;
+                    if (hit_rec(c[0], c[1], c[2], O, v, t_min, poly, t, bk)) {
+                        const int pid = __float_as_int(c[3].y);
+                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                    }
+                }
+                if (leaf1 && in) {
+                    float t;
+                    ++nprim;
+                    if (hit_rec(c[4], c[5], c[6], O, v, t_min, poly, t, bk)) {
+                        const int pid = __float_as_int(c[7].y);
+                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                    }
+                }
+                __syncwarp();
+                if (next < 0) break;
+                mask = nmask;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) c[k] = nc[k];
+            }
+        }
+        if (live) {  // heap sort: the largest key leaves first, into the last slot
+            for (int k = K - 1; k >= 0; --k) {
+                const float tk = kb.t[threadIdx.x];
+                const int ik = kb.i[threadIdx.x];
+                const bool valid = ik != 0x7fffffff;
+                t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
+                idx_out[(size_t)k * stride + j] = valid ? ik : -1;
+                if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
+            }
+        }
+        __syncwarp();
+    }
+    if (STATS) {
+        for (int o = 16; o > 0; o >>= 1) nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
+        if (lane == 0 && (nprim | nnode)) {
+            atomicAdd(stats + ST_PRIM_TESTS, nprim);
+            atomicAdd(stats + ST_NODES, nnode);
+        }
+    }
+}
+
+
 // The heap traversal over the 4-wide hierarchy: one 128-byte line per visit, four box tests per lane;
 // entered internal children are visited nearest first (by the warp's nearest entry distance), the
 // others pushed; the next node's fetch is issued before this node's leaf tests.  The stack holds node
@@ -962,6 +1123,21 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
         return FLARE_OK;
     }
     static const bool persist = getenv_int("FLARE_TRACE_PERSIST", 1) != 0;
+    if (k == K_PASS && K_PASS != K_HITS && heap && persist && r->nodesL) {
+        const size_t smem = (size_t)K_PASS * 128 * 8;
+        FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heapL_kernel<true, K_PASS>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        int per_sm = 0;
+        FLARE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trace_heapL_kernel<true, K_PASS>, B,
+                                                                     smem));
+        const int grid = std::max(1, std::min((count + B - 1) / B, r->num_sms * std::max(per_sm, 1)));
+        FLARE_CUDA_TRY(cudaMemsetAsync(r->counters + 2, 0, sizeof(int), st));
+        trace_heapL_kernel<true, K_PASS><<<grid, B, smem, st>>>(
+            O, v, t_min, ray_ids, count, r->nodesL, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,
+            r->dstatus, r->dstats, t_max, r->counters + 2);
+        FLARE_CUDA_TRY(cudaGetLastError());
+        return FLARE_OK;
+    }
     if (k == K_PASS && K_PASS != K_HITS && heap && persist) {
         const size_t smem = (size_t)K_PASS * 128 * 8;
         FLARE_CUDA_TRY(cudaFuncSetAttribute(trace_heap_kernel<true, K_PASS, true>,

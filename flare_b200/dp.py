@@ -5,7 +5,9 @@ train.py:449-858: SetGeometry on the activated parameters, Forward_training over
 loss and its gradient in torch, Backward into zeroed gradient buffers.  Here the same step runs on N
 ranks: the scene is replicated, the rays of the step's views are sharded by view (and by row band when
 there are more ranks than views), each rank renders and back-propagates its shard into one flat fp32
-gradient buffer, and a single all-reduce (NCCL over NVLink) sums that buffer once per step.  The loss is
+gradient buffer, and a single all-reduce (NCCL over NVLink) sums that buffer once per step.  With the
+decoder, that buffer holds each primitive's 80-float gradient row (flare_backward_args.prim_rows)
+rather than its 110 expanded gradient floats; the rows expand after the exchange.  The loss is
 normalised by the global ray count, so the summed gradient equals the single-GPU gradient of the whole
 batch.
 
@@ -42,45 +44,72 @@ def shard_rays(n_views: int, rays_per_view: int, world: int, rank: int):
     return [(v, lo, hi - lo)]
 
 
-# gradient tensors of one step, in the order they sit in the flat buffer: name -> shape (N = primitives)
+PRIM_ROW = 80  # FLARE_PRIM_ROW_FLOATS: [dm 3 | ds 2 | dq 4 | dRGB 3 | dA 1 | dk 1 | 0 0 | d1 64]
+PER_PRIM = ("RGB", "A", "k", "m", "s", "q", "cond")
+
+
 def grad_layout(n: int, decoder: bool, cond_dim: int = 96, n_features: int = 13154):
-    lay = [("loss", (1,)), ("RGB", (n, 3)), ("A", (n, 1)), ("k", (n, 1)), ("m", (n, 3)), ("s", (n, 2)), ("q", (n, 4))]
-    if decoder:
-        lay += [("cond", (n, cond_dim)), ("features", (n_features,)), ("w3", (1, 512)), ("b3", (1, 64)), ("w2", (1, 4096)),
-                ("b2", (1, 512)), ("w1", (1, 8192)), ("b1", (1, 512))]
-    return lay
+    """(exchanged, local) segments of one step's gradients: name -> shape (N = primitives).  The decoder
+    path exchanges each primitive's 80-float row (its geometry / colour gradients and the sum of its
+    layer-1 deltas, from which the descriptor gradient is formed after the exchange: it is linear in
+    them) instead of the 14 + descriptor-width floats of the expanded gradients; those stay local."""
+    per = [("RGB", (n, 3)), ("A", (n, 1)), ("k", (n, 1)), ("m", (n, 3)), ("s", (n, 2)), ("q", (n, 4))]
+    if not decoder:
+        return [("loss", (1,))] + per, []
+    exch = [("loss", (1,)), ("rows", (n, PRIM_ROW)), ("features", (n_features,)), ("w3", (1, 512)), ("b3", (1, 64)),
+            ("w2", (1, 4096)), ("b2", (1, 512)), ("w1", (1, 8192)), ("b1", (1, 512))]
+    return exch, per + [("cond", (n, cond_dim))]
 
 
 class GradBuffer:
-    """All gradients of a step as views into one contiguous fp32 buffer (one all-reduce per step)."""
+    """All gradients of a step as views into contiguous fp32 buffers: `flat`, summed over ranks by one
+    all-reduce per step, and (decoder path) `local`, the per-primitive gradients that
+    expand_rows_() forms from the summed rows."""
 
     ALIGN = 16  # floats: every segment starts on a 64-byte boundary (the kernels use vector reductions)
 
     def __init__(self, n: int, decoder: bool, device, cond_dim: int = 96, n_features: int = 13154):
-        self.layout = grad_layout(n, decoder, cond_dim, n_features)
+        self.n, self.decoder = n, decoder
+        exch, local = grad_layout(n, decoder, cond_dim, n_features)
+        self.layout = exch + local
+        self.views = {}
+        self.flat = self._alloc(exch, device)
+        self.local = self._alloc(local, device)
+
+    def _alloc(self, layout, device):
         offs, off = [], 0
-        for _, shape in self.layout:
+        for _, shape in layout:
             offs.append(off)
             cnt = int(torch.tensor(shape).prod())
             off += (cnt + self.ALIGN - 1) // self.ALIGN * self.ALIGN
-        self.flat = torch.zeros(off, dtype=torch.float32, device=device)
-        self.views = {}
-        for (name, shape), o in zip(self.layout, offs):
+        buf = torch.zeros(off, dtype=torch.float32, device=device)
+        for (name, shape), o in zip(layout, offs):
             cnt = int(torch.tensor(shape).prod())
-            self.views[name] = self.flat[o:o + cnt].view(*shape)
+            self.views[name] = buf[o:o + cnt].view(*shape)
+        return buf
 
     def __getitem__(self, k):
         return self.views[k]
 
     def zero_(self):
         self.flat.zero_()
+        self.local.zero_()
 
     def allreduce_(self, group=None):
         if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
             dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
 
+    def expand_rows_(self, A1, decoder_kind: int):
+        """Adds the (summed) per-primitive rows into the per-primitive gradients (decoder path)."""
+        if self.decoder:
+            from .renderer import scatter_prim_rows
+            v = self.views
+            scatter_prim_rows(v["rows"], A1, decoder_kind, v["RGB"], v["A"], v["k"], v["m"], v["s"], v["q"],
+                              v["cond"])
+
     @property
     def nbytes(self):
+        """Bytes summed over ranks per step."""
         return self.flat.numel() * 4
 
 
@@ -156,10 +185,13 @@ class TrainStep:
                 r.Backward(*dec, sh.O, sh.v, *self.bg, sc.m, sc.s, sc.q, sc.RGBA, sc.k, I, b["dLdI"], G["RGB"], G["A"],
                            G["k"], G["w3"], G["b3"], G["w2"], G["b2"], G["w1"], G["b1"], G["cond"], G["features"],
                            G["m"], G["s"], G["q"], T_THRESHOLD_TRAINING, b["dacc"], b["prefix"],
-                           self.lambda_depth, REG_A, REG_B, b["dai"], b["sn"], b["nacc"], self.lambda_normal)
+                           self.lambda_depth, REG_A, REG_B, b["dai"], b["sn"], b["nacc"], self.lambda_normal,
+                           prim_rows=G["rows"])
             else:
                 r.Backward_base(sh.O, sh.v, *self.bg, sc.m, sc.s, sc.q, sc.RGBA, sc.k, I, b["dLdI"], G["RGB"], G["A"],
                                 G["k"], G["m"], G["s"], G["q"], T_THRESHOLD_TRAINING, b["dacc"], b["prefix"],
                                 self.lambda_depth, REG_A, REG_B, b["dai"], b["sn"], b["nacc"], self.lambda_normal)
         G.allreduce_(self.group)
+        if self.decoder:
+            G.expand_rows_(sc.A1, 1 if sc.cond.shape[1] == 32 else 0)
         return self.loss

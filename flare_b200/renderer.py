@@ -25,6 +25,7 @@ from . import _lib
 
 F32, F16, I32 = torch.float32, torch.float16, torch.int32
 PASS_SLOTS = 42  # FLARE_PASS_SLOTS: hit slots of an internal traversal pass
+PRIM_ROW = 80    # FLARE_PRIM_ROW_FLOATS: floats of a per-primitive gradient row
 
 # decoder kind -> (descriptor width, feature-table floats): 0 = the reference's LUT / sin-cos / 96-wide
 # decoder, 1 = the dense-grid / spherical-harmonics / 32-wide variant (include/flare_b200.h)
@@ -252,15 +253,18 @@ class CPyOptiXFLARERenderer:
                  bg_color_G, bg_color_B, m, s, q, RGBA, kappa, I, dL_dI, dL_dRGB, dL_dA, dL_d_kappa, dL_dw3, dL_db3,
                  dL_dw2, dL_db2, dL_dw1, dL_db1, dL_d_conditioning, dL_d_deatures, dL_dm, dL_ds, dL_dq, T_threshold,
                  depth_reg_accums, depth_normal_reg_prefix_sums, lambda_depth, reg_a, reg_b, depth_and_index,
-                 surface_normal, normal_reg_accums, lambda_normal):
+                 surface_normal, normal_reg_accums, lambda_normal, prim_rows=None):
+        """prim_rows (extension, keyword only): a caller-zeroed (N, 80) f32 tensor that receives the
+        per-primitive gradient rows instead of dL_dRGB .. dL_dq and dL_d_conditioning (see
+        scatter_prim_rows), for data-parallel callers that sum the rows over ranks."""
         sc = self._scene(m, s, q, RGBA, kappa, (conditioning_variable, features_P_hit_object, A1, b1, A2, b2, A3, b3))
         dec = (dL_dw3, dL_db3, dL_dw2, dL_db2, dL_dw1, dL_db1, dL_d_conditioning, dL_d_deatures)
         self._backward(sc, O, v, (bg_color_R, bg_color_G, bg_color_B), I, dL_dI, dL_dRGB, dL_dA, dL_d_kappa, dL_dm,
                        dL_ds, dL_dq, dec, T_threshold, depth_reg_accums, depth_normal_reg_prefix_sums, lambda_depth,
-                       reg_a, reg_b, surface_normal, lambda_normal)
+                       reg_a, reg_b, surface_normal, lambda_normal, prim_rows)
 
     def _backward(self, sc, O, v, bg, I, dL_dI, dL_dRGB, dL_dA, dL_dk, dL_dm, dL_ds, dL_dq, dec, T_threshold,
-                  depth_reg_accums, prefix, lambda_depth, reg_a, reg_b, surface_normal, lambda_normal):
+                  depth_reg_accums, prefix, lambda_depth, reg_a, reg_b, surface_normal, lambda_normal, prim_rows=None):
         R = self._rays(O, v)
         n, dv = self._n, self.device
         a = _lib.BackwardArgs(O=_ptr(O), v=_ptr(v), n_rays=R, T_threshold=float(T_threshold),
@@ -292,6 +296,9 @@ class CPyOptiXFLARERenderer:
                 raise ValueError(f"dL_d_features: expected {nfeat} elements")
             a.dL_dw1, a.dL_db1, a.dL_dw2, a.dL_db2 = _ptr(dw1), _ptr(db1), _ptr(dw2), _ptr(db2)
             a.dL_dw3, a.dL_db3, a.dL_dcond, a.dL_dfeatures = _ptr(dw3), _ptr(db3), _ptr(dcond), _ptr(dfeat)
+            if prim_rows is not None:
+                _need(prim_rows, "prim_rows", F32, (n, PRIM_ROW), dv)
+                a.prim_rows = _ptr(prim_rows)
         _lib.check(self._lib.flare_backward(self._h, ctypes.byref(sc), ctypes.byref(a), self._stream()), "Backward")
 
     # ------------------------------------------------------------------------------ extras
@@ -335,6 +342,26 @@ class CPyOptiXFLARERenderer:
         out = torch.empty((self._n, 12), dtype=F32, device=f"cuda:{self.device}")
         _lib.check(self._lib.flare_get_frames(self._h, _ptr(out), self._stream()), "frames")
         return out
+
+
+def scatter_prim_rows(rows, A1, decoder, dL_dRGB, dL_dA, dL_dk, dL_dm, dL_ds, dL_dq, dL_d_conditioning):
+    """Adds per-primitive gradient rows (N, 80) -- from Backward(..., prim_rows=...), possibly summed over
+    data-parallel ranks -- into the per-primitive gradients (flare_scatter_prim_rows)."""
+    lib = _lib.load()
+    n = rows.shape[0]
+    dv = rows.device.index
+    _need(rows, "rows", F32, (n, PRIM_ROW), dv)
+    _need(A1, "A1", F16, (64, 128), dv)
+    cdim, _ = DECODERS[int(decoder)]
+    for t, nm, w in ((dL_dRGB, "dL_dRGB", 3), (dL_dA, "dL_dA", 1), (dL_dk, "dL_d_kappa", 1), (dL_dm, "dL_dm", 3),
+                     (dL_ds, "dL_ds", 2), (dL_dq, "dL_dq", 4), (dL_d_conditioning, "dL_d_conditioning", cdim)):
+        _need(t, nm, F32, None, dv)
+        if t.numel() != n * w:
+            raise ValueError(f"{nm}: {t.numel()} elements, expected {n * w}")
+    stream = ctypes.c_void_p(torch.cuda.current_stream(rows.device).cuda_stream)
+    _lib.check(lib.flare_scatter_prim_rows(_ptr(rows), n, _ptr(A1), int(decoder), _ptr(dL_dRGB), _ptr(dL_dA),
+                                           _ptr(dL_dk), _ptr(dL_dm), _ptr(dL_ds), _ptr(dL_dq),
+                                           _ptr(dL_d_conditioning), stream), "scatter_prim_rows")
 
 
 def GenerateRays(R, D, F, width, height, fov_X, fov_Y):

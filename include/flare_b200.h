@@ -166,6 +166,12 @@ typedef struct flare_backward_args {
     float lambda_depth, reg_a, reg_b;
     const float *surface_normal;             /* (R,3) */
     float lambda_normal;
+    /* Decoder path only, optional (NULL: off).  When set, the per-primitive gradients are ACCUMULATED
+       (+=) into these caller-zeroed rows (N, FLARE_PRIM_ROW_FLOATS), 16-byte aligned, and dL_dRGB, dL_dA,
+       dL_dk, dL_dm, dL_ds, dL_dq and dL_dcond are left untouched; flare_scatter_prim_rows turns the rows
+       into them.  Data-parallel callers sum the rows over ranks first: a row is 80 floats where the
+       outputs it expands to are 14 + the descriptor width (110 for the reference decoder). */
+    float *prim_rows;
 } flare_backward_args;
 
 /*
@@ -174,6 +180,20 @@ typedef struct flare_backward_args {
  * (CPyOptiXFLARERenderer.cpp:345-450 -> *_Backward_base.cu:641-804) when it is NULL.
  */
 int flare_backward(flare_renderer *r, const flare_scene *scene, const flare_backward_args *a, void *stream);
+
+/*
+ * Per-primitive gradient rows of the decoder backward (flare_backward_args.prim_rows): row p =
+ * [dm 3, ds 2, dq 4, dRGB 3, dA 1, dk 1, 0 0 | d1 64], d1 = the sum over p's hits of the gradient of
+ * layer 1's pre-activations.  The descriptor gradient is linear in d1 (dcond = W1[:, 32:32+C]^T d1,
+ * C the descriptor width), so rows summed over data-parallel ranks expand to the summed gradients.
+ * flare_scatter_prim_rows adds row p's parts into dm / ds / dq / dRGB / dA / dk and W1[:, 32:]^T d1
+ * into dcond (all (N, .) f32 device arrays, accumulated), for n rows; A1 is the (64,128) f16 weight,
+ * decoder a FLARE_DECODER_* kind.  Rows that are all zero are skipped.  No reference counterpart (the
+ * reference writes its per-hit gradients straight into the outputs, Backward.cu:1300-2234).
+ */
+#define FLARE_PRIM_ROW_FLOATS 80
+int flare_scatter_prim_rows(const float *rows, int n, const void *A1, int decoder, float *dL_dRGB, float *dL_dA,
+                            float *dL_dk, float *dL_dm, float *dL_ds, float *dL_dq, float *dL_dcond, void *stream);
 
 /*
  * Secondary rays (replaces CPyOptiXFLAREVIEWERRenderer::Forward, source/viewer_renderer/

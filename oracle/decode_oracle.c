@@ -27,6 +27,7 @@
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
+#include <omp.h>
 
 #define K_HITS 16
 #define LUT_SCALE 0.29689279887990428378374198030042f
@@ -403,5 +404,69 @@ long oracle_viewer_composite(const float *m, const float *s, const float *q, con
         T_io[r] = T;
         for (int c = 0; c < 3; ++c) rgb_io[3 * (long)r + c] = rgb[c];
     }
+    return total;
+}
+
+/*
+ * The whole forward of the reference on the CPU (the timed CPU baseline): per ray, passes of
+ * 16-nearest queries on the CPU hierarchy (oracle_bvh_build) restarting at nextafter(t_16)
+ * (Forward_training.cu:1004-1131), each shaded by shade_pass until the ray terminates.  OpenMP over
+ * rays.  Outputs as oracle_shade_csr; the composited hits of ray r go to hit_t / hit_idx
+ * [r * cap, r * cap + nhits[r]) (cap >= nhits or the excess is dropped from the list, not the image).
+ * times[0] / times[1]: thread-seconds spent in traversal / shading.
+ */
+void oracle_bvh_hits_one(const void *h, int nsides, const float *pc, const float *ps, const float *O, const float *v,
+                         float t_min, float *tb, int *ib);
+void oracle_polygon_constants(int nsides, float *c, float *s);
+
+long oracle_render_bvh(const void *bvh, int nsides, const float *m, const float *s, const float *q, const float *RGBA,
+                       const float *k, const void *cond, const float *features, const void *A1, const float *b1,
+                       const void *A2, const float *b2, const void *A3, const float *b3, int mode, const float *bg,
+                       float T_thr, float reg_a, float reg_b, const float *O, const float *v, int R, int cap,
+                       float *hit_t, int *hit_idx, float *rgb, float *Tout, int *nhits, double *times, int decoder) {
+    oscene S = {m, s, q, RGBA, k, (const _Float16 *)cond, features, (const _Float16 *)A1, (const _Float16 *)A2,
+                (const _Float16 *)A3, b1, b2, b3, NULL, decoder};
+    oparams P;
+    P.mode = mode;
+    P.bg[0] = bg[0]; P.bg[1] = bg[1]; P.bg[2] = bg[2];
+    P.T_thr = T_thr; P.reg_a = reg_a; P.reg_b = reg_b;
+    float pc[64], ps[64];
+    oracle_polygon_constants(nsides, pc, ps);
+    long total = 0;
+    double t_trace = 0.0, t_shade = 0.0;
+#pragma omp parallel for schedule(dynamic, 16) reduction(+ : total, t_trace, t_shade)
+    for (int r = 0; r < R; ++r) {
+        oray st;
+        memset(&st, 0, sizeof(st));
+        st.T = 1.0f;
+        st.med_t = INFINITY;
+        st.med_idx = -1;
+        int cnt = 0, kept = 0;
+        float t_min = 0.0f;
+        for (;;) {
+            float tb[K_HITS];
+            int ib[K_HITS];
+            const double w0 = omp_get_wtime();
+            oracle_bvh_hits_one(bvh, nsides, pc, ps, O + 3 * r, v + 3 * r, t_min, tb, ib);
+            const double w1 = omp_get_wtime();
+            const int before = st.hits;
+            const int act = shade_pass(&S, &P, O + 3 * r, v + 3 * r, tb, ib, K_HITS, NULL, &st, &cnt);
+            t_trace += w1 - w0;
+            t_shade += omp_get_wtime() - w1;
+            for (int h = 0; h < st.hits - before && kept < cap; ++h, ++kept) {
+                hit_t[(long)r * cap + kept] = tb[h];
+                hit_idx[(long)r * cap + kept] = ib[h];
+            }
+            if (!act) break;
+            t_min = nextafterf(tb[K_HITS - 1], INFINITY);
+        }
+        finish_ray(&P, &st);
+        total += cnt;
+        for (int c = 0; c < 3; ++c) rgb[3 * r + c] = st.rgb[c];
+        if (Tout) Tout[r] = st.T;
+        nhits[r] = kept;
+    }
+    times[0] = t_trace;
+    times[1] = t_shade;
     return total;
 }

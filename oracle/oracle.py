@@ -43,6 +43,11 @@ def lib():
         _lib.oracle_shade_csr.restype = ctypes.c_long
         _lib.oracle_next_tmin.restype = ctypes.c_float
         _lib.oracle_next_tmin.argtypes = [ctypes.c_float]
+        _lib.oracle_bvh_build.restype = ctypes.c_void_p
+        _lib.oracle_bvh_build.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        _lib.oracle_bvh_free.argtypes = [ctypes.c_void_p]
+        _lib.oracle_bvh_hits.argtypes = [ctypes.c_void_p] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 2 + \
+            [ctypes.c_void_p] * 2
     return _lib
 
 
@@ -241,3 +246,58 @@ def csr_from_passes(per_ray_passes):
     tt = np.concatenate(lists_t).astype(np.float32) if lists_t else np.zeros(0, np.float32)
     ii = np.concatenate(lists_i).astype(np.int32) if lists_i else np.zeros(0, np.int32)
     return off, tt, ii
+
+
+class CpuBvh:
+    """The oracle's CPU hierarchy over a scene's frames (oracle_bvh_build): hits(O, v, t_min) gives the same
+    16-nearest lists as hits() without scanning every primitive.  Keeps `frames` alive."""
+
+    def __init__(self, frames, nsides=8):
+        self.frames = _f32(_np(frames))
+        self.nsides = nsides
+        self.h = lib().oracle_bvh_build(_p(self.frames), ctypes.c_int(self.frames.shape[0]))
+
+    def hits(self, O, v, t_min):
+        O, v, t_min = (_f32(_np(x)) for x in (O, v, t_min))
+        R = O.shape[0]
+        t = np.zeros((K, R), np.float32)
+        idx = np.zeros((K, R), np.int32)
+        lib().oracle_bvh_hits(ctypes.c_void_p(self.h), _p(O), _p(v), _p(t_min), ctypes.c_int(R),
+                              ctypes.c_int(self.nsides), _p(t), _p(idx))
+        return t, idx
+
+    def render(self, scene, O, v, mode="training", base=False, bg=(0.0, 0.0, 0.0), T_thr=1e-4, reg_a=0.0, reg_b=0.0,
+               cap=512):
+        """The reference's forward on the CPU end to end (oracle_render_bvh): multi-pass 16-nearest queries on
+        this hierarchy, each pass decoded and composited until the ray terminates.  Returns (rgb, CSR of the
+        composited hits, nhits, traversal thread-seconds, shading thread-seconds)."""
+        S = scene_arrays(scene)
+        O, v = _f32(_np(O)), _f32(_np(v))
+        R = O.shape[0]
+        rgb = np.zeros((R, 3), np.float32)
+        T = np.zeros(R, np.float32)
+        nh = np.zeros(R, np.int32)
+        ht = np.zeros((R, cap), np.float32)
+        hi = np.zeros((R, cap), np.int32)
+        times = np.zeros(2, np.float64)
+        bgv = _f32(bg)
+        G = lambda k_: _p(S.get(k_)) if not base else None  # noqa: E731
+        lib().oracle_render_bvh(
+            ctypes.c_void_p(self.h), ctypes.c_int(self.nsides), _p(S["m"]), _p(S["s"]), _p(S["q"]), _p(S["RGBA"]),
+            _p(S["k"]), G("cond"), G("features"), G("A1"), G("b1"), G("A2"), G("b2"), G("A3"), G("b3"),
+            ctypes.c_int(MODES[mode]), _p(bgv), ctypes.c_float(T_thr), ctypes.c_float(reg_a), ctypes.c_float(reg_b),
+            _p(O), _p(v), ctypes.c_int(R), ctypes.c_int(cap), _p(ht), _p(hi), _p(rgb), _p(T), _p(nh), _p(times),
+            ctypes.c_int(decoder_of(S)))
+        off = np.zeros(R + 1, np.int64)
+        off[1:] = np.cumsum(nh)
+        tt = np.concatenate([ht[r, :nh[r]] for r in range(R)]) if R else np.zeros(0, np.float32)
+        ii = np.concatenate([hi[r, :nh[r]] for r in range(R)]) if R else np.zeros(0, np.int32)
+        return rgb, (off, tt, ii), nh, float(times[0]), float(times[1])
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                lib().oracle_bvh_free(ctypes.c_void_p(self.h))
+                self.h = None
+        except Exception:  # interpreter shutdown
+            pass

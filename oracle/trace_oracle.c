@@ -268,3 +268,218 @@ int oracle_all_hits(const float *frames, int n, const float *O, const float *v, 
     free(buf);
     return worst;
 }
+
+/* ------------------------------------------------------------------------------------------------
+ * CPU bounding-volume hierarchy for the timed CPU baseline (bench.py) and the large-scene oracle runs:
+ * the same k-nearest query as oracle_hits, culled by a binary hierarchy over conservative primitive
+ * boxes.  Culling is conservative and the hit test is the exact one above, so the hits equal the
+ * brute-force search bit for bit (tests/test_oracle.py checks it).
+ *
+ * Build: primitives sorted by a 30-bit Morton code of their centres, then ranges split at the highest
+ * differing code bit (at the middle when the codes are equal) down to leaves of at most 4 primitives;
+ * boxes bottom-up.  Box of a primitive: the polygon lies in the ellipse m + a U' + b V' (a^2 + b^2 <= 1)
+ * with U' = Ua / |Ua|^2, V' = Va / |Va|^2 (Ua, Va the frame's scaled in-plane axes), whose extent along
+ * axis x is sqrt(U'x^2 + V'x^2); the box is padded by a relative 1e-4 and 1e-6.
+ * ------------------------------------------------------------------------------------------------ */
+typedef struct {
+    float lo[3], hi[3];
+    int left, right;   /* internal: child nodes; leaf: left = -1 - first sorted position, right = count */
+} obvh_node;
+
+typedef struct {
+    int n, n_nodes;
+    obvh_node *nodes;
+    int *order;        /* sorted position -> primitive index */
+    const float *frames;
+} obvh;
+
+static unsigned spread3(unsigned v) {
+    v &= 1023u;
+    v = (v | (v << 16)) & 0x030000FFu;
+    v = (v | (v << 8)) & 0x0300F00Fu;
+    v = (v | (v << 4)) & 0x030C30C3u;
+    v = (v | (v << 2)) & 0x09249249u;
+    return v;
+}
+
+typedef struct { unsigned key; int idx; } okey;
+static int cmp_okey(const void *a, const void *b) {
+    const okey *x = (const okey *)a, *y = (const okey *)b;
+    if (x->key != y->key) return x->key < y->key ? -1 : 1;
+    return (x->idx > y->idx) - (x->idx < y->idx);
+}
+
+static void prim_box(const float *f, float *lo, float *hi) {
+    const float *Ua = f + 6, *Va = f + 9;
+    const double uu = (double)Ua[0] * Ua[0] + (double)Ua[1] * Ua[1] + (double)Ua[2] * Ua[2];
+    const double vv = (double)Va[0] * Va[0] + (double)Va[1] * Va[1] + (double)Va[2] * Va[2];
+    for (int a = 0; a < 3; ++a) {
+        const double up = uu > 0 ? Ua[a] / uu : 1e30, vp = vv > 0 ? Va[a] / vv : 1e30;
+        double ext = sqrt(up * up + vp * vp);
+        ext = ext * (1.0 + 1e-4) + 1e-6;
+        lo[a] = (float)(f[a] - ext);
+        hi[a] = (float)(f[a] + ext);
+        if (!(lo[a] <= hi[a])) { lo[a] = -INFINITY; hi[a] = INFINITY; }  /* degenerate frame: never culled */
+    }
+}
+
+static int build_range(obvh *b, const okey *keys, int first, int last, const float *pbox) {
+    const int id = b->n_nodes++;
+    obvh_node *nd = &b->nodes[id];
+    if (last - first + 1 <= 4) {
+        nd->left = -1 - first;
+        nd->right = last - first + 1;
+        for (int a = 0; a < 3; ++a) { nd->lo[a] = INFINITY; nd->hi[a] = -INFINITY; }
+        for (int p = first; p <= last; ++p)
+            for (int a = 0; a < 3; ++a) {
+                const float *bx = pbox + 6 * (size_t)keys[p].idx;
+                if (bx[a] < nd->lo[a]) nd->lo[a] = bx[a];
+                if (bx[3 + a] > nd->hi[a]) nd->hi[a] = bx[3 + a];
+            }
+        return id;
+    }
+    int split = (first + last) / 2;
+    const unsigned kf = keys[first].key, kl = keys[last].key;
+    if (kf != kl) {
+        const int bit = 31 - __builtin_clz(kf ^ kl);
+        int lo = first, hi = last;  /* last position whose key has that bit clear */
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) / 2;
+            if ((keys[mid].key >> bit) & 1u) hi = mid - 1; else lo = mid;
+        }
+        split = lo;
+    }
+    const int l = build_range(b, keys, first, split, pbox);
+    const int r = build_range(b, keys, split + 1, last, pbox);
+    nd = &b->nodes[id];
+    nd->left = l;
+    nd->right = r;
+    for (int a = 0; a < 3; ++a) {
+        nd->lo[a] = fminf(b->nodes[l].lo[a], b->nodes[r].lo[a]);
+        nd->hi[a] = fmaxf(b->nodes[l].hi[a], b->nodes[r].hi[a]);
+    }
+    return id;
+}
+
+void *oracle_bvh_build(const float *frames, int n) {
+    obvh *b = (obvh *)calloc(1, sizeof(obvh));
+    b->n = n;
+    b->frames = frames;
+    if (n == 0) return b;
+    float *pbox = (float *)malloc(sizeof(float) * 6 * (size_t)n);
+    float clo[3] = {INFINITY, INFINITY, INFINITY}, chi[3] = {-INFINITY, -INFINITY, -INFINITY};
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < n; ++i) prim_box(frames + 12 * (size_t)i, pbox + 6 * (size_t)i, pbox + 6 * (size_t)i + 3);
+    for (int i = 0; i < n; ++i)
+        for (int a = 0; a < 3; ++a) {
+            const float c = frames[12 * (size_t)i + a];
+            if (c < clo[a]) clo[a] = c;
+            if (c > chi[a]) chi[a] = c;
+        }
+    okey *keys = (okey *)malloc(sizeof(okey) * (size_t)n);
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < n; ++i) {
+        unsigned code = 0;
+        for (int a = 0; a < 3; ++a) {
+            const float ext = chi[a] - clo[a];
+            float x = ext > 0 ? (frames[12 * (size_t)i + a] - clo[a]) / ext : 0.5f;
+            int q = (int)(x * 1023.0f);
+            q = q < 0 ? 0 : (q > 1023 ? 1023 : q);
+            code |= spread3((unsigned)q) << (2 - a);
+        }
+        keys[i].key = code;
+        keys[i].idx = i;
+    }
+    qsort(keys, n, sizeof(okey), cmp_okey);
+    b->nodes = (obvh_node *)malloc(sizeof(obvh_node) * (size_t)(2 * n + 1));
+    b->order = (int *)malloc(sizeof(int) * (size_t)n);
+    for (int i = 0; i < n; ++i) b->order[i] = keys[i].idx;
+    build_range(b, keys, 0, n - 1, pbox);
+    free(keys);
+    free(pbox);
+    return b;
+}
+
+void oracle_bvh_free(void *h) {
+    obvh *b = (obvh *)h;
+    if (!b) return;
+    free(b->nodes);
+    free(b->order);
+    free(b);
+}
+
+static inline int box_hit(const obvh_node *nd, const float *O, const float *iv, float tlo, float thi, float *tn) {
+    float t0 = tlo, t1 = thi;
+    for (int a = 0; a < 3; ++a) {
+        float ta = (nd->lo[a] - O[a]) * iv[a], tb = (nd->hi[a] - O[a]) * iv[a];
+        if (ta > tb) { float x = ta; ta = tb; tb = x; }
+        if (ta > t0) t0 = ta;
+        if (tb < t1) t1 = tb;
+    }
+    *tn = t0;
+    return t0 <= t1;
+}
+
+/* The K_HITS nearest hits of one ray at or beyond t_min (slot order, +inf / -1 padding). */
+static void bvh_hits16(const obvh *b, int nsides, const float *pc, const float *ps, const float *O, const float *v,
+                       float t_min, float *tb, int *ib) {
+    for (int k = 0; k < K_HITS; ++k) { tb[k] = INFINITY; ib[k] = 0x7fffffff; }
+    if (b->n == 0 || !(t_min < INFINITY)) goto out;
+    {
+        float iv[3];
+        for (int a = 0; a < 3; ++a) iv[a] = 1.0f / (fabsf(v[a]) > 1e-30f ? v[a] : copysignf(1e-30f, v[a]));
+        const float tlo = t_min - fabsf(t_min) * 1e-5f;
+        int stack[256], sp = 0;
+        stack[sp++] = 0;
+        while (sp) {
+            const obvh_node *nd = &b->nodes[stack[--sp]];
+            const float bk = tb[K_HITS - 1];
+            float tn;
+            if (!box_hit(nd, O, iv, tlo, bk + fabsf(bk) * 1e-5f, &tn)) continue;
+            if (nd->left < 0) {
+                const int first = -1 - nd->left;
+                for (int p = first; p < first + nd->right; ++p) {
+                    const int i = b->order[p];
+                    float t;
+                    if (hit_test(b->frames + 12 * (size_t)i, O, v, t_min, nsides, pc, ps, &t)) kbuf_push(tb, ib, t, i);
+                }
+                continue;
+            }
+            float tl, tr;
+            const int hl = box_hit(&b->nodes[nd->left], O, iv, tlo, bk + fabsf(bk) * 1e-5f, &tl);
+            const int hr = box_hit(&b->nodes[nd->right], O, iv, tlo, bk + fabsf(bk) * 1e-5f, &tr);
+            if (sp + 2 > 256) continue;  /* cannot happen: depth <= 2 * 32 code bits + leaf levels */
+            if (hl && hr) {
+                if (tl <= tr) { stack[sp++] = nd->right; stack[sp++] = nd->left; }
+                else { stack[sp++] = nd->left; stack[sp++] = nd->right; }
+            } else if (hl) stack[sp++] = nd->left;
+            else if (hr) stack[sp++] = nd->right;
+        }
+    }
+out:
+    for (int k = 0; k < K_HITS; ++k)
+        if (ib[k] == 0x7fffffff) { tb[k] = INFINITY; ib[k] = -1; }
+}
+
+/* One ray's 16-nearest query for the CPU renderer in decode_oracle.c. */
+void oracle_bvh_hits_one(const void *h, int nsides, const float *pc, const float *ps, const float *O, const float *v,
+                         float t_min, float *tb, int *ib) {
+    bvh_hits16((const obvh *)h, nsides, pc, ps, O, v, t_min, tb, ib);
+}
+
+void oracle_bvh_hits(const void *h, const float *O, const float *v, const float *t_min, int R, int nsides,
+                     float *t_out, int *idx_out) {
+    const obvh *b = (const obvh *)h;
+    float pc[64], ps[64];
+    oracle_polygon_constants(nsides, pc, ps);
+#pragma omp parallel for schedule(dynamic, 16)
+    for (int r = 0; r < R; ++r) {
+        float tb[K_HITS];
+        int ib[K_HITS];
+        bvh_hits16(b, nsides, pc, ps, O + 3 * r, v + 3 * r, t_min[r], tb, ib);
+        for (int k = 0; k < K_HITS; ++k) {
+            t_out[(long)k * R + r] = tb[k];
+            idx_out[(long)k * R + r] = ib[k];
+        }
+    }
+}

@@ -32,9 +32,24 @@ def test_shard_rays_covers_every_ray_once():
 def test_grad_buffer_segments_are_aligned_views():
     g = dp.GradBuffer(37, True, "cpu")
     for name, t in g.views.items():
-        assert (t.data_ptr() - g.flat.data_ptr()) % 64 == 0, name
+        base = g.flat if name not in dp.PER_PRIM else g.local
+        assert (t.data_ptr() - base.data_ptr()) % 64 == 0, name
         t.fill_(1.0)
-    assert g.flat.sum().item() == sum(t.numel() for t in g.views.values())
+    assert g.flat.sum().item() + g.local.sum().item() == sum(t.numel() for t in g.views.values())
+    # the exchanged buffer holds 80 floats per primitive, not the 110 of the expanded gradients
+    assert g.views["rows"].shape == (37, dp.PRIM_ROW) and "cond" not in dict(dp.grad_layout(37, True)[0])
+
+
+def scatter_rows_cpu(rows, A1, decoder, dRGB, dA, dk, dm, ds, dq, dcond):
+    """CPU restatement of flare_scatter_prim_rows (row layout of include/flare_b200.h)."""
+    dm += rows[:, 0:3]
+    ds += rows[:, 3:5]
+    dq += rows[:, 5:9]
+    dRGB += rows[:, 9:12]
+    dA += rows[:, 12:13]
+    dk += rows[:, 13:14]
+    c = dcond.shape[1]
+    dcond += rows[:, 16:80] @ A1.float()[:, 32:32 + c]
 
 
 class FakeRenderer:
@@ -51,12 +66,12 @@ class FakeRenderer:
         O, v, bitmap = a[8], a[9], a[10]
         bitmap += torch.sigmoid(v * 3.0 + O)
 
-    def Backward(self, *a):
+    def Backward(self, *a, prim_rows=None):
         v, dLdI = a[9], a[19]
-        dRGB, dm, dcond = a[20], a[31], a[29]
-        dRGB[0] += dLdI.sum(0)
-        dm[1] += (dLdI * v).sum(0)
-        dcond[2, :3] += (dLdI * v * v).sum(0)
+        rows = prim_rows
+        rows[0, 9:12] += dLdI.sum(0)                 # dRGB of primitive 0
+        rows[1, 0:3] += (dLdI * v).sum(0)           # dm of primitive 1
+        rows[2, 16:19] += (dLdI * v * v).sum(0)     # layer-1 deltas of primitive 2 -> its descriptor gradient
 
 
 def _step(world, rank, scene, n_views=4, rpv=64):
@@ -67,9 +82,13 @@ def _step(world, rank, scene, n_views=4, rpv=64):
     for v, lo, cnt in dp.shard_rays(n_views, rpv, world, rank):
         sl = slice(v * rpv + lo, v * rpv + lo + cnt)
         shards.append(dp.Shard(torch.zeros(cnt, 3), allv[sl].contiguous(), target[sl].contiguous()))
+    from flare_b200 import renderer
+    renderer.scatter_prim_rows = scatter_rows_cpu  # the CUDA expansion, restated on the CPU
     st = dp.TrainStep(FakeRenderer(), scene, shards, n_views * rpv)
     st()
-    return st.grads.flat.clone()
+    G = st.grads
+    assert G["cond"][2].abs().sum() > 0 and G["RGB"][0].abs().sum() > 0  # the rows were expanded
+    return torch.cat([G.flat, G.local]).clone()
 
 
 def _free_port():

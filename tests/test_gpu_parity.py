@@ -540,3 +540,30 @@ def test_config0_forward_backward(decoder):
         if not e < (GRAD_TOL_RELU_KINK if k in kink else GRAD_TOL):
             bad[k] = e
     assert not bad, f"relative L2 above the bar: {bad}"
+
+
+def test_backward_prim_rows_then_scatter_equals_direct(case_dense):
+    """Backward into per-primitive rows (the data-parallel exchange format) + flare_scatter_prim_rows gives
+    the same gradients, bit for bit, as the Backward that writes them itself."""
+    from flare_b200.renderer import PRIM_ROW, scatter_prim_rows
+    c = case_dense
+    R, n = c.R, c.sc.n
+    outs = []
+    for rows_mode in (False, True):
+        bitmap, dacc, nacc, dai, sn = z(R, 3), z(R, 4), z(R, 4), z(R, 2), z(R, 3)
+        c.r.Forward_training(*c.dec(), c.Og, c.vg, bitmap, 0.1, 0.2, 0.3, *c.geo(), 1e-4, dacc, REG_A, REG_B, dai, sn,
+                             nacc)
+        dLdI = torch.randn(R, 3, generator=torch.Generator().manual_seed(8)).cuda() / R
+        G = dict(RGB=z(n, 3), A=z(n, 1), k=z(n, 1), m=z(n, 3), s=z(n, 2), q=z(n, 4), cond=z(n, 96), f=z(13154))
+        W = [z(1, 512), z(1, 64), z(1, 4096), z(1, 512), z(1, 8192), z(1, 512)]
+        rows = z(n, PRIM_ROW) if rows_mode else None
+        c.r.Backward(*c.dec(), c.Og, c.vg, 0.1, 0.2, 0.3, *c.geo(), bitmap.clone(), dLdI, G["RGB"], G["A"], G["k"], *W,
+                     G["cond"], G["f"], G["m"], G["s"], G["q"], 1e-4, dacc, z(R, 4), 0.0, REG_A, REG_B, dai, sn, nacc,
+                     0.0, prim_rows=rows)
+        if rows_mode:
+            assert all(not G[k].any() for k in ("RGB", "A", "k", "m", "s", "q", "cond"))  # untouched
+            scatter_prim_rows(rows, c.g.A1, 0, G["RGB"], G["A"], G["k"], G["m"], G["s"], G["q"], G["cond"])
+        torch.cuda.synchronize()
+        outs.append({**G, "w1": W[4]})
+    for k in outs[0]:
+        assert torch.equal(outs[0][k], outs[1][k]), k
