@@ -46,14 +46,14 @@ B_HIT_TRACE = 64                 # one 64-B node per composited hit
 B_HIT_FWD = 56 + 192             # primitive record + fp16 descriptor row
 B_HIT_BWD = 56 + 192 + 440       # re-read + gradient writes (14 geometry + 96 descriptor fp32)
 B_RAY_FWD, B_RAY_BWD = 44, 24
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each timed kernel, measured with
-# a one-pass ncu capture of the config-3 bench command (mean over the launches captured: passes 0-3 of one
-# view).  Traversal: mostly the 42-slot (t, index) hit
-# lists each pass writes (8 B per slot), node and record fetches being mostly L2 hits; shading: descriptor
-# rows, primitive parameters and hit lists read, per-primitive gradient rows written.  Only valid for the
-# config-3 workload; other workloads report null.
-DRAM_BYTES_PER_LAUNCH = {"trace": {3: 398.4e6}, "shade_forward": {3: 594.7e6}, "shade_backward": {3: 648.3e6}}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per composited hit of each timed kernel, from a
+# one-kernel ncu capture of this build on the small profiling workload (tests/profile_workload.py: 1M
+# primitives, 400x400 rays, whose scene and hit lists exceed the 126 MB L2), divided by that launch's
+# composited hits; the bench scales it by the hits of its own launches (traffic grows with the hits a
+# launch processes).  None: not captured for this build.
+DRAM_BYTES_PER_HIT = {"trace": None, "shade_forward": None, "shade_backward": None}
 FLOP_HIT_FWD = 2 * (128 * 64 + 64 * 64 + 64 * 4)
+T_THR_FORWARD = 1e-4  # BASELINE config 1's early-termination threshold
 
 
 def peaks():
@@ -163,6 +163,24 @@ def time_steps(fn, steps, world):
     return ms
 
 
+def path_roofline(hits, rays, ms, hbm, tflops, backward=True):
+    """Roofline of the whole path (north star): the slower of its algorithmic bytes over HBM bandwidth
+    and its decoder FLOPs over the tensor peak.  Forward: 312 B + 25088 FLOP per composited hit and 44 B per
+    ray; forward + backward: 1064 B + 100352 FLOP per hit and 68 B per ray."""
+    if backward:
+        nbytes = hits * (2 * B_HIT_TRACE + B_HIT_FWD + B_HIT_BWD) + rays * (B_RAY_FWD + B_RAY_BWD)
+        flops = hits * 4 * FLOP_HIT_FWD
+    else:
+        nbytes = hits * (B_HIT_TRACE + B_HIT_FWD) + rays * B_RAY_FWD
+        flops = hits * FLOP_HIT_FWD
+    t_mem, t_flop = nbytes / (hbm * 1e9), flops / (tflops * 1e12)
+    t_roof = max(t_mem, t_flop)
+    return {"roofline_ms": t_roof * 1e3, "frac": t_roof / (ms * 1e-3), "algo_bytes": nbytes, "flops": flops,
+            "bound": "hbm" if t_mem >= t_flop else "tensor",
+            "note": ("1064 B + 100352 FLOP per composited hit, 68 B per ray" if backward else
+                     "312 B + 25088 FLOP per composited hit, 44 B per ray") + "; peaks of MEASURED_PEAKS.json"}
+
+
 def kernel_roofline(kt, hits, rays, hbm, traversals=1.0):
     """Achieved GB/s of each kernel = algorithmic bytes / kernel time; the dominant one is returned.
     `traversals` = traversals of the hit lists per step (1 when the backward replays the forward's cached
@@ -181,12 +199,25 @@ def kernel_roofline(kt, hits, rays, hbm, traversals=1.0):
     return dom, out
 
 
-class CpuPort:
-    """The CPU port (oracle/) of the whole path on a bounded sample: brute-force multi-pass traversal,
-    decode + composite (C, OpenMP, all cores) and the autograd backward (torch, float64).  Frame prep
-    (the SetGeometry analogue) runs once in the constructor."""
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    def __init__(self, cfg, sample_rays=8, seed=0):
+
+class CpuPort:
+    """The reference's path on the host cores, from the CPU port in oracle/ (the reference itself needs
+    OptiX and an RT-core GPU): a C hierarchy over the primitives (built once, the SetGeometry analogue),
+    then per step, for a fixed block of rays of the workload's first view: the multi-pass 16-nearest
+    traversal with the reference's restarts, decode + composite after every pass until each ray terminates
+    (C, OpenMP over all host cores), and -- training workloads -- the backward over the composited hit lists
+    (torch autograd, float64)."""
+
+    def __init__(self, cfg, sample_rays=16384, seed=0):
         import numpy as np
 
         from flare_b200.scene import camera_rays, make_scene, sphere_eye
@@ -196,54 +227,46 @@ class CpuPort:
         self.sc = make_scene(c["n_prims"], seed)
         W, H, V = c["width"], c["height"], c["views"]
         O, v = camera_rays(W, H, 60.0, eye=sphere_eye(0, V) if V > 1 else (0.0, 0.0, 3.0))
-        cy, cx = H // 2, W // 2  # a centred block: these rays cross the scene
         side = int(math.ceil(math.sqrt(sample_rays)))
+        cy, cx = H // 2 - side // 2, W // 2 - side // 2  # a centred block: these rays cross the scene
         idx = [(cy + dy) * W + (cx + dx) for dy in range(side) for dx in range(side)][:sample_rays]
         self.O, self.v = O[idx].numpy(), v[idx].numpy()
         self.target = np.random.RandomState(seed).rand(len(idx), 3).astype(np.float32)
         t0 = time.perf_counter()
         self.frames = oracle.prep_frames(*self.sc.activated())
-        self.prep_s = time.perf_counter() - t0
+        self.bvh = oracle.CpuBvh(self.frames)
+        self.build_s = time.perf_counter() - t0
         self.train = c["mode"] == "train"
+        self.T_thr = 1e-4
 
     def step(self):
         import numpy as np
 
-        from oracle import grad_oracle, oracle
+        from oracle import grad_oracle
         t1 = time.perf_counter()
-
-        def stop(ids, per_t, per_i):
-            # composite what each ray has so far; a ray whose transmittance fell below the threshold is done
-            off = np.zeros(len(ids) + 1, np.int64)
-            off[1:] = np.cumsum([len(per_i[r]) for r in ids])
-            part = (off, np.array([x for r in ids for x in per_t[r]], np.float32),
-                    np.array([x for r in ids for x in per_i[r]], np.int32))
-            f = oracle.forward(self.sc, self.O[ids], self.v[ids], part, "training")
-            return f["T"] < 1e-4
-
-        csr = oracle.hit_lists(self.frames, self.O, self.v, stop=stop)
-        ref = oracle.forward(self.sc, self.O, self.v, csr, "training", reg_a=-0.1 * 1000 / 999.9,
-                             reg_b=1000 / 999.9)
-        img = np.clip(ref["rgb"], 0, 1)
+        rgb, csr, nh, tr_s, sh_s = self.bvh.render(self.sc, self.O, self.v, "training", T_thr=self.T_thr,
+                                                    reg_a=-0.1 * 1000 / 999.9, reg_b=1000 / 999.9)
+        img = np.clip(rgb, 0, 1)
         dLdI = (np.sign(img - self.target) / (3 * len(self.O))).astype(np.float32)
         t2 = time.perf_counter()
         if self.train:
-            grad_oracle.gradients(self.sc, self.O, self.v, csr, ref["nhits"], dLdI, compact=True)
+            grad_oracle.gradients(self.sc, self.O, self.v, csr, nh, dLdI, compact=True)
         t3 = time.perf_counter()
-        self.last = (t2 - t1, t3 - t2, int(ref["total_hits"]))
+        self.last = (t2 - t1, t3 - t2, int(nh.sum()), tr_s, sh_s)
         return t3 - t1
 
     def describe(self):
-        fwd, bwd, hits = self.last
+        fwd, bwd, hits, tr_s, sh_s = self.last
         c = CONFIGS[self.cfg]
-        return (f"{len(self.O)} central rays of config {self.cfg} view 0 per step ({hits} composited hits); "
-                f"brute-force k-nearest traversal over all {c['n_prims']} primitives, passes until termination, "
-                f"+ decode/composite (C, OpenMP) "
-                f"+ autograd backward (torch fp64); frame prep {self.prep_s:.2f}s once, per step fwd {fwd:.2f}s "
-                f"bwd {bwd:.2f}s")
+        return (f"{len(self.O)} central rays of config {self.cfg} view 0 per step ({hits} composited hits), "
+                f"{c['n_prims']} primitives, T_threshold {self.T_thr}; host {cpu_model()}, {os.cpu_count()} "
+                f"threads. Forward: C hierarchy traversal (16-nearest passes, reference restarts) + C decode / "
+                f"composite, OpenMP over rays, {fwd:.2f} s ({tr_s:.1f} thread-s traversal, {sh_s:.1f} thread-s "
+                f"shading); backward: torch fp64 autograd over the composited hit lists, {bwd:.2f} s; hierarchy "
+                f"build {self.build_s:.2f} s once (not in the step)")
 
 
-def cpu_baseline(cfg, sample_rays=8, steps=1):
+def cpu_baseline(cfg, sample_rays=16384, steps=1):
     port = CpuPort(cfg, sample_rays)
     ts = [port.step() for _ in range(steps)]
     t = statistics.median(ts)
@@ -256,9 +279,9 @@ def run_reference(args, world, rank):
         return
     port = CpuPort(args.config, args.ref_rays)
     ts = []
-    for i in range(min(args.warmup, 1) + args.steps):
+    for i in range(args.warmup + args.steps):
         t = port.step()
-        if i >= min(args.warmup, 1):
+        if i >= args.warmup:
             ts.append(t)
     v = len(port.O) / statistics.median(ts) / 1e6
     cb = dict(value=v, unit="Mrays/s", cores=os.cpu_count(), kind="port", sample=port.describe())
@@ -304,7 +327,7 @@ def measure_viewer(cfg, scene, sh, steps, warmup, device, world):
                 kernels={k: dict(ms=v[0], launches=v[1]) for k, v in kt.items() if v[1]})
 
 
-def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True, decoder="lut_pe"):
+def measure_config(cfg, world, rank, steps, warmup, device, hbm, tflops, profile=True, decoder="lut_pe"):
     from flare_b200.dp import TrainStep
     from flare_b200.renderer import CPyOptiXFLARERenderer
     scene, shards, host, total_rays = build_workload(cfg, world, rank, device, decoder=decoder)
@@ -327,13 +350,21 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True, d
         def fwd():
             bitmap.zero_(); normal.zero_(); edn.zero_()
             r.Forward_inference_with_geometry(*dec, sh.O, sh.v, bitmap, normal, alpha, edn, 0.0, 0.0, 0.0, scene.m,
-                                              scene.s, scene.q, scene.RGBA, scene.k, 0.01)
+                                              scene.s, scene.q, scene.RGBA, scene.k, T_THR_FORWARD)
         for _ in range(warmup):
             fwd()
         ms = time_steps(fwd, steps, world) / steps
         hits = r.stats()["hits_composited"]
-        out = dict(workload=f"config {cfg} forward", ms_per_step=ms, value=total_rays / (ms * 1e-3) / 1e6,
-                   hits_per_ray=hits / sh.O.shape[0])
+        r.profile(True)
+        fwd()
+        torch.cuda.synchronize()
+        kt = r.kernel_times()
+        r.profile(False)
+        R = sh.O.shape[0]
+        out = dict(workload=f"config {cfg} forward (Forward_inference_with_geometry, T_threshold {T_THR_FORWARD})",
+                   ms_per_step=ms, value=total_rays / (ms * 1e-3) / 1e6, hits_per_ray=hits / R,
+                   kernels={k: dict(ms=v[0], launches=v[1]) for k, v in kt.items() if v[1]},
+                   roofline=path_roofline(hits, R, ms, hbm, tflops, backward=False))
         return out
     step = TrainStep(r, scene, shards, total_rays)
     for _ in range(warmup):
@@ -356,7 +387,8 @@ def measure_config(cfg, world, rank, steps, warmup, device, hbm, profile=True, d
     out = dict(workload=f"config {cfg} training step{tag}", ms_per_step=ms, value=total_rays / (ms * 1e-3) / 1e6,
                hits_per_ray=hits / max(my_rays, 1), hits=hits, kernels=per, dominant=dom, step_algo_bytes=step_bytes,
                traversals_per_step=traversals,
-               kernel_times={k: v for k, v in kt.items()}, grad_allreduce_bytes=step.grads.nbytes)
+               kernel_times={k: v for k, v in kt.items()}, grad_allreduce_bytes=step.grads.nbytes,
+               step_roofline=path_roofline(hits, my_rays, ms, hbm, tflops))
     # end to end: rays and target from pinned host memory every step, loss read back every step
     def e2e_step():
         for sh, h in zip(shards, host):
@@ -400,7 +432,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="flare", choices=["flare", "reference"])
     ap.add_argument("--config", type=int, default=3, choices=[2, 3])
-    ap.add_argument("--ref-rays", type=int, default=32)
+    ap.add_argument("--ref-rays", type=int, default=4096)
     ap.add_argument("--no-extra", action="store_true", help="skip the config-1/2 extras and the CPU baseline")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
@@ -414,18 +446,19 @@ def main():
     main_cfg = args.config
     # warm-up + timed steps of the headline workload, clocks sampled meanwhile
     with ClockSampler(smi_index) as cs:
-        res = measure_config(main_cfg, world, rank, args.steps, args.warmup, device, hbm)
+        res = measure_config(main_cfg, world, rank, args.steps, args.warmup, device, hbm, tflops_sus)
     clocks = cs.summary()
     extras = {}
     if world == 1 and not args.no_extra:
         runs = [(2, "lut_pe")] if main_cfg == 3 else []
         runs += [(1, "lut_pe"), (4, "lut_pe"), (2, "grid_sh")]
         for c, dk in runs:
-            e = measure_config(c, 1, 0, max(2, args.steps), 2, device, hbm, decoder=dk)
+            e = measure_config(c, 1, 0, max(2, args.steps), 3, device, hbm, tflops_sus, decoder=dk)
             e.pop("_r", None)
             extras[f"config{c}" + ("" if dk == "lut_pe" else f"_{dk}")] = {
                 k: v for k, v in e.items() if k in ("workload", "ms_per_step", "value", "hits_per_ray", "dominant",
-                                                    "kernels", "traversal_passes", "optimizer_step")}
+                                                    "kernels", "traversal_passes", "optimizer_step", "roofline",
+                                                    "step_roofline")}
     if rank != 0:
         dist.destroy_process_group()
         return
@@ -434,18 +467,14 @@ def main():
     d = per[dom]
     roof = {"bound": "hbm", "kernel": dom, "achieved": d["achieved_gbs"], "peak": hbm, "unit": "GB/s",
             "frac": d["achieved_gbs"] / hbm,
-            "traffic": DRAM_BYTES_PER_LAUNCH.get(dom, {}).get(main_cfg),
+            "traffic": (DRAM_BYTES_PER_HIT[dom] * res["hits"] / max(d["launches"], 1)
+                        if DRAM_BYTES_PER_HIT.get(dom) else None),
             "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
             if peak_kind == "measured" else "fallback 6.65 TB/s",
             "algo_bytes_per_launch": d["algo_bytes"] / max(d["launches"], 1),
             "avg_launch_ms": d["ms"] / max(d["launches"], 1)}
     # whole-step roofline of the path: the slower of algorithmic bytes / HBM and decoder FLOPs / tensor peak
-    step_s = res["ms_per_step"] * 1e-3
-    flops = res["hits"] * 4 * FLOP_HIT_FWD
-    t_roof = max(res["step_algo_bytes"] / (hbm * 1e9), flops / (tflops_sus * 1e12))
-    step_roof = {"roofline_ms": t_roof * 1e3, "frac": t_roof / step_s, "algo_bytes": res["step_algo_bytes"],
-                 "flops": flops, "bound": "hbm" if res["step_algo_bytes"] / (hbm * 1e9) >= flops / (tflops_sus * 1e12)
-                 else "tensor", "note": "per rank; 1064 B + 100352 FLOP per composited hit, 68 B per ray"}
+    step_roof = dict(res["step_roofline"], note=res["step_roofline"]["note"] + "; per rank")
     line = {
         "metric": METRIC, "value": res["value"], "unit": "Mrays/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
@@ -473,7 +502,7 @@ def main():
         line["extra_configs"] = extras
     if world == 1 and not args.no_extra:
         try:
-            line["cpu_baseline"] = cpu_baseline(main_cfg, sample_rays=args.ref_rays, steps=1)
+            line["cpu_baseline"] = cpu_baseline(main_cfg, sample_rays=16384, steps=1)
         except Exception as ex:  # the baseline is reported, never required
             line["cpu_baseline"] = {"error": str(ex)}
     print(json.dumps(line), flush=True)
