@@ -5,9 +5,12 @@
 Renders a seeded scene (BASELINE config-0 distributions) with Forward_training + Backward twice through
 CPyOptiXFLARERenderer, so each kernel launches several times; pick launches with ncu -k / -s / -c.
 """
+import os
 import sys
 
 import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from flare_b200.renderer import CPyOptiXFLARERenderer
 from flare_b200.scene import camera_rays, make_scene

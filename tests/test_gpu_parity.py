@@ -544,7 +544,8 @@ def test_config0_forward_backward(decoder):
 
 def test_backward_prim_rows_then_scatter_equals_direct(case_dense):
     """Backward into per-primitive rows (the data-parallel exchange format) + flare_scatter_prim_rows gives
-    the same gradients, bit for bit, as the Backward that writes them itself."""
+    the same gradients as the Backward that writes them itself (equal up to the order of the float
+    reductions from different thread blocks, which two runs of either path do not share either)."""
     from flare_b200.renderer import PRIM_ROW, scatter_prim_rows
     c = case_dense
     R, n = c.R, c.sc.n
@@ -566,4 +567,4 @@ def test_backward_prim_rows_then_scatter_equals_direct(case_dense):
         torch.cuda.synchronize()
         outs.append({**G, "w1": W[4]})
     for k in outs[0]:
-        assert torch.equal(outs[0][k], outs[1][k]), k
+        assert grad_oracle.rel_l2(outs[0][k].cpu().numpy(), outs[1][k].cpu().numpy()) < 1e-5, k
