@@ -115,6 +115,22 @@ __device__ __forceinline__ bool slab(float lx, float ly, float lz, float hx, flo
     return tn <= tf;
 }
 
+// FLARE_SLAB_FMA: the slab distances as fma(bound, 1/v, -O/v) (one rounding step fewer per plane).  The
+// boxes are padded well beyond that rounding (prep_kernel), so the culling stays conservative.
+#ifndef FLARE_SLAB_FMA
+#define FLARE_SLAB_FMA 0
+#endif
+__device__ __forceinline__ bool slab_fma(float lx, float ly, float lz, float hx, float hy, float hz, float3 niv,
+                                         float3 iv, float tlo, float thi, float &tnear) {
+    float tx0 = __fmaf_rn(lx, iv.x, niv.x), tx1 = __fmaf_rn(hx, iv.x, niv.x);
+    float ty0 = __fmaf_rn(ly, iv.y, niv.y), ty1 = __fmaf_rn(hy, iv.y, niv.y);
+    float tz0 = __fmaf_rn(lz, iv.z, niv.z), tz1 = __fmaf_rn(hz, iv.z, niv.z);
+    float tn = fmaxf(fmaxf(fminf(tx0, tx1), fminf(ty0, ty1)), fmaxf(fminf(tz0, tz1), tlo));
+    float tf = fminf(fminf(fmaxf(tx0, tx1), fmaxf(ty0, ty1)), fminf(fmaxf(tz0, tz1), thi));
+    tnear = tn;
+    return tn <= tf;
+}
+
 // Traversal kernel: the 32 rays of a warp share one traversal stack (in shared memory) and every node
 // fetch; each lane keeps its own k-buffer and interval [t_min, t_16], and a child is entered when any
 // lane's interval overlaps its box (lane masks ride on the stack).  Control flow is warp-uniform, so
@@ -252,6 +268,86 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
 // column, so accesses are bank-conflict free).  An accepted hit replaces the root (the current K-th
 // nearest) and sifts down about log2 K levels instead of shifting a sorted register array; the heap is
 // sorted once when the pass ends.  Frees the ~2K registers of the register buffer.
+// FLARE_HEAP64: each entry is one 64-bit key (order-preserving bits of t + 0 above the index), so a
+// comparison is one integer compare and an entry one 8-byte access; same order as (t, index).
+#ifndef FLARE_HEAP64
+#define FLARE_HEAP64 0
+#endif
+__device__ __forceinline__ bool key_greater(float ta, int ia, float tb, int ib) {
+    return ta > tb || (ta == tb && ia > ib);
+}
+
+#if FLARE_HEAP64
+__device__ __forceinline__ unsigned long long hkey(float t, int id) {
+    const unsigned u = __float_as_uint(t + 0.0f);  // -0 -> +0: equal t compare equal
+    const unsigned o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)o << 32) | (unsigned)id;
+}
+__device__ __forceinline__ float hkey_t(unsigned long long k) {
+    const unsigned o = (unsigned)(k >> 32);
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+template <int K>
+struct HeapBuf {
+    unsigned long long *k;  // k[slot * 128 + lane]
+    unsigned long long rk;  // root key (the current K-th nearest), cached
+    float rt;
+};
+template <int K>
+__device__ __forceinline__ void heap_init(HeapBuf<K> &h, unsigned char *smem) {
+    h.k = reinterpret_cast<unsigned long long *>(smem);
+    const unsigned long long e = hkey(INFINITY, 0x7fffffff);
+    for (int s = 0; s < K; ++s) h.k[s * 128 + threadIdx.x] = e;
+    h.rk = e;
+    h.rt = INFINITY;
+}
+template <int K>
+__device__ __forceinline__ bool heap_accepts(const HeapBuf<K> &h, float t, int id) {
+    return hkey(t, id) < h.rk;
+}
+template <int K>
+__device__ __forceinline__ float heap_root_t(const HeapBuf<K> &h) { return h.rt; }
+template <int K>
+__device__ __forceinline__ void heap_sift(HeapBuf<K> &h, int size, unsigned long long key) {
+    const int c = threadIdx.x;
+    int pos = 0;
+    while (true) {
+        const int l = 2 * pos + 1;
+        if (l >= size) break;
+        unsigned long long kc = h.k[l * 128 + c];
+        int ch = l;
+        if (l + 1 < size) {
+            const unsigned long long kr = h.k[(l + 1) * 128 + c];
+            if (kr > kc) {
+                kc = kr;
+                ch = l + 1;
+            }
+        }
+        if (!(kc > key)) break;
+        h.k[pos * 128 + c] = kc;
+        pos = ch;
+    }
+    h.k[pos * 128 + c] = key;
+}
+template <int K>
+__device__ __forceinline__ void heap_insert(HeapBuf<K> &h, float t, int id) {
+    heap_sift(h, K, hkey(t, id));
+    h.rk = h.k[threadIdx.x];
+    h.rt = hkey_t(h.rk);
+}
+// Writes the K entries in ascending order (slot-major, +inf / -1 padding); destroys the heap.
+template <int K>
+__device__ __forceinline__ void heap_emit(HeapBuf<K> &h, float *t_out, int *idx_out, int stride, int j) {
+    for (int s = K - 1; s >= 0; --s) {  // the largest key leaves first, into the last slot
+        const unsigned long long top = h.k[threadIdx.x];
+        const int ik = (int)(unsigned)top;
+        const bool valid = ik != 0x7fffffff;
+        t_out[(size_t)s * stride + j] = valid ? hkey_t(top) : INFINITY;
+        idx_out[(size_t)s * stride + j] = valid ? ik : -1;
+        if (s > 0) heap_sift(h, s, h.k[s * 128 + threadIdx.x]);
+    }
+}
+#else
 template <int K>
 struct HeapBuf {
     float *t;  // t[k * 128 + lane]
@@ -259,10 +355,23 @@ struct HeapBuf {
     float rt;  // root key (the current K-th nearest), cached
     int ri;
 };
-
-__device__ __forceinline__ bool key_greater(float ta, int ia, float tb, int ib) {
-    return ta > tb || (ta == tb && ia > ib);
+template <int K>
+__device__ __forceinline__ void heap_init(HeapBuf<K> &h, unsigned char *smem) {
+    h.t = reinterpret_cast<float *>(smem);
+    h.i = reinterpret_cast<int *>(smem + (size_t)K * 128 * sizeof(float));
+    for (int k = 0; k < K; ++k) {
+        h.t[k * 128 + threadIdx.x] = INFINITY;
+        h.i[k * 128 + threadIdx.x] = 0x7fffffff;
+    }
+    h.rt = INFINITY;
+    h.ri = 0x7fffffff;
 }
+template <int K>
+__device__ __forceinline__ bool heap_accepts(const HeapBuf<K> &h, float t, int id) {
+    return t < h.rt || (t == h.rt && id < h.ri);
+}
+template <int K>
+__device__ __forceinline__ float heap_root_t(const HeapBuf<K> &h) { return h.rt; }
 
 template <int K>
 __device__ __forceinline__ void heap_sift(HeapBuf<K> &h, int size, float t, int id) {
@@ -298,6 +407,19 @@ __device__ __forceinline__ void heap_insert(HeapBuf<K> &h, float t, int id) {
     h.rt = h.t[threadIdx.x];
     h.ri = h.i[threadIdx.x];
 }
+// Writes the K entries in ascending order (slot-major, +inf / -1 padding); destroys the heap.
+template <int K>
+__device__ __forceinline__ void heap_emit(HeapBuf<K> &h, float *t_out, int *idx_out, int stride, int j) {
+    for (int k = K - 1; k >= 0; --k) {  // the largest key leaves first, into the last slot
+        const float tk = h.t[threadIdx.x];
+        const int ik = h.i[threadIdx.x];
+        const bool valid = ik != 0x7fffffff;
+        t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
+        idx_out[(size_t)k * stride + j] = valid ? ik : -1;
+        if (k > 0) heap_sift(h, k, h.t[k * 128 + threadIdx.x], h.i[k * 128 + threadIdx.x]);
+    }
+}
+#endif
 
 template <bool STATS, int K, bool PERSIST>
 __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
@@ -334,18 +456,14 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
     }
     extern __shared__ __align__(16) unsigned char heap_smem[];
     HeapBuf<K> kb;
-    kb.t = reinterpret_cast<float *>(heap_smem);
-    kb.i = reinterpret_cast<int *>(heap_smem + (size_t)K * 128 * sizeof(float));
-    for (int k = 0; k < K; ++k) {
-        kb.t[k * 128 + threadIdx.x] = INFINITY;
-        kb.i[k * 128 + threadIdx.x] = 0x7fffffff;
-    }
-    kb.rt = INFINITY;
-    kb.ri = 0x7fffffff;
+    heap_init(kb, heap_smem);
     const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
                                   1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
                                   1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
     const float tlo = __fmaf_rn(-fabsf(t_min), 1e-5f, t_min);
+#if FLARE_SLAB_FMA
+    const float3 niv = make_float3(-O.x * iv.x, -O.y * iv.y, -O.z * iv.z);
+#endif
     const bool want = live && t_min < INFINITY;
     if (n == 1) {
         float t;
@@ -369,11 +487,16 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
             }
             const bool in = (mask >> lane) & 1u;
             const bool leaf0 = d.x < 0, leaf1 = d.y < 0;  // warp-uniform
-            const float bk = fminf(kb.rt, tcap);
+            const float bk = fminf(heap_root_t(kb), tcap);
             const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
             float t0 = 0.0f, t1 = 0.0f;
+#if FLARE_SLAB_FMA
+            const bool h0 = in && slab_fma(a.x, a.y, a.z, a.w, b.x, b.y, niv, iv, tlo, thi, t0);
+            const bool h1 = in && slab_fma(b.z, b.w, c.x, c.y, c.z, c.w, niv, iv, tlo, thi, t1);
+#else
             const bool h0 = in && slab(a.x, a.y, a.z, a.w, b.x, b.y, O, iv, tlo, thi, t0);
             const bool h1 = in && slab(b.z, b.w, c.x, c.y, c.z, c.w, O, iv, tlo, thi, t1);
+#endif
             const bool i0 = h0 && !leaf0, i1 = h1 && !leaf1;
             const unsigned m0 = __ballot_sync(0xffffffffu, i0), m1 = __ballot_sync(0xffffffffu, i1);
             int next = -1;
@@ -421,7 +544,7 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
                 ++nprim;
                 if (hit_prim(rec, ~d.x, O, v, t_min, poly, t, bk)) {
                     const int pid = d.z;
-                    if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                    if (heap_accepts(kb, t, pid)) heap_insert(kb, t, pid);
                 }
             }
             if (leaf1 && h1) {
@@ -429,7 +552,7 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
                 ++nprim;
                 if (hit_prim(rec, ~d.y, O, v, t_min, poly, t, bk)) {
                     const int pid = d.w;
-                    if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                    if (heap_accepts(kb, t, pid)) heap_insert(kb, t, pid);
                 }
             }
             __syncwarp();
@@ -442,15 +565,8 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
             d = nd;
         }
     }
-    if (live) {  // heap sort: the largest key leaves first, into the last slot
-        for (int k = K - 1; k >= 0; --k) {
-            const float tk = kb.t[threadIdx.x];
-            const int ik = kb.i[threadIdx.x];
-            const bool valid = ik != 0x7fffffff;
-            t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
-            idx_out[(size_t)k * stride + j] = valid ? ik : -1;
-            if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
-        }
+    if (live) {  // heap sort into ascending slots
+        heap_emit(kb, t_out, idx_out, stride, j);
     }
     __syncwarp();
     if (!PERSIST) break;
@@ -499,14 +615,7 @@ __global__ void __launch_bounds__(128, 5) trace_heapL_kernel(
             if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
         }
         HeapBuf<K> kb;
-        kb.t = reinterpret_cast<float *>(heap_smem);
-        kb.i = reinterpret_cast<int *>(heap_smem + (size_t)K * 128 * sizeof(float));
-        for (int k = 0; k < K; ++k) {
-            kb.t[k * 128 + threadIdx.x] = INFINITY;
-            kb.i[k * 128 + threadIdx.x] = 0x7fffffff;
-        }
-        kb.rt = INFINITY;
-        kb.ri = 0x7fffffff;
+        heap_init(kb, heap_smem);
         const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
                                       1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
                                       1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
@@ -536,7 +645,7 @@ __global__ void __launch_bounds__(128, 5) trace_heapL_kernel(
                 const bool in = (mask >> lane) & 1u;
                 const int link0 = __float_as_int(c[3].x), link1 = __float_as_int(c[7].x);
                 const bool leaf0 = link0 < 0, leaf1 = link1 < 0;  // warp-uniform
-                const float bk = fminf(kb.rt, tcap);
+                const float bk = fminf(heap_root_t(kb), tcap);
                 const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
                 float t0 = 0.0f, t1 = 0.0f;
                 const bool i0 = in && !leaf0 && slab(c[0].x, c[0].y, c[0].z, c[0].w, c[1].x, c[1].y, O, iv, tlo, thi, t0);
@@ -586,7 +695,7 @@ __global__ void __launch_bounds__(128, 5) trace_heapL_kernel(
                     ++nprim;
                     if (hit_rec(c[0], c[1], c[2], O, v, t_min, poly, t, bk)) {
                         const int pid = __float_as_int(c[3].y);
-                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                        if (heap_accepts(kb, t, pid)) heap_insert(kb, t, pid);
                     }
                 }
                 if (leaf1 && in) {
@@ -594,7 +703,7 @@ __global__ void __launch_bounds__(128, 5) trace_heapL_kernel(
                     ++nprim;
                     if (hit_rec(c[4], c[5], c[6], O, v, t_min, poly, t, bk)) {
                         const int pid = __float_as_int(c[7].y);
-                        if (t < kb.rt || (t == kb.rt && pid < kb.ri)) heap_insert(kb, t, pid);
+                        if (heap_accepts(kb, t, pid)) heap_insert(kb, t, pid);
                     }
                 }
                 __syncwarp();
@@ -604,15 +713,8 @@ __global__ void __launch_bounds__(128, 5) trace_heapL_kernel(
                 for (int k = 0; k < 8; ++k) c[k] = nc[k];
             }
         }
-        if (live) {  // heap sort: the largest key leaves first, into the last slot
-            for (int k = K - 1; k >= 0; --k) {
-                const float tk = kb.t[threadIdx.x];
-                const int ik = kb.i[threadIdx.x];
-                const bool valid = ik != 0x7fffffff;
-                t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
-                idx_out[(size_t)k * stride + j] = valid ? ik : -1;
-                if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
-            }
+        if (live) {  // heap sort into ascending slots
+            heap_emit(kb, t_out, idx_out, stride, j);
         }
         __syncwarp();
     }
@@ -660,14 +762,7 @@ __global__ void __launch_bounds__(128, 5) trace_heap4_kernel(
     }
     extern __shared__ __align__(16) unsigned char heap_smem[];
     HeapBuf<K> kb;
-    kb.t = reinterpret_cast<float *>(heap_smem);
-    kb.i = reinterpret_cast<int *>(heap_smem + (size_t)K * 128 * sizeof(float));
-    for (int k = 0; k < K; ++k) {
-        kb.t[k * 128 + threadIdx.x] = INFINITY;
-        kb.i[k * 128 + threadIdx.x] = 0x7fffffff;
-    }
-    kb.rt = INFINITY;
-    kb.ri = 0x7fffffff;
+    heap_init(kb, heap_smem);
     const float3 iv = make_float3(1.0f / (fabsf(v.x) > 1e-30f ? v.x : copysignf(1e-30f, v.x)),
                                   1.0f / (fabsf(v.y) > 1e-30f ? v.y : copysignf(1e-30f, v.y)),
                                   1.0f / (fabsf(v.z) > 1e-30f ? v.z : copysignf(1e-30f, v.z)));
@@ -694,7 +789,7 @@ __global__ void __launch_bounds__(128, 5) trace_heap4_kernel(
                 break;
             }
             const bool in = (mask >> lane) & 1u;
-            const float bk = fminf(kb.rt, tcap);
+            const float bk = fminf(heap_root_t(kb), tcap);
             const float thi = __fmaf_rn(fabsf(bk), 1e-5f, bk);
             const float clx[4] = {lx.x, lx.y, lx.z, lx.w}, cly[4] = {ly.x, ly.y, ly.z, ly.w},
                         clz[4] = {lz.x, lz.y, lz.z, lz.w}, chx[4] = {hx.x, hx.y, hx.z, hx.w},
@@ -767,7 +862,7 @@ __global__ void __launch_bounds__(128, 5) trace_heap4_kernel(
                     ++nprim;
                     if (hit_prim(rec, ~link[c], O, v, t_min, poly, t, bk)) {
                         const int p = pids[c];
-                        if (t < kb.rt || (t == kb.rt && p < kb.ri)) heap_insert(kb, t, p);
+                        if (heap_accepts(kb, t, p)) heap_insert(kb, t, p);
                     }
                 }
             }
@@ -778,15 +873,8 @@ __global__ void __launch_bounds__(128, 5) trace_heap4_kernel(
             ln = nln; pd = npd;
         }
     }
-    if (live) {  // heap sort: the largest key leaves first, into the last slot
-        for (int k = K - 1; k >= 0; --k) {
-            const float tk = kb.t[threadIdx.x];
-            const int ik = kb.i[threadIdx.x];
-            const bool valid = ik != 0x7fffffff;
-            t_out[(size_t)k * stride + j] = valid ? tk : INFINITY;
-            idx_out[(size_t)k * stride + j] = valid ? ik : -1;
-            if (k > 0) heap_sift(kb, k, kb.t[k * 128 + threadIdx.x], kb.i[k * 128 + threadIdx.x]);
-        }
+    if (live) {  // heap sort into ascending slots
+        heap_emit(kb, t_out, idx_out, stride, j);
     }
     if (STATS) {
         for (int o = 16; o > 0; o >>= 1) nprim += __shfl_xor_sync(0xffffffffu, nprim, o);
