@@ -126,9 +126,6 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
 
 // trace.cu: writes the coherence order of R rays into list_out
 int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st);
-// trace.cu: reorders a later pass's active list by restart point O + t_min v and direction
-int order_by_restart(flare_renderer *r, const float *O, const float *v, const float *t_min, int *list, int count,
-                     cudaStream_t st);
 size_t ray_sort_temp_bytes(int max_rays);
 int compact_active(flare_renderer *r, const int *list_in, int count, int *list_out, cudaStream_t st);
 size_t select_temp_bytes(int max_rays);

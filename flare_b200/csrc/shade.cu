@@ -1618,14 +1618,6 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
             set_error("pass loop did not terminate after %lld passes", passes);
             return FLARE_E_DEVICE;
         }
-        static const bool resort = [] {
-            const char *e = getenv("FLARE_RESORT");
-            return !(e && strcmp(e, "0") == 0);
-        }();
-        if (resort && passes > 0 && count > 16384) {  // later, large passes: regroup by restart point
-            int e = order_by_restart(r, O, v, r->t_min, r->list[cur], count, st);
-            if (e) return e;
-        }
         float *ht = r->hit_t;
         int *hi = r->hit_idx;
         if (cached && (off + count > r->hc_cap || passes >= flare_renderer::HC_MAX_PASSES)) cached = false;

@@ -1048,53 +1048,6 @@ __global__ void ray_key_kernel(const float *__restrict__ O, const float *__restr
     ids[i] = i;
 }
 
-// Keys of the rays of a later pass: the Morton code of each ray's restart point O + t_min v (10 bits per
-// axis within the primitive-centre bounds, which the padded scene may exceed a little: clamped) above the
-// octahedral direction code.  Rays that resume the walk in the same region of the scene and head the same
-// way share a 32-ray packet, so a packet's lanes want the same subtrees again.
-__global__ void restart_key_kernel(const float *__restrict__ O, const float *__restrict__ v,
-                                   const float *__restrict__ tmin, const int *__restrict__ list, int count,
-                                   const int *__restrict__ bounds, unsigned long long *__restrict__ keys,
-                                   int *__restrict__ ids) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= count) return;
-    const int ray = list[i];
-    const float t = tmin[ray];
-    const float tt = t < INFINITY ? t : 0.0f;
-    unsigned oc = 0;
-    for (int a = 0; a < 3; ++a) {
-        float lo = ord_inv(bounds[a]), hi = ord_inv(bounds[3 + a]);
-        const float p = __fmaf_rn(v[3 * (size_t)ray + a], tt, O[3 * (size_t)ray + a]);
-        float x = hi > lo ? (p - lo) / (hi - lo) : 0.5f;
-        oc |= spread10((unsigned)fminf(fmaxf(x * 1024.0f, 0.0f), 1023.0f)) << (2 - a);
-    }
-    float dx = v[3 * (size_t)ray], dy = v[3 * (size_t)ray + 1], dz = v[3 * (size_t)ray + 2];
-    float l1 = fabsf(dx) + fabsf(dy) + fabsf(dz);
-    float px = l1 > 0.0f ? dx / l1 : 0.0f, py = l1 > 0.0f ? dy / l1 : 0.0f;
-    if (dz < 0.0f) {
-        float qx = (1.0f - fabsf(py)) * copysignf(1.0f, px), qy = (1.0f - fabsf(px)) * copysignf(1.0f, py);
-        px = qx;
-        py = qy;
-    }
-    unsigned ux = (unsigned)fminf(fmaxf((px * 0.5f + 0.5f) * 65536.0f, 0.0f), 65535.0f);
-    unsigned uy = (unsigned)fminf(fmaxf((py * 0.5f + 0.5f) * 65536.0f, 0.0f), 65535.0f);
-    keys[i] = ((unsigned long long)oc << 32) | (spread16(ux) << 1) | spread16(uy);
-    ids[i] = ray;
-}
-
-int order_by_restart(flare_renderer *r, const float *O, const float *v, const float *t_min, int *list, int count,
-                     cudaStream_t st) {
-    if (count <= 1) return FLARE_OK;
-    restart_key_kernel<<<(count + 255) / 256, 256, 0, st>>>(O, v, t_min, list, count,
-                                                           reinterpret_cast<const int *>(r->bounds), r->ray_keys,
-                                                           r->ray_ids_tmp);
-    size_t tmp = r->ray_sort_tmp_bytes;
-    FLARE_CUDA_TRY(cub::DeviceRadixSort::SortPairs(r->ray_sort_tmp, tmp, r->ray_keys, r->ray_keys + r->max_rays,
-                                                   r->ray_ids_tmp, list, count, 0, 64, st));
-    FLARE_CUDA_TRY(cudaGetLastError());
-    return FLARE_OK;
-}
-
 __global__ void init_bounds6_kernel(int *b) {
     if (threadIdx.x < 3) b[threadIdx.x] = 0x7FFFFFFF;
     else if (threadIdx.x < 6) b[threadIdx.x] = (int)0x80000000;
