@@ -301,11 +301,15 @@ __device__ __forceinline__ void write_x_row(char *tile, int r, const float2 *lut
         return;
     }
     if constexpr (DK == 1) {
-        // chunks 0-1: grid levels 0-7 (level l -> elements 2l, 2l+1); one chunk at a time keeps the
+        // Each of the 32 grid / spherical-harmonics inputs x is split into an f16 hi part (chunks 0-3) and
+        // the f16 remainder x - hi (chunks 8-11, met by a copy of W1's columns 0..31): the layer-1
+        // pre-activations see x to ~22 bits instead of f16's 11, so the sign of a ReLU input near zero --
+        // which gates the whole layer-1 gradient -- does not hang on the f16 rounding of x.
+        // chunks 0-1 / 8-9: grid levels 0-7 (level l -> elements 2l, 2l+1); one chunk at a time keeps the
         // corner loads in flight to 16 float2
 #pragma unroll 1
         for (int hc = 0; hc < 2; ++hc) {
-            __half2 h[4];
+            __half2 h[4], lo[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 LutCell c = lut_cell<1>(4 * hc + q, cu, cw);
@@ -314,26 +318,36 @@ __device__ __forceinline__ void write_x_row(char *tile, int r, const float2 *lut
                 float r0x = __fmaf_rn(f00.x, vx, f10.x * ux), r0y = __fmaf_rn(f00.y, vx, f10.y * ux);
                 float r1x = __fmaf_rn(f01.x, vx, f11.x * ux), r1y = __fmaf_rn(f01.y, vx, f11.y * ux);
                 float uy = c.fy, vy = 1.0f - uy;
-                h[q] = __floats2half2_rn(__fmaf_rn(r0x, vy, r1x * uy), __fmaf_rn(r0y, vy, r1y * uy));
+                const float gx = __fmaf_rn(r0x, vy, r1x * uy), gy = __fmaf_rn(r0y, vy, r1y * uy);
+                h[q] = __floats2half2_rn(gx, gy);
+                const float2 hf = __half22float2(h[q]);
+                lo[q] = __floats2half2_rn(gx - hf.x, gy - hf.y);
             }
             T[hc * 128 + r] = *reinterpret_cast<uint4 *>(h);
+            T[(8 + hc) * 128 + r] = *reinterpret_cast<uint4 *>(lo);
         }
-        // chunks 2-3: spherical harmonics of v
+        // chunks 2-3 / 10-11: spherical harmonics of v
         float shv[16];
         sh_deg3(v.x, v.y, v.z, shv);
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {
-            __half2 h[4];
+            __half2 h[4], lo[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(shv[8 * hc + 2 * q], shv[8 * hc + 2 * q + 1]);
+            for (int q = 0; q < 4; ++q) {
+                const float a0 = shv[8 * hc + 2 * q], a1 = shv[8 * hc + 2 * q + 1];
+                h[q] = __floats2half2_rn(a0, a1);
+                const float2 hf = __half22float2(h[q]);
+                lo[q] = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+            }
             T[(2 + hc) * 128 + r] = *reinterpret_cast<uint4 *>(h);
+            T[(10 + hc) * 128 + r] = *reinterpret_cast<uint4 *>(lo);
         }
-        // chunks 4-7: the 32-wide descriptor row; 8-15: zero
+        // chunks 4-7: the 32-wide descriptor row (f16 already); 12-15: zero
         const uint4 *cr = sc.cond + (size_t)idx * 4;
 #pragma unroll
         for (int j = 0; j < 4; ++j) T[(4 + j) * 128 + r] = __ldg(cr + j);
 #pragma unroll
-        for (int kc = 8; kc < 16; ++kc) T[kc * 128 + r] = make_uint4(0, 0, 0, 0);
+        for (int kc = 12; kc < 16; ++kc) T[kc * 128 + r] = make_uint4(0, 0, 0, 0);
     } else {
     // chunk 0: LUT (level l -> elements 2l, 2l+1)
     __half2 h[4];
@@ -412,14 +426,18 @@ __device__ __forceinline__ void write_row16_split(char *tile_hi, char *tile_lo, 
 }
 
 // Loads the decoder weights, biases (and optionally the LUT) into shared memory.
-__device__ void load_decoder(char *smem, const SceneP &sc, bool with_lut, bool dup_w3 = false) {
+// grid_lo (decoder 1): W1 columns 0..31 are copied into columns 64..95, which that decoder does not use, so
+// the f16 lo parts of its grid and spherical-harmonics inputs (X columns 64..95, see write_x_row) meet the
+// same weights as their hi parts.
+__device__ void load_decoder(char *smem, const SceneP &sc, bool with_lut, bool dup_w3 = false, bool grid_lo = false) {
     const int tid = threadIdx.x, nt = blockDim.x;
     const uint4 *A1 = reinterpret_cast<const uint4 *>(sc.A1);
     const uint4 *A2 = reinterpret_cast<const uint4 *>(sc.A2);
     const uint4 *A3 = reinterpret_cast<const uint4 *>(sc.A3);
     for (int c = tid; c < 64 * 16; c += nt) {  // W1: row o, chunk kc
         int o = c >> 4, kc = c & 15;
-        *reinterpret_cast<uint4 *>(smem + SM_W1 + kc * 1024 + o * 16) = __ldg(A1 + c);
+        const int src = (grid_lo && kc >= 8 && kc < 12) ? c - 8 : c;
+        *reinterpret_cast<uint4 *>(smem + SM_W1 + kc * 1024 + o * 16) = __ldg(A1 + src);
     }
     for (int c = tid; c < 64 * 8; c += nt) {
         int o = c >> 3, kc = c & 7;
@@ -491,9 +509,11 @@ __device__ __forceinline__ void tmem_row64(uint32_t tmem, int col, float *y) {
 // Leaves h1/h2 in `tile` at the end (h2), returns y[0..3] (+ b3) for this thread's row.
 // If keep_d1 is non-null the layer-1 Hardswish derivatives are stored there (fp32).  Layer 2 accumulates
 // into TMEM columns [y2col, y2col+64): the backward keeps them there to form delta2 exactly.
+// With DK == 1 (ReLU) the derivatives are 0 / 1 and go to the 64-bit mask keep_m1 instead (bit o = z1[o] > 0).
 template <int DK = 0>
 __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char *h1_tile, char *h2_tile, Mma &mm,
-                                                 float *y4, float *keep_d1, int y2col) {
+                                                 float *y4, float *keep_d1, int y2col,
+                                                 unsigned long long *keep_m1 = nullptr) {
     const float *bias = reinterpret_cast<const float *>(smem + SM_BIAS);
     const int r = threadIdx.x;
     float y[64];
@@ -511,6 +531,8 @@ __device__ __forceinline__ bool mlp_forward_tile(char *smem, char *x_tile, char 
             keep_d1[o] = act_d<DK>(z0);
             keep_d1[o + 1] = act_d<DK>(z1);
         }
+        if (keep_m1)
+            *keep_m1 |= ((unsigned long long)(z0 > 0.0f) << o) | ((unsigned long long)(z1 > 0.0f) << (o + 1));
         y[o] = act<DK>(z0);
         y[o + 1] = act<DK>(z1);
     }
@@ -570,7 +592,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             s_abort = 0;
         }
         if (tid < 32) tmem_alloc(tmem_slot, TM_FWD_COLS);
-        load_decoder(smem, sc, FLARE_FWD_LUT_SMEM);
+        load_decoder(smem, sc, FLARE_FWD_LUT_SMEM, false, DK == 1);
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
@@ -874,7 +896,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             s_first = 1;
         }
         if (tid < 32) tmem_alloc(tmem_slot, TM_BWD_COLS);
-        load_decoder(smem, sc, false, true);
+        load_decoder(smem, sc, false, true, DK == 1);
         {   // ones column tile (128 rows x 8, element 0 = 1)
             uint4 *ones = reinterpret_cast<uint4 *>(smem + SM_BWD_ONES);
             __half2 h[4] = {__floats2half2_rn(1.0f, 0.0f), __floats2half2_rn(0.0f, 0.0f), __floats2half2_rn(0.0f, 0.0f),
@@ -956,7 +978,13 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             else g = Geo{};
             const float cu = g.u * LUT_SCALE, cw = g.w * LUT_SCALE;
             float y4[4] = {0, 0, 0, 0};
-            float hd1[64];
+            // layer-1 activation derivatives: fp32 for the Hardswish decoder (then the layer-1 deltas, kept for
+            // the per-primitive row); decoder 1's ReLU needs only a bit each, and its deltas are re-read from
+            // TMEM, where G1 stays because that decoder's dX goes to columns 64..79
+            constexpr int HD1 = DK == 1 ? 1 : 64;
+            constexpr uint32_t DXCOL = DK == 1 ? 64u : 0u;  // TMEM column of dX (y2's, free by then)
+            float hd1[HD1];
+            unsigned long long m1 = 0ull;
             float pg[PG_N];  // this hit's per-primitive gradients (layout PG_*)
 #pragma unroll
             for (int e = 0; e < PG_N; ++e) pg[e] = 0.0f;
@@ -977,7 +1005,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
-                mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, hd1, 64);
+                mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, DK == 1 ? nullptr : hd1, 64, DK == 1 ? &m1 : nullptr);
                 prefetch_hit<DK>(sc, ind_next);
             }
             // ---- compositing gradient (restates Backward.cu:1700-1900) ----
@@ -1146,8 +1174,12 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        gv[e] *= hd1[16 * cb + e];
-                        hd1[16 * cb + e] = gv[e];  // delta1, kept for the per-primitive row
+                        if constexpr (DK == 1) {
+                            gv[e] = ((m1 >> (16 * cb + e)) & 1ull) ? gv[e] : 0.0f;
+                        } else {
+                            gv[e] *= hd1[16 * cb + e];
+                            hd1[16 * cb + e] = gv[e];  // delta1, kept for the per-primitive row
+                        }
                     }
                     write_row16_split(h1t, h2t, tid, 2 * cb, gv);
                 }
@@ -1160,11 +1192,11 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     // are not formed per hit: dX[:, 32:128) = d1 W1[:, 32:128) is linear in d1, so each
                     // primitive's sum of d1 is reduced instead and multiplied by W1 once per primitive.
                     for (int ks = 0; ks < 4; ++ks)
-                        mma_f16_ss(mm.tmem, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
+                        mma_f16_ss(mm.tmem + DXCOL, sdesc(smem_u32(h1t) + ks * 4096, 2048, 128),
                                    sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1),
                                    ks > 0);
                     for (int ks = 0; ks < 4; ++ks)
-                        mma_f16_ss(mm.tmem, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
+                        mma_f16_ss(mm.tmem + DXCOL, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
                                    sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1), 1);
                     // dW1 += d1^T X : M=64, N=128, K=128 hits (hi and lo parts of d1)
                     for (int ks = 0; ks < 8; ++ks)
@@ -1188,14 +1220,32 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 mma_wait(mm);
                 const int wid = tid >> 5;
                 float *dcrow = reinterpret_cast<float *>(wid < 2 ? xt : h1t) + ((wid & 1) * 32 + (tid & 31)) * DC_ROW;
-                if (valid) {  // delta1 into the staging row now (the tiles are free), ahead of the LUT work
+                if constexpr (DK == 1) {  // delta1 = G1 (still in TMEM columns 0..63) gated by the ReLU mask
+#pragma unroll
+                    for (int cb = 0; cb < 4; ++cb) {
+                        float gv[16];
+                        tmem_ld16(mm.tmem + lane + 16 * cb, gv);
+                        tmem_wait_ld();
+                        if (valid) {
+#pragma unroll
+                            for (int e = 0; e < 16; e += 4) {
+                                float d[4];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    d[q] = ((m1 >> (16 * cb + e + q)) & 1ull) ? gv[e + q] * ginv : 0.0f;
+                                *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + 16 * cb + e) =
+                                    make_float4(d[0], d[1], d[2], d[3]);
+                            }
+                        }
+                    }
+                } else if (valid) {  // delta1 into the staging row now (the tiles are free), ahead of the LUT work
 #pragma unroll
                     for (int e = 0; e < 64; e += 4)
                         *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + e) =
                             make_float4(hd1[e] * ginv, hd1[e + 1] * ginv, hd1[e + 2] * ginv, hd1[e + 3] * ginv);
                 }
                 float dx16[16];
-                tmem_ld16(mm.tmem + lane, dx16);
+                tmem_ld16(mm.tmem + lane + DXCOL, dx16);
                 tmem_wait_ld();
                 float dxu = 0.0f, dxw = 0.0f;
                 if (valid) {
@@ -1281,8 +1331,9 @@ done:
                 for (int e = 0; e < 16; ++e) {
                     const int col = 16 * b + e;
                     const float x = vals[e] * ginv;
-                    if (l < 16) {  // half 0: dW1 row mrow
-                        atomicAdd(bo.dw + DW_W1 + mrow * 128 + col, x);
+                    if (l < 16) {  // half 0: dW1 row mrow (decoder 1: columns 64..95 hold the lo inputs' share of
+                                   // columns 0..31)
+                        atomicAdd(bo.dw + DW_W1 + mrow * 128 + ((DK == 1 && col >= 64 && col < 96) ? col - 64 : col), x);
                     } else {       // half 1: dW2 row mrow | dW3^T row mrow | db2 | db3 | db1
                         if (col < 64) atomicAdd(bo.dw + DW_W2 + mrow * 64 + col, x);
                         else if (col < 72) atomicAdd(bo.dw + DW_W3 + ((col - 64) & 3) * 64 + mrow, x);

@@ -134,9 +134,9 @@ static void decode(const oscene *S, int idx, float cu, float cw, const float *v,
         float enc[16], sh[16];
         grid_encode(S->features, cu, cw, 8, grid_res, grid_off, enc);
         sh_deg3(v[0], v[1], v[2], sh);
-        for (int i = 0; i < 16; ++i) {
-            x[i] = (float)(_Float16)enc[i];
-            x[16 + i] = (float)(_Float16)sh[i];
+        for (int i = 0; i < 16; ++i) {  /* fed as f16 hi + lo parts (~22 bits): not rounded to f16 */
+            x[i] = enc[i];
+            x[16 + i] = sh[i];
         }
         for (int j = 0; j < 32; ++j) x[32 + j] = (float)S->cond[(long)idx * 32 + j];
         for (int j = 64; j < 128; ++j) x[j] = 0.0f;

@@ -150,9 +150,10 @@ def gradients(scene, O, v, csr, nhits, dL_dI, base=False, bg=(0.0, 0.0, 0.0), re
     else:
         grid = P["cond"].shape[1] == 32  # the grid/SH decoder variant
         if grid:
-            x = torch.cat([_st16(_lut(P["features"], u * LUT_SCALE, w * LUT_SCALE, GRID_RES, GRID_OFF)),
-                           _sh(vh).to(torch.float16).to(dt), P["cond"][idx_t],
-                           torch.zeros(vh.shape[0], 64, dtype=dt)], 1)
+            # the kernel feeds the grid and spherical-harmonics inputs to layer 1 as f16 hi + lo parts (~22
+            # bits), so they are not rounded to f16 here
+            x = torch.cat([_lut(P["features"], u * LUT_SCALE, w * LUT_SCALE, GRID_RES, GRID_OFF),
+                           _sh(vh), P["cond"][idx_t], torch.zeros(vh.shape[0], 64, dtype=dt)], 1)
             act = torch.relu
         else:
             x = torch.cat([_st16(_lut(P["features"], u * LUT_SCALE, w * LUT_SCALE)),
