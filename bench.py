@@ -50,8 +50,8 @@ B_RAY_FWD, B_RAY_BWD = 44, 24
 # one-kernel ncu capture of this build on the small profiling workload (tests/profile_workload.py: 1M
 # primitives, 400x400 rays, whose scene and hit lists exceed the 126 MB L2), divided by that launch's
 # composited hits; the bench scales it by the hits of its own launches (traffic grows with the hits a
-# launch processes).  None: not captured for this build.
-DRAM_BYTES_PER_HIT = {"trace": None, "shade_forward": None, "shade_backward": None}
+# launch processes).
+DRAM_BYTES_PER_HIT = {"trace": 20.9, "shade_forward": 36.2, "shade_backward": 56.1}
 FLOP_HIT_FWD = 2 * (128 * 64 + 64 * 64 + 64 * 4)
 T_THR_FORWARD = 1e-4  # BASELINE config 1's early-termination threshold
 
