@@ -4,8 +4,9 @@
 
 Workload (seeded synthetic data; no dataset is available offline):
   config 3 (default): data-parallel training step, 6M primitives, 8 views of 1920x1080 on a radius-3
-      sphere, views split over the N ranks (strong scaling: the same 16.6M rays at every N); one NCCL
-      all-reduce of the flat gradient buffer per step.
+      sphere (strong scaling: the same 16.6M rays at every N); every rank takes the same row band of every
+      view and renders its bands as one ray batch (FLARE_BENCH_SHARDING=views: whole views per rank); one
+      NCCL all-reduce of the flat gradient buffer per step.
   config 2: training step, 3M primitives, one 1600x1064 view (rays split in row bands over ranks).
 A step = SetGeometry (LBVH rebuild, as the reference rebuilds its IAS every step) + Forward_training +
 L1 loss / dL/dI in torch + Backward (+ all-reduce).  At N=1 the line also carries the config-2
@@ -124,19 +125,27 @@ def dist_setup(args):
     return world, rank, local
 
 
-def build_workload(cfg, world, rank, device, seed=0, decoder="lut_pe"):
-    from flare_b200.dp import Shard, shard_rays
+def build_workload(cfg, world, rank, device, seed=0, decoder="lut_pe", sharding=None):
+    """Scene + this rank's rays.  sharding "banded" (default for training): the rank's row band of every
+    view, concatenated into one ray batch (balanced ranks, one renderer call per step); "views": whole views
+    dealt round-robin, one batch per view."""
+    from flare_b200.dp import Shard, shard_rays, shard_rays_banded
     from flare_b200.scene import camera_rays, make_scene, sphere_eye
     c = CONFIGS[cfg]
+    sharding = sharding or os.environ.get("FLARE_BENCH_SHARDING", "banded")
     scene = make_scene(c["n_prims"], seed, decoder=decoder).to(device)
     W, H, V = c["width"], c["height"], c["views"]
     host = []
-    for view, lo, cnt in shard_rays(V, W * H, world, rank):
+    pieces = shard_rays_banded(V, W * H, world, rank) if sharding == "banded" else shard_rays(V, W * H, world, rank)
+    for view, lo, cnt in pieces:
         eye = sphere_eye(view, V) if V > 1 else (0.0, 0.0, 3.0)
         O, v = camera_rays(W, H, 60.0, eye=eye)
         g = torch.Generator().manual_seed(1000 + view)
         target = torch.rand(W * H, 3, generator=g)
-        host.append(tuple(t[lo:lo + cnt].contiguous().pin_memory() for t in (O, v, target)))
+        host.append(tuple(t[lo:lo + cnt].contiguous() for t in (O, v, target)))
+    if sharding == "banded" and len(host) > 1:
+        host = [tuple(torch.cat([h[k] for h in host]) for k in range(3))]
+    host = [tuple(t.pin_memory() for t in h) for h in host]
     shards = [Shard(*(t.to(device) for t in h)) for h in host]
     return scene, shards, host, W * H * V
 
@@ -482,6 +491,7 @@ def main():
         "config": {"workload": res["workload"], "primitives": CONFIGS[main_cfg]["n_prims"],
                    "rays_per_step": CONFIGS[main_cfg]["width"] * CONFIGS[main_cfg]["height"] * CONFIGS[main_cfg]["views"],
                    "views": CONFIGS[main_cfg]["views"], "parallelism": f"dp{world} (rays sharded, scene replicated)",
+                   "sharding": os.environ.get("FLARE_BENCH_SHARDING", "banded"),
                    "l2": "inputs larger than L2 (scene >= 0.75 GB); no flush",
                    "hits_per_ray": res["hits_per_ray"], "grad_allreduce_bytes": res["grad_allreduce_bytes"]},
         "roofline": roof,

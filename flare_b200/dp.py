@@ -44,6 +44,20 @@ def shard_rays(n_views: int, rays_per_view: int, world: int, rank: int):
     return [(v, lo, hi - lo)]
 
 
+def shard_rays_banded(n_views: int, rays_per_view: int, world: int, rank: int):
+    """This rank's (view, first ray, ray count) pieces when every rank takes the same row band of every
+    view: band `rank` of `world` contiguous bands per view.  A rank's work then averages over all views
+    (views differ in hits per ray, so dealing whole views leaves the rank with the densest view as the
+    step's straggler); a caller passes a rank's pieces to the renderer as ONE ray batch."""
+    out = []
+    for v in range(n_views):
+        lo = rays_per_view * rank // world
+        hi = rays_per_view * (rank + 1) // world
+        if hi > lo:
+            out.append((v, lo, hi - lo))
+    return out
+
+
 PRIM_ROW = 80  # FLARE_PRIM_ROW_FLOATS: [dm 3 | ds 2 | dq 4 | dRGB 3 | dA 1 | dk 1 | 0 0 | d1 64]
 PER_PRIM = ("RGB", "A", "k", "m", "s", "q", "cond")
 

@@ -29,6 +29,23 @@ def test_shard_rays_covers_every_ray_once():
             assert len(seen) == views * rpv
 
 
+def test_banded_sharding_covers_every_ray_once_and_balances():
+    for views, rpv in [(8, 100), (1, 97), (3, 10)]:
+        for world in (1, 2, 3, 4, 8):
+            seen = {}
+            per_rank = []
+            for rank in range(world):
+                cnt_r = 0
+                for v, lo, cnt in dp.shard_rays_banded(views, rpv, world, rank):
+                    cnt_r += cnt
+                    for i in range(lo, lo + cnt):
+                        assert (v, i) not in seen
+                        seen[(v, i)] = rank
+                per_rank.append(cnt_r)
+            assert len(seen) == views * rpv
+            assert max(per_rank) - min(per_rank) <= views  # every rank has its share of every view
+
+
 def test_grad_buffer_segments_are_aligned_views():
     g = dp.GradBuffer(37, True, "cpu")
     for name, t in g.views.items():
