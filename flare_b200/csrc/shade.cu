@@ -171,6 +171,68 @@ __device__ __forceinline__ void prefetch_hit(const SceneP &sc, int idx) {
     }
 }
 
+// A hit's raw primitive parameters, loaded one slot ahead by the forward kernel (load_raw) so that their
+// latency hides behind the current slot's tensor-core waits.
+struct Raw {
+    float2 s;
+    float4 q;
+    float k;
+    float m[3];
+    float4 rgba;
+};
+__device__ __forceinline__ Raw load_raw(const SceneP &sc, int idx) {
+    Raw r;
+    r.s = __ldg(reinterpret_cast<const float2 *>(sc.s) + idx);
+    r.q = __ldg(reinterpret_cast<const float4 *>(sc.q) + idx);
+    r.k = __ldg(sc.k + idx);
+    const float *m = sc.m + 3 * (size_t)idx;
+    r.m[0] = __ldg(m);
+    r.m[1] = __ldg(m + 1);
+    r.m[2] = __ldg(m + 2);
+    r.rgba = __ldg(reinterpret_cast<const float4 *>(sc.RGBA) + idx);
+    return r;
+}
+
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// geometry() on parameters already in registers (same operations, same results).
+__device__ __forceinline__ void geometry_raw(const Raw &r, float t, float3 O, float3 v, Geo &g) {
+    const float2 s = r.s;
+    const float4 q = r.q;
+    g.sx = expf(-s.x);
+    g.sy = expf(-s.y);
+    g.q[0] = q.x; g.q[1] = q.y; g.q[2] = q.z; g.q[3] = q.w;
+    float aa = q.x * q.x, bb = q.y * q.y, cc = q.z * q.z, dd = q.w * q.w;
+    float S = __fdiv_rn(2.0f, aa + bb + cc + dd);
+    g.S = S;
+    float bs = q.y * S, cs = q.z * S, ds = q.w * S;
+    float ab = q.x * bs, ac = q.x * cs, ad = q.x * ds;
+    bb *= S;
+    float bc = q.y * cs, bd = q.y * ds;
+    cc *= S;
+    float cd = q.z * ds;
+    dd *= S;
+    g.U[0] = 1.0f - cc - dd; g.U[1] = bc + ad; g.U[2] = bd - ac;
+    g.V[0] = bc - ad; g.V[1] = 1.0f - bb - dd; g.V[2] = cd + ab;
+    g.N[0] = bd + ac; g.N[1] = cd - ab; g.N[2] = 1.0f - bb - cc;
+    g.kraw = r.k;
+    g.kappa = 1.0f + log1pf(expf(g.kraw));
+    g.kinv = 1.0f / g.kappa;
+    g.d[0] = __fmaf_rn(v.x, t, O.x) - r.m[0];
+    g.d[1] = __fmaf_rn(v.y, t, O.y) - r.m[1];
+    g.d[2] = __fmaf_rn(v.z, t, O.z) - r.m[2];
+    g.u = g.sx * __fmaf_rn(g.U[0], g.d[0], __fmaf_rn(g.U[1], g.d[1], g.U[2] * g.d[2]));
+    g.w = g.sy * __fmaf_rn(g.V[0], g.d[0], __fmaf_rn(g.V[1], g.d[1], g.V[2] * g.d[2]));
+    g.r2 = __fmaf_rn(g.u, g.u, g.w * g.w);
+    float pk = __powf(g.r2, g.kappa - 1.0f);
+    if (isnan(pk)) pk = 0.0f;
+    g.pk = pk;
+    g.r2k = g.r2 * pk;
+    g.G = __expf(-0.5f * g.kinv * g.r2k);
+}
+
 __device__ __forceinline__ void geometry(const SceneP &sc, int idx, float t, float3 O, float3 v, Geo &g) {
     float2 s = __ldg(reinterpret_cast<const float2 *>(sc.s) + idx);
     float4 q = __ldg(reinterpret_cast<const float4 *>(sc.q) + idx);
@@ -637,14 +699,24 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
         }
         int ind = -1;
         float t_hit = 0.0f;
+        // Software pipeline over the hit slots: slot h+1's list entry is read at the top of slot h and its
+        // primitive parameters are loaded (and its descriptor row prefetched into L1) before slot h's
+        // tensor-core chain, whose waits hide their latency.
+        int ind_nx = have ? pp.hit_idx[slot] : -1;
+        float t_nx = have ? pp.hit_t[slot] : 0.0f;
+        Raw raw_nx{};
+        if (ind_nx >= 0) raw_nx = load_raw(sc, ind_nx);
         for (int h = 0; h < K_PASS; ++h) {
-            ind = have ? pp.hit_idx[(size_t)h * pp.count + slot] : -1;
-            t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
+            ind = ind_nx;
+            t_hit = t_nx;
+            const Raw raw = raw_nx;
+            ind_nx = (ind >= 0 && h + 1 < K_PASS) ? pp.hit_idx[(size_t)(h + 1) * pp.count + slot] : -1;
+            t_nx = ind_nx >= 0 ? pp.hit_t[(size_t)(h + 1) * pp.count + slot] : 0.0f;
             bool valid = ind >= 0 && T >= pp.T_thr;
             if (MODE == FLARE_FWD_MEDIAN) valid = valid && (T > 0.5f);
             const int idc = ind >= 0 ? ind : 0;
             Geo g;
-            if (ind >= 0) geometry(sc, idc, t_hit, O, v, g);
+            if (ind >= 0) geometry_raw(raw, t_hit, O, v, g);
             else g = Geo{};
             float y4[4] = {0, 0, 0, 0};
             if (DEC) {
@@ -658,11 +730,19 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
+                if (ind_nx >= 0 && valid) {
+                    raw_nx = load_raw(sc, ind_nx);
+                    const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)ind_nx * Dec<DK>::COND_CHUNKS);
+                    prefetch_l1(c);
+                    if (DK == 0) prefetch_l1(c + 128);
+                }
                 mlp_forward_tile<DK>(smem, tile, tile, tile, mm, y4, nullptr, 0);
+            } else if (ind_nx >= 0) {
+                raw_nx = load_raw(sc, ind_nx);
             }
             if (!valid) continue;
             {
-                float4 rgba = __ldg(reinterpret_cast<const float4 *>(sc.RGBA) + ind);
+                const float4 rgba = raw.rgba;
                 float sig_y = DEC ? sigm(y4[3]) : 1.0f;
                 float opa1 = sigm(rgba.w);
                 float alpha = opa1 * g.G * sig_y;
