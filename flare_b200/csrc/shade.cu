@@ -1008,7 +1008,9 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     float Nm[3] = {0, 0, 0};
     bool nvalid = false;
     int ind = -1, ind_next = -1;
-    float t_hit = 0.0f;
+    float t_hit = 0.0f, t_next = 0.0f;
+    Raw raw_next{};
+    bool raw_ok = false;  // raw_next / t_next hold this row's next slot
     unsigned long long ntiles = 0;
     bool bulk_pending = false;  // this thread's last bulk reduction may still be reading its staging row
     while (true) {
@@ -1049,12 +1051,16 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
         }
         {
             ind = have ? ind_next : -1;
-            t_hit = have ? pp.hit_t[(size_t)h * pp.count + slot] : 0.0f;
+            // this slot's parameters: loaded during the previous slot when the row kept its ray (the same
+            // software pipeline as the forward), else now
+            t_hit = have ? (raw_ok ? t_next : pp.hit_t[(size_t)h * pp.count + slot]) : 0.0f;
+            const Raw raw = (raw_ok || ind < 0) ? raw_next : load_raw(sc, ind);
             ind_next = (have && ind >= 0 && h + 1 < K_PASS) ? pp.hit_idx[(size_t)(h + 1) * pp.count + slot] : -1;
+            raw_ok = false;
             const bool valid = ind >= 0 && T >= pp.T_thr;
             const int idc = ind >= 0 ? ind : 0;
             Geo g;
-            if (ind >= 0) geometry(sc, idc, t_hit, O, v, g);
+            if (ind >= 0) geometry_raw(raw, t_hit, O, v, g);
             else g = Geo{};
             const float cu = g.u * LUT_SCALE, cw = g.w * LUT_SCALE;
             float y4[4] = {0, 0, 0, 0};
@@ -1085,14 +1091,21 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 fence_async_smem();
                 tc_fence_before();
                 __syncthreads();
+                if (valid && ind_next >= 0) {  // the next slot of this ray: its parameters now, its row into L2
+                    raw_next = load_raw(sc, ind_next);
+                    t_next = pp.hit_t[(size_t)(h + 1) * pp.count + slot];
+                    raw_ok = true;
+                    const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)ind_next * Dec<DK>::COND_CHUNKS);
+                    prefetch_l2(c);
+                    if (DK == 0) prefetch_l2(c + 128);
+                }
                 mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, DK == 1 ? nullptr : hd1, 64, DK == 1 ? &m1 : nullptr);
-                prefetch_hit<DK>(sc, ind_next);
             }
             // ---- compositing gradient (restates Backward.cu:1700-1900) ----
             float gu = 0.0f, gw = 0.0f, dLdt_depth = 0.0f, ow = 0.0f, sgn = 1.0f;
             float d3[4] = {0, 0, 0, 0};
             if (valid) {
-                float4 rgba = __ldg(reinterpret_cast<const float4 *>(sc.RGBA) + ind);
+                const float4 rgba = raw.rgba;
                 float z3[3] = {1.0f, 1.0f, 1.0f}, sig_y = 1.0f, dz3[4] = {1.0f, 1.0f, 1.0f, 0.0f};
                 if (DEC) {
 #pragma unroll
