@@ -31,6 +31,7 @@ struct flare_renderer {
 
     // ---- per-ray scratch, sized max_rays ----
     float *t_min = nullptr;
+    float *hint = nullptr;   // per ray: bound of its next pass (hits at t < hint), +inf = unbounded
     float *T = nullptr;
     int *list[2] = {nullptr, nullptr};
     float *hit_t = nullptr;   // (16, max_rays)

@@ -93,12 +93,43 @@ struct PassP {
     const float *hit_t;
     const int *hit_idx;
     float *T, *t_min;
+    float *hint;           // per ray: the next pass collects hits at t < hint only (null: unbounded passes)
     unsigned char *flags;  // per list slot: the ray stays active (compacted in list order after the pass)
     int *work;             // next unclaimed list slot (zeroed before each launch that claims rays)
     int *status;
     unsigned long long *stats;
     float bg0, bg1, bg2, T_thr;
 };
+
+// Bounded later passes.  A pass that filled all K_PASS slots sets the ray's next pass to collect only hits
+// at t < hint = t_K + 3 (t_K - t_{K/2}): about three times the depth the second half of its buffer spanned.
+// From its first node visit that pass prunes every subtree beyond the bound instead of exploring with an
+// unbounded K-th distance until its buffer fills (a restarted packet's lanes start deep inside the scene at
+// different t_min).  A bounded pass that found fewer than K_PASS hits has every hit below the bound, so the
+// ray continues at t_min = hint with an unbounded pass: the sequence of hits is the same, only the pass
+// boundaries move.  (t_K, t_{K/2}: the K-th and (K/2)-th hit of the pass.)
+struct PassEnd {
+    bool more;        // hits beyond this pass may exist
+    float t_min, hint;
+};
+__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur) {
+    PassEnd e;
+    if (full) {
+        e.more = true;
+        e.t_min = nextafterf(t_K, INFINITY);
+        const float h = __fadd_rn(t_K, __fmul_rn(3.0f, __fsub_rn(t_K, t_half)));
+        e.hint = h > e.t_min ? h : INFINITY;
+    } else if (hint_cur < INFINITY) {
+        e.more = true;
+        e.t_min = hint_cur;
+        e.hint = INFINITY;
+    } else {
+        e.more = false;
+        e.t_min = INFINITY;
+        e.hint = INFINITY;
+    }
+    return e;
+}
 
 struct FwdOut {
     float *bitmap, *dacc, *nacc, *normal, *alpha, *edn, *med;
@@ -170,6 +201,10 @@ __device__ __forceinline__ void prefetch_hit(const SceneP &sc, int idx) {
         if (DK == 0) prefetch_l2(c + 128);
     }
 }
+
+#ifndef FLARE_BWD_PREFETCH_L1
+#define FLARE_BWD_PREFETCH_L1 0
+#endif
 
 // A hit's raw primitive parameters, loaded one slot ahead by the forward kernel (load_raw) so that their
 // latency hides behind the current slot's tensor-core waits.
@@ -796,7 +831,11 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             }
         }
         {
-            bool active = have && ind >= 0 && T >= pp.T_thr;
+            PassEnd pe{ind >= 0, ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
+            if (pp.hint && have)
+                pe = pass_end(ind >= 0, t_hit, ind >= 0 ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
+                              pp.hint[ray]);
+            bool active = have && pe.more && T >= pp.T_thr;
             if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
             if (have) {
                 if (MODE != FLARE_FWD_MEDIAN) {
@@ -821,7 +860,8 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                     fo.med[2 * (size_t)ray] = med_t;
                     fo.med[2 * (size_t)ray + 1] = med_i;
                 }
-                pp.t_min[ray] = ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY;
+                pp.t_min[ray] = pe.t_min;
+                if (pp.hint) pp.hint[ray] = pe.hint;
                 pp.T[ray] = T;
             }
             if (have) pp.flags[slot] = active;
@@ -1096,8 +1136,13 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     t_next = pp.hit_t[(size_t)(h + 1) * pp.count + slot];
                     raw_ok = true;
                     const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)ind_next * Dec<DK>::COND_CHUNKS);
+#if FLARE_BWD_PREFETCH_L1
+                    prefetch_l1(c);
+                    if (DK == 0) prefetch_l1(c + 128);
+#else
                     prefetch_l2(c);
                     if (DK == 0) prefetch_l2(c + 128);
+#endif
                 }
                 mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, DK == 1 ? nullptr : hd1, 64, DK == 1 ? &m1 : nullptr);
             }
@@ -1392,10 +1437,17 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
             if (have) {
                 ++h;
                 if (!valid || h == K_PASS) {  // this ray's pass is done: write its state back
-                    const bool active = valid && T >= pp.T_thr;  // all K_PASS slots composited, not terminated
+                    // full: all K_PASS slots composited; a bounded pass that ended early continues too
+                    const bool full = valid && h == K_PASS;
+                    PassEnd pe{full, full ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
+                    if (pp.hint)
+                        pe = pass_end(full, t_hit, full ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
+                                      pp.hint[ray]);
+                    const bool active = pe.more && T >= pp.T_thr;
                     for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
                     for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
-                    pp.t_min[ray] = active ? nextafterf(t_hit, INFINITY) : INFINITY;
+                    pp.t_min[ray] = active ? pe.t_min : INFINITY;
+                    if (pp.hint) pp.hint[ray] = pe.hint;
                     pp.T[ray] = T;
                     pp.flags[slot] = active;
                     have = false;
@@ -1447,11 +1499,12 @@ done:
 // ================================================================================================
 // helpers: init, gradient scale, dW packing into the reference fragment layout
 // ================================================================================================
-__global__ void init_rays_kernel(int R, float *T, float *t_min, int *list, float *med) {
+__global__ void init_rays_kernel(int R, float *T, float *t_min, int *list, float *med, float *hint) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= R) return;
     T[i] = 1.0f;
     t_min[i] = 0.0f;
+    if (hint) hint[i] = INFINITY;
     list[i] = i;
     if (med) {
         med[2 * (size_t)i] = INFINITY;
@@ -1747,6 +1800,15 @@ static void grow_cache(flare_renderer *r) {
     r->hc_cap = want;
 }
 
+// Bounded later passes (pass_end above); FLARE_PASS_BOUND=0 turns them off.
+static bool pass_bound_on() {
+    static const bool on = [] {
+        const char *e = getenv("FLARE_PASS_BOUND");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    return on;
+}
+
 // Runs the pass loop: trace -> shade -> compaction, until no ray is active.
 template <typename ShadeFn>
 static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, cudaStream_t st, int shade_kind,
@@ -1775,7 +1837,8 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
         }
         off += count;
         int slot = prof_begin(r, PK_TRACE, st);
-        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st, K_PASS);
+        int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st, K_PASS,
+                             pass_bound_on() ? r->hint : nullptr);
         prof_end(r, slot, st);
         if (e) return e;
         slot = prof_begin(r, shade_kind, st);
@@ -1821,6 +1884,7 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
 static PassP make_pass(flare_renderer *r, const float *O, const float *v, float bg0, float bg1, float bg2,
                        float T_thr) {
     PassP pp{};
+    pp.hint = pass_bound_on() ? r->hint : nullptr;
     pp.O = O; pp.v = v;
     pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
     pp.T = r->T; pp.t_min = r->t_min;
@@ -1844,7 +1908,8 @@ int run_forward(flare_renderer *r, const flare_scene *sc, const flare_forward_ar
     fo.med = a->depth_and_index; fo.surface_normal = a->surface_normal;
     fo.reg_a = a->reg_a; fo.reg_b = a->reg_b;
     init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0],
-                                                       a->mode == FLARE_FWD_MEDIAN ? a->depth_and_index : nullptr);
+                                                       a->mode == FLARE_FWD_MEDIAN ? a->depth_and_index : nullptr,
+                                                       pass_bound_on() ? r->hint : nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
     {
         int e = order_rays(r, a->O, a->v, R, r->list[0], st);
@@ -1899,7 +1964,8 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     }
     bo.pgrad = rows_out ? a->prim_rows : r->pgrad;
     bo.vec4 = (reinterpret_cast<uintptr_t>(a->dL_dq) & 15) == 0;
-    init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr);
+    init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr,
+                                                       pass_bound_on() ? r->hint : nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
     {
         int e = order_rays(r, a->O, a->v, R, r->list[0], st);
@@ -2057,6 +2123,7 @@ int launch_shade_viewer(flare_renderer *r, const flare_scene *sc, const float *O
     if (count <= 0) return FLARE_OK;
     SceneP sp = scene_params(sc, nullptr);
     PassP pp = make_pass(r, O, v, 0.0f, 0.0f, 0.0f, T_thr);
+    pp.hint = nullptr;  // the viewer bounds its passes by the nearest sphere instead
     pp.T = T;
     pp.t_min = t_min;
     pp.list_in = lin;

@@ -5,8 +5,9 @@ For each config the GPU renders the whole image (every ray, so traversal runs un
 contention: the persistent heap kernel for large passes, the warp-per-ray kernel for the sparse tail).
 Then, for the sampled rays:
   * hit lists: every traversal pass the GPU ran (read back from the renderer's hit cache) equals, bit for
-    bit, the oracle's pass of a 42-slot buffer restarting at nextafter(t_42), cut from the oracle's full
-    (t, index)-sorted hit sequence (one brute-force sweep over all primitives per sampled ray);
+    bit, the oracle's pass of a 42-slot buffer (restarts at nextafter(t_42), bounded later passes:
+    oracle.bounded_passes), cut from the oracle's full (t, index)-sorted hit sequence (one brute-force
+    sweep over all primitives per sampled ray);
   * forward: RGB, depth / normal accumulators (training) and RGB / normal / alpha / expected depth
     (inference with geometry, config 1 at the config's T_threshold 1e-4) within 1e-3 of the oracle's
     compositing over the reference's 16-slot passes;
@@ -94,7 +95,7 @@ def test_pass_hit_lists_bit_exact(full):
     passes = f.r.pass_hits()
     assert len(passes) >= 2
     where = {int(r): j for j, r in enumerate(f.S)}
-    expect = [oracle.restart_passes(t, i, PASS_SLOTS) for t, i in f.hits]
+    expect = [oracle.bounded_passes(t, i, PASS_SLOTS) for t, i in f.hits]
     seen = np.zeros(len(f.S), np.int64)
     multi = 0
     for p, (ids, t, idx) in enumerate(passes):
