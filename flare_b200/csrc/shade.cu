@@ -94,6 +94,7 @@ struct PassP {
     const int *hit_idx;
     float *T, *t_min;
     float *hint;           // per ray: the next pass collects hits at t < hint only (null: unbounded passes)
+    float bound_f;         // bound of a pass after a full one: t_K + bound_f (t_K - t_{K/2})
     unsigned char *flags;  // per list slot: the ray stays active (compacted in list order after the pass)
     int *work;             // next unclaimed list slot (zeroed before each launch that claims rays)
     int *status;
@@ -112,12 +113,12 @@ struct PassEnd {
     bool more;        // hits beyond this pass may exist
     float t_min, hint;
 };
-__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur) {
+__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur, float bound_f) {
     PassEnd e;
     if (full) {
         e.more = true;
         e.t_min = nextafterf(t_K, INFINITY);
-        const float h = __fadd_rn(t_K, __fmul_rn(3.0f, __fsub_rn(t_K, t_half)));
+        const float h = __fadd_rn(t_K, __fmul_rn(bound_f, __fsub_rn(t_K, t_half)));
         e.hint = h > e.t_min ? h : INFINITY;
     } else if (hint_cur < INFINITY) {
         e.more = true;
@@ -201,10 +202,6 @@ __device__ __forceinline__ void prefetch_hit(const SceneP &sc, int idx) {
         if (DK == 0) prefetch_l2(c + 128);
     }
 }
-
-#ifndef FLARE_BWD_PREFETCH_L1
-#define FLARE_BWD_PREFETCH_L1 0
-#endif
 
 // A hit's raw primitive parameters, loaded one slot ahead by the forward kernel (load_raw) so that their
 // latency hides behind the current slot's tensor-core waits.
@@ -834,7 +831,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             PassEnd pe{ind >= 0, ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
             if (pp.hint && have)
                 pe = pass_end(ind >= 0, t_hit, ind >= 0 ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                              pp.hint[ray]);
+                              pp.hint[ray], pp.bound_f);
             bool active = have && pe.more && T >= pp.T_thr;
             if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
             if (have) {
@@ -1136,13 +1133,8 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     t_next = pp.hit_t[(size_t)(h + 1) * pp.count + slot];
                     raw_ok = true;
                     const char *c = reinterpret_cast<const char *>(sc.cond + (size_t)ind_next * Dec<DK>::COND_CHUNKS);
-#if FLARE_BWD_PREFETCH_L1
-                    prefetch_l1(c);
-                    if (DK == 0) prefetch_l1(c + 128);
-#else
                     prefetch_l2(c);
                     if (DK == 0) prefetch_l2(c + 128);
-#endif
                 }
                 mlp_forward_tile<DK>(smem, xt, h1t, h2t, mm, y4, DK == 1 ? nullptr : hd1, 64, DK == 1 ? &m1 : nullptr);
             }
@@ -1442,7 +1434,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     PassEnd pe{full, full ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
                     if (pp.hint)
                         pe = pass_end(full, t_hit, full ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                                      pp.hint[ray]);
+                                      pp.hint[ray], pp.bound_f);
                     const bool active = pe.more && T >= pp.T_thr;
                     for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
                     for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
@@ -1801,6 +1793,15 @@ static void grow_cache(flare_renderer *r) {
 }
 
 // Bounded later passes (pass_end above); FLARE_PASS_BOUND=0 turns them off.
+// FLARE_PASS_BOUND_F: the factor of the bound (default 3; the pass-exact parity test assumes 3).
+static float pass_bound_factor() {
+    static const float f = [] {
+        const char *e = getenv("FLARE_PASS_BOUND_F");
+        return e ? (float)atof(e) : 3.0f;
+    }();
+    return f;
+}
+
 static bool pass_bound_on() {
     static const bool on = [] {
         const char *e = getenv("FLARE_PASS_BOUND");
@@ -1885,6 +1886,7 @@ static PassP make_pass(flare_renderer *r, const float *O, const float *v, float 
                        float T_thr) {
     PassP pp{};
     pp.hint = pass_bound_on() ? r->hint : nullptr;
+    pp.bound_f = pass_bound_factor();
     pp.O = O; pp.v = v;
     pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
     pp.T = r->T; pp.t_min = r->t_min;
