@@ -1004,10 +1004,13 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     const int tid = threadIdx.x;
     Mma mm{};
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SM_BWD_MISC + 8);
+    void *mbar2 = smem + SM_BWD_MISC + 16;  // completion of a slot's layer-1 weight-gradient MMAs
+    uint32_t par2 = 0;
     float gscale = 1.0f, ginv = 1.0f;
     if (DEC) {
         if (tid == 0) {
             mbar_init(smem + SM_BWD_MISC, 1);
+            mbar_init(smem + SM_BWD_MISC + 16, 1);  // second barrier: the layer-1 weight-gradient MMAs
             fence_mbar_init();
             s_abort = 0;
             s_first = 1;
@@ -1328,6 +1331,10 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     for (int ks = 0; ks < 4; ++ks)
                         mma_f16_ss(mm.tmem + DXCOL, sdesc(smem_u32(h2t) + ks * 4096, 2048, 128),
                                    sdesc(smem_u32(smem + SM_W1) + ks * 256, 128, 1024), idesc_f16(128, 16, 0, 1), 1);
+                    // dX is all the rest of the slot waits for: a barrier of its own, so the LUT and geometry
+                    // gradients start while the weight-gradient MMAs below still run (they only read the
+                    // tiles, which nothing writes before the second barrier is waited for)
+                    mma_commit(mm.mbar);
                     // dW1 += d1^T X : M=64, N=128, K=128 hits (hi and lo parts of d1)
                     for (int ks = 0; ks < 8; ++ks)
                         mma_f16_ss(dwreg, sdesc(smem_u32(h1t) + ks * 256, 128, 2048),
@@ -1345,35 +1352,11 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                         mma_f16_ss(dwreg + half1 + 88, sdesc(smem_u32(h2t) + ks * 256, 128, 2048),
                                    sdesc(smem_u32(smem + SM_BWD_ONES) + ks * 256, 128, 2048), idesc_f16(64, 8, 1, 1),
                                    1);
-                    mma_commit(mm.mbar);
+                    mma_commit(mbar2);
                 }
-                mma_wait(mm);
+                mma_wait(mm);  // dX
                 const int wid = tid >> 5;
                 float *dcrow = reinterpret_cast<float *>(wid < 2 ? xt : h1t) + ((wid & 1) * 32 + (tid & 31)) * DC_ROW;
-                if constexpr (DK == 1) {  // delta1 = G1 (still in TMEM columns 0..63) gated by the ReLU mask
-#pragma unroll
-                    for (int cb = 0; cb < 4; ++cb) {
-                        float gv[16];
-                        tmem_ld16(mm.tmem + lane + 16 * cb, gv);
-                        tmem_wait_ld();
-                        if (valid) {
-#pragma unroll
-                            for (int e = 0; e < 16; e += 4) {
-                                float d[4];
-#pragma unroll
-                                for (int q = 0; q < 4; ++q)
-                                    d[q] = ((m1 >> (16 * cb + e + q)) & 1ull) ? gv[e + q] * ginv : 0.0f;
-                                *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + 16 * cb + e) =
-                                    make_float4(d[0], d[1], d[2], d[3]);
-                            }
-                        }
-                    }
-                } else if (valid) {  // delta1 into the staging row now (the tiles are free), ahead of the LUT work
-#pragma unroll
-                    for (int e = 0; e < 64; e += 4)
-                        *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + e) =
-                            make_float4(hd1[e] * ginv, hd1[e + 1] * ginv, hd1[e + 2] * ginv, hd1[e + 3] * ginv);
-                }
                 float dx16[16];
                 tmem_ld16(mm.tmem + lane + DXCOL, dx16);
                 tmem_wait_ld();
@@ -1406,8 +1389,35 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                 }
                 gu += dxu;
                 gw += dxw;
+                if (valid) geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
+                // the weight-gradient MMAs have read the X / H1 / H2 tiles: the staging rows may overwrite them
+                if (!mbar_wait(mbar2, par2)) atomicExch(&s_abort, 1);
+                par2 ^= 1u;
+                if constexpr (DK == 1) {  // delta1 = G1 (still in TMEM columns 0..63) gated by the ReLU mask
+#pragma unroll
+                    for (int cb = 0; cb < 4; ++cb) {
+                        float gv[16];
+                        tmem_ld16(mm.tmem + lane + 16 * cb, gv);
+                        tmem_wait_ld();
+                        if (valid) {
+#pragma unroll
+                            for (int e = 0; e < 16; e += 4) {
+                                float d[4];
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    d[q] = ((m1 >> (16 * cb + e + q)) & 1ull) ? gv[e + q] * ginv : 0.0f;
+                                *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + 16 * cb + e) =
+                                    make_float4(d[0], d[1], d[2], d[3]);
+                            }
+                        }
+                    }
+                } else if (valid) {  // delta1 into the staging row
+#pragma unroll
+                    for (int e = 0; e < 64; e += 4)
+                        *reinterpret_cast<float4 *>(dcrow + PGRAD_FLOATS + e) =
+                            make_float4(hd1[e] * ginv, hd1[e + 1] * ginv, hd1[e + 2] * ginv, hd1[e + 3] * ginv);
+                }
                 if (valid) {
-                    geom_grads(g, v, gu, gw, dLdt_depth, ow, sgn, nvalid, Nm, bo.lambda_normal, pg);
                     // this hit's row [packed primitive gradients | delta1] -> one bulk reduction
 #pragma unroll
                     for (int e = 0; e < PG_N; e += 2)
