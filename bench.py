@@ -5,8 +5,8 @@
 Workload (seeded synthetic data; no dataset is available offline):
   config 3 (default): data-parallel training step, 6M primitives, 8 views of 1920x1080 on a radius-3
       sphere (strong scaling: the same 16.6M rays at every N); every rank takes the same row band of every
-      view and renders its bands as one ray batch (FLARE_BENCH_SHARDING=views: whole views per rank); one
-      NCCL all-reduce of the flat gradient buffer per step.
+      view and renders its bands as one ray batch (FLARE_BENCH_SHARDING=views: whole views per rank,
+      =rows[:B]: row blocks dealt round-robin); one NCCL all-reduce of the flat gradient buffer per step.
   config 2: training step, 3M primitives, one 1600x1064 view (rays split in row bands over ranks).
 A step = SetGeometry (LBVH rebuild, as the reference rebuilds its IAS every step) + Forward_training +
 L1 loss / dL/dI in torch + Backward (+ all-reduce).  At N=1 the line also carries the config-2
@@ -126,24 +126,39 @@ def dist_setup(args):
 
 
 def build_workload(cfg, world, rank, device, seed=0, decoder="lut_pe", sharding=None):
-    """Scene + this rank's rays.  sharding "banded" (default for training): the rank's row band of every
-    view, concatenated into one ray batch (balanced ranks, one renderer call per step); "views": whole views
-    dealt round-robin, one batch per view."""
-    from flare_b200.dp import Shard, shard_rays, shard_rays_banded
+    """Scene + this rank's rays.  sharding "banded" (default): the rank's contiguous row band of every view,
+    concatenated into one ray batch (one renderer call per step); "rows[:B]": blocks of B image rows of
+    every view dealt round-robin over the ranks, one batch; "views": whole views dealt round-robin, one
+    batch per view.  Measured per-rank compute at 8 ranks (config 3, emulated on one GPU): banded 121-139 ms,
+    rows:68 122-139, rows:34 125-142, rows:1 158-160 (every 8th row: incoherent packets)."""
+    from flare_b200.dp import Shard, shard_rays, shard_rays_banded, shard_rays_interleaved
     from flare_b200.scene import camera_rays, make_scene, sphere_eye
     c = CONFIGS[cfg]
     sharding = sharding or os.environ.get("FLARE_BENCH_SHARDING", "banded")
     scene = make_scene(c["n_prims"], seed, decoder=decoder).to(device)
     W, H, V = c["width"], c["height"], c["views"]
     host = []
-    pieces = shard_rays_banded(V, W * H, world, rank) if sharding == "banded" else shard_rays(V, W * H, world, rank)
+    if sharding.startswith("rows"):  # "rows" or "rows:<block rows>"
+        blk = int(sharding.split(":")[1]) if ":" in sharding else max(1, -(-H // (4 * world)))
+        pieces = shard_rays_interleaved(V, W, H, world, rank, blk)
+    elif sharding == "banded":
+        pieces = shard_rays_banded(V, W * H, world, rank)
+    else:
+        pieces = shard_rays(V, W * H, world, rank)
+    by_view = {}
     for view, lo, cnt in pieces:
+        by_view.setdefault(view, []).append((lo, cnt))
+    for view, rng in by_view.items():
         eye = sphere_eye(view, V) if V > 1 else (0.0, 0.0, 3.0)
         O, v = camera_rays(W, H, 60.0, eye=eye)
         g = torch.Generator().manual_seed(1000 + view)
         target = torch.rand(W * H, 3, generator=g)
-        host.append(tuple(t[lo:lo + cnt].contiguous() for t in (O, v, target)))
-    if sharding == "banded" and len(host) > 1:
+        sel = torch.cat([torch.arange(lo, lo + cnt) for lo, cnt in rng])
+        if sharding == "views":
+            host += [tuple(t[lo:lo + cnt].contiguous() for t in (O, v, target)) for lo, cnt in rng]
+        else:
+            host.append(tuple(t[sel].contiguous() for t in (O, v, target)))
+    if sharding != "views" and len(host) > 1:
         host = [tuple(torch.cat([h[k] for h in host]) for k in range(3))]
     host = [tuple(t.pin_memory() for t in h) for h in host]
     shards = [Shard(*(t.to(device) for t in h)) for h in host]

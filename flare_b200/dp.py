@@ -44,6 +44,22 @@ def shard_rays(n_views: int, rays_per_view: int, world: int, rank: int):
     return [(v, lo, hi - lo)]
 
 
+def shard_rays_interleaved(n_views: int, width: int, height: int, world: int, rank: int, block_rows: int = 1):
+    """This rank's rays when the image rows of every view are cut into blocks of `block_rows` rows dealt
+    round-robin over the ranks (rank r takes blocks r, r + world, ...): (view, first ray, ray count) pieces
+    of one block each.  Every rank then sees a mix of dense and sparse parts of every view (one contiguous
+    band per rank is not balanced: the middle rows of an image cross the scene's densest part), while a
+    block of rows keeps its rays' directions close (a traversal packet stays coherent); a caller passes a
+    rank's pieces to the renderer as ONE ray batch."""
+    out = []
+    nblk = (height + block_rows - 1) // block_rows
+    for v in range(n_views):
+        for b in range(rank, nblk, world):
+            y0, y1 = b * block_rows, min(height, (b + 1) * block_rows)
+            out.append((v, y0 * width, (y1 - y0) * width))
+    return out
+
+
 def shard_rays_banded(n_views: int, rays_per_view: int, world: int, rank: int):
     """This rank's (view, first ray, ray count) pieces when every rank takes the same row band of every
     view: band `rank` of `world` contiguous bands per view.  A rank's work then averages over all views

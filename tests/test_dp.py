@@ -46,6 +46,20 @@ def test_banded_sharding_covers_every_ray_once_and_balances():
             assert max(per_rank) - min(per_rank) <= views  # every rank has its share of every view
 
 
+def test_interleaved_sharding_covers_every_ray_once():
+    for views, W, H in [(8, 7, 10), (1, 5, 3), (3, 4, 9)]:
+        for world in (1, 2, 3, 4, 8):
+            for blk in (1, 3):
+                seen = set()
+                for rank in range(world):
+                    for v, lo, cnt in dp.shard_rays_interleaved(views, W, H, world, rank, blk):
+                        assert lo % W == 0 and ((lo // W) // blk) % world == rank and cnt % W == 0
+                        for i in range(lo, lo + cnt):
+                            assert (v, i) not in seen
+                            seen.add((v, i))
+                assert len(seen) == views * W * H
+
+
 def test_grad_buffer_segments_are_aligned_views():
     g = dp.GradBuffer(37, True, "cpu")
     for name, t in g.views.items():
