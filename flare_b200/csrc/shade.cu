@@ -95,6 +95,7 @@ struct PassP {
     float *T, *t_min;
     float *hint;           // per ray: the next pass collects hits at t < hint only (null: unbounded passes)
     float bound_f;         // bound of a pass after a full one: t_K + bound_f (t_K - t_{K/2})
+    int bound_T;           // the bound follows the ray's remaining transmittance (pass_end)
     unsigned char *flags;  // per list slot: the ray stays active (compacted in list order after the pass)
     int *work;             // next unclaimed list slot (zeroed before each launch that claims rays)
     int *status;
@@ -113,12 +114,22 @@ struct PassEnd {
     bool more;        // hits beyond this pass may exist
     float t_min, hint;
 };
-__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur, float bound_f) {
+// bound_T (FLARE_PASS_BOUND_T=1): the bound instead follows the hits the ray still needs: with d the mean
+// optical depth -ln(1 - alpha) of this pass's K hits (from T0, T at its start, to T1 at its end) about
+// n = ln(T1 / T_thr) / d more hits bring T below T_thr, so the bound is t_K + bound_f n (t_K - t_{K/2}) / (K/2).
+__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur, float bound_f,
+                                            bool bound_T = false, float T0 = 1.0f, float T1 = 1.0f,
+                                            float T_thr = 0.0f) {
     PassEnd e;
     if (full) {
         e.more = true;
         e.t_min = nextafterf(t_K, INFINITY);
-        const float h = __fadd_rn(t_K, __fmul_rn(bound_f, __fsub_rn(t_K, t_half)));
+        float h = __fadd_rn(t_K, __fmul_rn(bound_f, __fsub_rn(t_K, t_half)));
+        if (bound_T) {
+            const float d = logf(T0 / T1) * (1.0f / K_PASS);
+            const float n = (d > 1e-6f && T1 > T_thr) ? logf(T1 / T_thr) / d : INFINITY;
+            h = t_K + bound_f * n * (t_K - t_half) * (2.0f / K_PASS);
+        }
         e.hint = h > e.t_min ? h : INFINITY;
     } else if (hint_cur < INFINITY) {
         e.more = true;
@@ -700,7 +711,16 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
     char *tile = smem + SM_FWD_TILE;
     unsigned long long nhits = 0, ntiles = 0;
     const int nchunks = (pp.count + 127) / 128;
-    for (int chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    // Chunks of 128 list slots are claimed in list order by whichever CTA is free (decoder path: the grid is
+    // the resident CTAs), so CTAs that drew cheap chunks take more instead of idling at the end of the pass.
+    __shared__ int s_chunk;
+    int chunk = blockIdx.x;
+    if (DEC) {
+        if (tid == 0) s_chunk = atomicAdd(pp.work, 1);
+        __syncthreads();
+        chunk = s_chunk;
+    }
+    for (; chunk < nchunks;) {
         const int slot = chunk * 128 + tid;
         const bool have = slot < pp.count;
         const int ray = have ? pp.list_in[slot] : -1;
@@ -831,7 +851,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             PassEnd pe{ind >= 0, ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
             if (pp.hint && have)
                 pe = pass_end(ind >= 0, t_hit, ind >= 0 ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                              pp.hint[ray], pp.bound_f);
+                              pp.hint[ray], pp.bound_f, pp.bound_T, pp.T[ray], T, pp.T_thr);
             bool active = have && pe.more && T >= pp.T_thr;
             if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
             if (have) {
@@ -862,6 +882,14 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
                 pp.T[ray] = T;
             }
             if (have) pp.flags[slot] = active;
+        }
+        if (DEC) {
+            __syncthreads();  // every row has read s_chunk
+            if (tid == 0) s_chunk = atomicAdd(pp.work, 1);
+            __syncthreads();
+            chunk = s_chunk;
+        } else {
+            chunk += gridDim.x;
         }
     }
 done:
@@ -1444,7 +1472,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     PassEnd pe{full, full ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
                     if (pp.hint)
                         pe = pass_end(full, t_hit, full ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                                      pp.hint[ray], pp.bound_f);
+                                      pp.hint[ray], pp.bound_f, pp.bound_T, pp.T[ray], T, pp.T_thr);
                     const bool active = pe.more && T >= pp.T_thr;
                     for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
                     for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
@@ -1667,6 +1695,7 @@ static int launch_fwd(flare_renderer *r, const SceneP &sp, const PassP &pp, cons
     if (DEC) FLARE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int chunks = (pp.count + 127) / 128;
     int grid = DEC ? std::min(chunks, r->num_sms * FLARE_FWD_CTAS) : chunks;
+    if (DEC) FLARE_CUDA_TRY(cudaMemsetAsync(pp.work, 0, sizeof(int), st));
     kern<<<grid, 128, smem, st>>>(sp, pp, fo);
     FLARE_CUDA_TRY(cudaGetLastError());
     return FLARE_OK;
@@ -1897,6 +1926,7 @@ static PassP make_pass(flare_renderer *r, const float *O, const float *v, float 
     PassP pp{};
     pp.hint = pass_bound_on() ? r->hint : nullptr;
     pp.bound_f = pass_bound_factor();
+    pp.bound_T = getenv("FLARE_PASS_BOUND_T") && strcmp(getenv("FLARE_PASS_BOUND_T"), "1") == 0;
     pp.O = O; pp.v = v;
     pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
     pp.T = r->T; pp.t_min = r->t_min;
