@@ -95,7 +95,6 @@ struct PassP {
     float *T, *t_min;
     float *hint;           // per ray: the next pass collects hits at t < hint only (null: unbounded passes)
     float bound_f;         // bound of a pass after a full one: t_K + bound_f (t_K - t_{K/2})
-    int bound_T;           // the bound follows the ray's remaining transmittance (pass_end)
     unsigned char *flags;  // per list slot: the ray stays active (compacted in list order after the pass)
     int *work;             // next unclaimed list slot (zeroed before each launch that claims rays)
     int *status;
@@ -114,22 +113,12 @@ struct PassEnd {
     bool more;        // hits beyond this pass may exist
     float t_min, hint;
 };
-// bound_T (FLARE_PASS_BOUND_T=1): the bound instead follows the hits the ray still needs: with d the mean
-// optical depth -ln(1 - alpha) of this pass's K hits (from T0, T at its start, to T1 at its end) about
-// n = ln(T1 / T_thr) / d more hits bring T below T_thr, so the bound is t_K + bound_f n (t_K - t_{K/2}) / (K/2).
-__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur, float bound_f,
-                                            bool bound_T = false, float T0 = 1.0f, float T1 = 1.0f,
-                                            float T_thr = 0.0f) {
+__device__ __forceinline__ PassEnd pass_end(bool full, float t_K, float t_half, float hint_cur, float bound_f) {
     PassEnd e;
     if (full) {
         e.more = true;
         e.t_min = nextafterf(t_K, INFINITY);
-        float h = __fadd_rn(t_K, __fmul_rn(bound_f, __fsub_rn(t_K, t_half)));
-        if (bound_T) {
-            const float d = logf(T0 / T1) * (1.0f / K_PASS);
-            const float n = (d > 1e-6f && T1 > T_thr) ? logf(T1 / T_thr) / d : INFINITY;
-            h = t_K + bound_f * n * (t_K - t_half) * (2.0f / K_PASS);
-        }
+        const float h = __fadd_rn(t_K, __fmul_rn(bound_f, __fsub_rn(t_K, t_half)));
         e.hint = h > e.t_min ? h : INFINITY;
     } else if (hint_cur < INFINITY) {
         e.more = true;
@@ -851,7 +840,8 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             PassEnd pe{ind >= 0, ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
             if (pp.hint && have)
                 pe = pass_end(ind >= 0, t_hit, ind >= 0 ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                              pp.hint[ray], pp.bound_f, pp.bound_T, pp.T[ray], T, pp.T_thr);
+                              pp.hint[ray], pp.bound_f
+                              );
             bool active = have && pe.more && T >= pp.T_thr;
             if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
             if (have) {
@@ -1472,7 +1462,8 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     PassEnd pe{full, full ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
                     if (pp.hint)
                         pe = pass_end(full, t_hit, full ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                                      pp.hint[ray], pp.bound_f, pp.bound_T, pp.T[ray], T, pp.T_thr);
+                                      pp.hint[ray], pp.bound_f
+                              );
                     const bool active = pe.more && T >= pp.T_thr;
                     for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
                     for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
@@ -1926,7 +1917,6 @@ static PassP make_pass(flare_renderer *r, const float *O, const float *v, float 
     PassP pp{};
     pp.hint = pass_bound_on() ? r->hint : nullptr;
     pp.bound_f = pass_bound_factor();
-    pp.bound_T = getenv("FLARE_PASS_BOUND_T") && strcmp(getenv("FLARE_PASS_BOUND_T"), "1") == 0;
     pp.O = O; pp.v = v;
     pp.hit_t = r->hit_t; pp.hit_idx = r->hit_idx;
     pp.T = r->T; pp.t_min = r->t_min;
