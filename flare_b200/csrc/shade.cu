@@ -840,8 +840,7 @@ __global__ void __launch_bounds__(128) shade_fwd_kernel(SceneP sc, PassP pp, Fwd
             PassEnd pe{ind >= 0, ind >= 0 ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
             if (pp.hint && have)
                 pe = pass_end(ind >= 0, t_hit, ind >= 0 ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                              pp.hint[ray], pp.bound_f
-                              );
+                              pp.hint[ray], pp.bound_f);
             bool active = have && pe.more && T >= pp.T_thr;
             if (MODE == FLARE_FWD_MEDIAN) active = active && (T > 0.5f);
             if (have) {
@@ -1462,8 +1461,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     PassEnd pe{full, full ? nextafterf(t_hit, INFINITY) : INFINITY, INFINITY};
                     if (pp.hint)
                         pe = pass_end(full, t_hit, full ? pp.hit_t[(size_t)(K_PASS / 2 - 1) * pp.count + slot] : 0.0f,
-                                      pp.hint[ray], pp.bound_f
-                              );
+                                      pp.hint[ray], pp.bound_f);
                     const bool active = pe.more && T >= pp.T_thr;
                     for (int c = 0; c < 3; ++c) bo.I[3 * (size_t)ray + c] = -run[c];
                     for (int c = 0; c < 4; ++c) bo.prefix[4 * (size_t)ray + c] = P[c];
