@@ -392,11 +392,13 @@ print("OK")
     assert out.returncode == 0 and "OK" in out.stdout, out.stdout[-2000:] + out.stderr[-2000:]
 
 
-@pytest.mark.parametrize("bvh4", ["1", "0"])
-def test_training_passes_heap_traversal(bvh4):
-    """Training passes through the block-wide heap traversal (4-wide or binary hierarchy), which full-size
-    passes use: FLARE_TRACE_G32_MAX=0 turns off the warp-per-ray kernel that passes of <= 16384 rays take.
-    Both environment switches are read once per process, hence the child process."""
+@pytest.mark.parametrize("variant", ["bvh4", "binary", "inline", "unbounded"])
+def test_training_passes_heap_traversal(variant):
+    """Training passes through the block-wide heap traversal, which full-size passes use
+    (FLARE_TRACE_G32_MAX=0 turns off the warp-per-ray kernel that passes of <= 16384 rays take), over the
+    4-wide hierarchy, the binary one, the binary one with inline leaf records (FLARE_TRACE_INLINE=1), and
+    with the bounded later passes turned off (FLARE_PASS_BOUND=0).  The switches are read once per
+    process, hence the child process."""
     import subprocess
     import sys
     code = r"""
@@ -425,7 +427,10 @@ assert np.abs(bitmap.cpu().numpy() - ref["rgb"]).max() < 1e-3
 print("OK")
 """
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, FLARE_BVH4=bvh4, FLARE_TRACE_G32_MAX="0",
+    extra = {"FLARE_BVH4": "0", "FLARE_TRACE_INLINE": "0", "FLARE_PASS_BOUND": "1"}
+    extra.update({"bvh4": {"FLARE_BVH4": "1"}, "binary": {}, "inline": {"FLARE_TRACE_INLINE": "1"},
+                  "unbounded": {"FLARE_PASS_BOUND": "0"}}[variant])
+    env = dict(os.environ, **extra, FLARE_TRACE_G32_MAX="0",
                PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
     out = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and "OK" in out.stdout, out.stdout[-2000:] + out.stderr[-2000:]
