@@ -48,10 +48,10 @@ B_HIT_FWD = 56 + 192             # primitive record + fp16 descriptor row
 B_HIT_BWD = 56 + 192 + 440       # re-read + gradient writes (14 geometry + 96 descriptor fp32)
 B_RAY_FWD, B_RAY_BWD = 44, 24
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per composited hit of each timed kernel, from a
-# one-pass ncu capture of this build over the config-3 bench workload itself (per-launch averages of the
-# captured launches x 39 launches per step / 1.0224e9 hits per step); the bench scales it by the hits of its
-# own launches, which reproduces the measured per-launch traffic on config 3.
-DRAM_BYTES_PER_HIT = {"trace": 13.0, "shade_forward": 18.9, "shade_backward": 20.3}
+# one-pass ncu capture of this build over the config-3 bench workload itself (bytes per step / 1.0224e9 hits
+# per step); the bench scales it by the hits of its own launches, which reproduces the measured per-launch
+# traffic on config 3.
+DRAM_BYTES_PER_HIT = {"trace": 16.2, "shade_forward": 17.8, "shade_backward": 20.2}
 FLOP_HIT_FWD = 2 * (128 * 64 + 64 * 64 + 64 * 4)
 T_THR_FORWARD = 1e-4  # BASELINE config 1's early-termination threshold
 
