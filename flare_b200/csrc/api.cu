@@ -148,6 +148,7 @@ int flare_create(int number_of_sides, float chi_square_squared_radius, int max_b
     if (e == cudaSuccess) e = cudaMalloc(&(p), (bytes))
     ALLOC(r->t_min, R * sizeof(float));
     ALLOC(r->hint, R * sizeof(float));
+    ALLOC(r->chunk_tk, (R / 256 + 2) * sizeof(float));
     ALLOC(r->T, R * sizeof(float));
     ALLOC(r->list[0], R * sizeof(int));
     ALLOC(r->list[1], R * sizeof(int));
@@ -191,7 +192,7 @@ int flare_destroy(flare_renderer *r) {
     for (int i = 0; i < 2 * flare_renderer::PROF_SLOTS; ++i)
         if (r->prof_ev[i]) cudaEventDestroy(r->prof_ev[i]);
     void *ptrs[] = {r->frames, r->rec, r->aabb, r->morton, r->morton_sorted, r->ids, r->ids_sorted, r->nodes,
-                    r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->hint, r->T, r->list[0], r->list[1],
+                    r->parent, r->refit_flag, r->bounds, r->sort_tmp, r->t_min, r->hint, r->chunk_tk, r->T, r->list[0], r->list[1],
                     r->hit_t, r->hit_idx, r->ray_aux, r->counters, r->dfeat_priv, r->pgrad, r->vw_buf, r->ray_keys, r->ray_ids_tmp, r->ray_sort_tmp, r->pass_flags, r->select_tmp, r->dw, r->gscale, r->hc_sum, r->hc_list, r->hc_t, r->hc_idx, r->dstatus, r->dstats,
                     r->ploc_scratch, r->nodes4, r->bvh4_scratch, r->nodesL};
     for (void *p : ptrs)

@@ -32,6 +32,7 @@ struct flare_renderer {
     // ---- per-ray scratch, sized max_rays ----
     float *t_min = nullptr;
     float *hint = nullptr;   // per ray: bound of its next pass (hits at t < hint), +inf = unbounded
+    float *chunk_tk = nullptr;  // two-phase first pass: largest K-th hit distance per sparse 32-ray chunk
     float *T = nullptr;
     int *list[2] = {nullptr, nullptr};
     float *hit_t = nullptr;   // (16, max_rays)
@@ -123,7 +124,9 @@ int build_geometry(flare_renderer *r, const float *m, const float *scale, const 
 // ray id; outputs (16, out_stride) slot-major at column j.
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
                  int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k = K_HITS,
-                 const float *t_max = nullptr);  // t_max: optional per-ray bound, hits at t >= t_max[ray] excluded
+                 const float *t_max = nullptr,  // t_max: optional per-ray bound, hits at t >= t_max[ray] excluded
+                 bool first = false);  // first pass of a bounded pass loop: t_max is the pass-bound array
+                                       // (all +inf), which the traversal may set (two-phase first pass)
 
 // trace.cu: writes the coherence order of R rays into list_out
 int order_rays(flare_renderer *r, const float *O, const float *v, int R, int *list_out, cudaStream_t st);

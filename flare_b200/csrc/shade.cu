@@ -1867,7 +1867,7 @@ static int pass_loop(flare_renderer *r, const float *O, const float *v, int R, c
         off += count;
         int slot = prof_begin(r, PK_TRACE, st);
         int e = launch_trace(r, O, v, r->t_min, r->list[cur], count, ht, hi, count, st, K_PASS,
-                             pass_bound_on() ? r->hint : nullptr);
+                             pass_bound_on() ? r->hint : nullptr, passes == 0);
         prof_end(r, slot, st);
         if (e) return e;
         slot = prof_begin(r, shade_kind, st);

@@ -269,6 +269,12 @@ __global__ void __launch_bounds__(128, FLARE_TRACE_MIN_BLOCKS) trace_packet_kern
 // column, so accesses are bank-conflict free).  An accepted hit replaces the root (the current K-th
 // nearest) and sifts down about log2 K levels instead of shifting a sorted register array; the heap is
 // sorted once when the pass ends.  Frees the ~2K registers of the register buffer.
+// Bound of a first-pass chunk: its phase-1 neighbours' largest K-th hit distance times this factor.
+#ifndef FLARE_FIRST_BOUND_F
+#define FLARE_FIRST_BOUND_F 1.0f
+#endif
+constexpr float FIRST_BOUND_F = FLARE_FIRST_BOUND_F;
+
 __device__ __forceinline__ bool key_greater(float ta, int ia, float tb, int ib) {
     return ta > tb || (ta == tb && ia > ib);
 }
@@ -351,7 +357,8 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
     const int *__restrict__ ray_ids, int count, const Node *__restrict__ nodes, const float4 *__restrict__ rec,
     const int *__restrict__ ids, int n, float *__restrict__ t_out, int *__restrict__ idx_out, int stride,
     const PolyConst poly, int *__restrict__ status, unsigned long long *__restrict__ stats,
-    const float *__restrict__ tmax_ = nullptr, int *__restrict__ chunk_ctr = nullptr) {
+    const float *__restrict__ tmax_ = nullptr, int *__restrict__ chunk_ctr = nullptr, int phase = 0,
+    float *__restrict__ chunk_tk = nullptr, float *__restrict__ hint_out = nullptr) {
     __shared__ int s_node[4][TRACE_STACK];
     __shared__ unsigned s_mask[4][TRACE_STACK];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
@@ -359,13 +366,25 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
     // PERSIST: the grid holds as many blocks as fit at once and every warp claims the next 32 rays of
     // the list until it is exhausted, so a warp slot frees as soon as its rays are done instead of
     // when the slowest warp of its block is (dense and sparse rays share blocks).
+    // First-pass phases (phase 1, then 2): phase 1 traces every FIRST_STRIDE-th 32-ray chunk of the list
+    // and records, per chunk, the largest K-th hit distance of its rays (+inf if one of them found fewer
+    // than K hits); phase 2 traces the other chunks, each bounded by its two phase-1 neighbours' record
+    // (coherent rays: the neighbouring packets of the ray order), the bound also going to hint_out so that
+    // a ray that finds fewer than K hits below it continues there (the bounded-pass rule).
+    constexpr int FIRST_STRIDE = 8;
+    const int nchunks = (count + 31) / 32;
     int base = blockIdx.x * blockDim.x + (threadIdx.x & ~31);
     while (true) {
+    int chunk = 0;
     if (PERSIST) {
         int b = 0;
-        if (lane == 0) b = atomicAdd(chunk_ctr, 32);
-        base = __shfl_sync(0xffffffffu, b, 0);
-        if (base >= count) break;
+        if (lane == 0) b = atomicAdd(chunk_ctr, phase ? 1 : 32);
+        b = __shfl_sync(0xffffffffu, b, 0);
+        if (phase == 1) chunk = b * FIRST_STRIDE;
+        else if (phase == 2) chunk = (b / (FIRST_STRIDE - 1)) * FIRST_STRIDE + b % (FIRST_STRIDE - 1) + 1;
+        else chunk = b / 32;
+        base = chunk * 32;
+        if (chunk >= nchunks) break;
     }
     const int j = base + lane;
     const bool live = j < count;
@@ -377,6 +396,16 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
         v = make_float3(v_[3 * (size_t)ray], v_[3 * (size_t)ray + 1], v_[3 * (size_t)ray + 2]);
         t_min = tmin_[ray];
         if (tmax_) tcap = nextafterf(tmax_[ray], -INFINITY);  // hits must lie before t_max
+    }
+    if (PERSIST && phase == 2) {
+        const int a = chunk / FIRST_STRIDE;
+        float bnd = __ldcg(chunk_tk + a);
+        if ((a + 1) * FIRST_STRIDE < nchunks) bnd = fmaxf(bnd, __ldcg(chunk_tk + a + 1));
+        bnd = __fmul_rn(bnd, FIRST_BOUND_F);
+        if (bnd < INFINITY && live && t_min < bnd) {
+            tcap = fminf(tcap, nextafterf(bnd, -INFINITY));
+            hint_out[ray] = bnd;
+        }
     }
     extern __shared__ __align__(16) unsigned char heap_smem[];
     HeapBuf<K> kb;
@@ -488,6 +517,11 @@ __global__ void __launch_bounds__(128, 5) trace_heap_kernel(
             c = nc;
             d = nd;
         }
+    }
+    if (PERSIST && phase == 1) {  // this chunk's largest K-th hit distance (+inf: a ray found fewer)
+        float tk = live ? (kb.ri != 0x7fffffff ? kb.rt : INFINITY) : -INFINITY;
+        for (int o = 16; o > 0; o >>= 1) tk = fmaxf(tk, __shfl_xor_sync(0xffffffffu, tk, o));
+        if (lane == 0) __stcg(chunk_tk + chunk / FIRST_STRIDE, tk);
     }
     if (live) {  // heap sort into ascending slots
         heap_emit(kb, t_out, idx_out, stride, j);
@@ -1098,7 +1132,7 @@ static int getenv_int(const char *name, int dflt) {
 
 int launch_trace(flare_renderer *r, const float *O, const float *v, const float *t_min, const int *ray_ids,
                  int count, float *t_out, int *idx_out, int out_stride, cudaStream_t st, int k,
-                 const float *t_max) {
+                 const float *t_max, bool first) {
     if (count <= 0) return FLARE_OK;
     const int B = 128;
     // Sparse passes: G lanes per ray, G chosen so the pass still spreads over the whole GPU
@@ -1158,6 +1192,19 @@ int launch_trace(flare_renderer *r, const float *O, const float *v, const float 
         FLARE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, trace_heap_kernel<true, K_PASS, true>, B,
                                                                      smem));
         const int grid = std::max(1, std::min((count + B - 1) / B, r->num_sms * std::max(per_sm, 1)));
+        static const bool first_phases = getenv_int("FLARE_FIRST_BOUND", 1) != 0;
+        if (first && t_max && first_phases && count >= 65536 && r->chunk_tk) {
+            // a first pass in two phases (see trace_heap_kernel): sparse chunks, then the rest bounded
+            for (int phase = 1; phase <= 2; ++phase) {
+                FLARE_CUDA_TRY(cudaMemsetAsync(r->counters + 2, 0, sizeof(int), st));
+                trace_heap_kernel<true, K_PASS, true><<<grid, B, smem, st>>>(
+                    O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride,
+                    r->poly, r->dstatus, r->dstats, t_max, r->counters + 2, phase, r->chunk_tk,
+                    const_cast<float *>(t_max));
+                FLARE_CUDA_TRY(cudaGetLastError());
+            }
+            return FLARE_OK;
+        }
         FLARE_CUDA_TRY(cudaMemsetAsync(r->counters + 2, 0, sizeof(int), st));
         trace_heap_kernel<true, K_PASS, true><<<grid, B, smem, st>>>(
             O, v, t_min, ray_ids, count, r->nodes, r->rec, r->ids_sorted, r->n, t_out, idx_out, out_stride, r->poly,

@@ -302,38 +302,3 @@ class CpuBvh:
         except Exception:  # interpreter shutdown
             pass
 
-
-def bounded_passes(t, idx, k):
-    """The renderer's internal passes over one ray's sorted hit sequence (k-slot buffer; bounded later
-    passes): a pass holds the next k hits at or beyond t_min and below the pass bound.  After a full pass
-    the next starts at nextafter(t_k) with bound t_k + 3 (t_k - t_{k/2}) (fp32, in that operation order; no
-    bound when that is not above the new t_min); after a bounded pass that came back short the next starts
-    at the bound, unbounded; an unbounded short pass ends the sequence.  Hits tied with t_k but later in
-    (t, index) order are skipped by a restart, as the reference's k-buffer skips them.  Returns the list of
-    (t, idx) arrays."""
-    t = np.asarray(t, np.float32)
-    idx = np.asarray(idx, np.int32)
-    n = len(t)
-    out = []
-    pos = 0
-    t_min = np.float32(0.0)
-    hint = np.float32(np.inf)
-    while True:
-        while pos < n and t[pos] < t_min:
-            pos += 1
-        end = pos
-        while end < n and end - pos < k and t[end] < hint:
-            end += 1
-        out.append((t[pos:end], idx[pos:end]))
-        if end - pos == k:
-            tk, th = t[end - 1], t[pos + k // 2 - 1]
-            t_min = np.nextafter(tk, np.float32(np.inf), dtype=np.float32)
-            h = np.float32(tk + np.float32(np.float32(3.0) * np.float32(tk - th)))
-            hint = h if h > t_min else np.float32(np.inf)
-            pos = end
-        elif hint < np.inf:
-            t_min = hint
-            hint = np.float32(np.inf)
-            pos = end
-        else:
-            return out
