@@ -1070,22 +1070,58 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
     bool raw_ok = false;  // raw_next / t_next hold this row's next slot
     unsigned long long ntiles = 0;
     bool bulk_pending = false;  // this thread's last bulk reduction may still be reading its staging row
+    // Each warp reserves list slots 32 at a time (one atomic), reads their ray ids and pulls the rays'
+    // state and first hit into L2 when it reserves them, and reserves the next 32 once half are used: a
+    // row that claims a ray then waits for one L2 round trip, not for an atomic, the id and the state in
+    // turn (a claim stalls the whole tile at the next barrier, and some row of a tile claims most slots).
+    int res_base = -1, res_used = 32, nx_base = -1;  // warp-uniform
+    int res_id = -1, nx_id = -1;                      // per lane: ray id of slot base + lane (-1: past the list)
+    auto fetch_reserve = [&](int &b, int &id) {
+        int x = 0;
+        if ((tid & 31) == 0) x = atomicAdd(pp.work, 32);
+        b = __shfl_sync(0xffffffffu, x, 0);
+        const int s_ = b + (tid & 31);
+        id = s_ < pp.count ? pp.list_in[s_] : -1;
+        if (id >= 0) {
+            prefetch_l2(pp.O + 3 * (size_t)id);
+            prefetch_l2(pp.v + 3 * (size_t)id);
+            prefetch_l2(pp.T + id);
+            prefetch_l2(bo.dL_dI + 3 * (size_t)id);
+            prefetch_l2(bo.I + 3 * (size_t)id);
+            prefetch_l2(bo.dacc + 4 * (size_t)id);
+            prefetch_l2(bo.prefix + 4 * (size_t)id);
+            prefetch_l2(bo.surface_normal + 3 * (size_t)id);
+            prefetch_l2(pp.hit_idx + s_);
+            prefetch_l2(pp.hit_t + s_);
+        }
+    };
     while (true) {
-        {   // rows without a ray claim the next ones (one atomic per warp)
+        {   // rows without a ray claim the next ones from the warp's reserve of list slots
             const bool need = !have && !exhausted;
             const unsigned nm = __ballot_sync(0xffffffffu, need);
+            const int ln = tid & 31;
             if (nm) {
-                const int ln = tid & 31, leader = __ffs(nm) - 1;
-                int base = 0;
-                if (ln == leader) base = atomicAdd(pp.work, __popc(nm));
-                base = __shfl_sync(0xffffffffu, base, leader);
+                const int k = __popc(nm);
+                // the reserve runs out with this claim: the next one must be there before the swap below
+                if (res_used + k >= 32 && nx_base < 0) fetch_reserve(nx_base, nx_id);
+                const int e = res_used + __popc(nm & ((1u << ln) - 1u));
+                const int id_r = __shfl_sync(0xffffffffu, res_id, e & 31);
+                const int id_n = __shfl_sync(0xffffffffu, nx_id, e & 31);
+                const int s_ = e < 32 ? res_base + e : nx_base + e - 32;
+                const int rid = e < 32 ? id_r : id_n;
+                res_used += k;
+                if (res_used >= 32) {
+                    res_base = nx_base;
+                    res_id = nx_id;
+                    res_used -= 32;
+                    nx_base = -1;
+                }
                 if (need) {
-                    const int s_ = base + __popc(nm & ((1u << ln) - 1u));
-                    if (s_ < pp.count) {
+                    if (s_ < pp.count && s_ >= 0 && rid >= 0) {
                         slot = s_;
                         have = true;
                         h = 0;
-                        ray = pp.list_in[slot];
+                        ray = rid;
                         O = make_float3(pp.O[3 * (size_t)ray], pp.O[3 * (size_t)ray + 1], pp.O[3 * (size_t)ray + 2]);
                         v = make_float3(pp.v[3 * (size_t)ray], pp.v[3 * (size_t)ray + 1], pp.v[3 * (size_t)ray + 2]);
                         T = pp.T[ray];
@@ -1105,6 +1141,7 @@ __global__ void __launch_bounds__(128) shade_bwd_kernel(SceneP sc, PassP pp, Bwd
                     }
                 }
             }
+            if (nx_base < 0 && res_used >= 16) fetch_reserve(nx_base, nx_id);  // the next 32 slots, ahead
         }
         {
             ind = have ? ind_next : -1;
