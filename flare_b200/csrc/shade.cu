@@ -2064,10 +2064,6 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
     init_rays_kernel<<<(R + 255) / 256, 256, 0, st>>>(R, r->T, r->t_min, r->list[0], nullptr,
                                                        pass_bound_on() ? r->hint : nullptr);
     FLARE_CUDA_TRY(cudaGetLastError());
-    {
-        int e = order_rays(r, a->O, a->v, R, r->list[0], st);
-        if (e) return e;
-    }
     if (dec) {
         FLARE_CUDA_TRY(cudaMemsetAsync(r->dw, 0, DW_TOTAL * sizeof(float), st));
         FLARE_CUDA_TRY(cudaMemsetAsync(r->gscale, 0, sizeof(float), st));
@@ -2128,8 +2124,9 @@ int run_backward(flare_renderer *r, const flare_scene *sc, const flare_backward_
         FLARE_CUDA_TRY(cudaMemcpyAsync(r->dstats + ST_PASSES, &np, sizeof(np), cudaMemcpyHostToDevice, st));
         FLARE_CUDA_TRY(cudaStreamSynchronize(st));
         prof_collect(r);
-    } else {
-        e = pass_loop(r, a->O, a->v, R, st, PK_SHADE_BWD, shade);
+    } else {  // no matching forward: trace again, from the coherence order of the rays
+        e = order_rays(r, a->O, a->v, R, r->list[0], st);
+        if (!e) e = pass_loop(r, a->O, a->v, R, st, PK_SHADE_BWD, shade);
     }
     if (e) return e;
     if (dec) {
