@@ -361,6 +361,53 @@ def test_backward_replay_equals_retrace(case_dense):
         assert grad_oracle.rel_l2(outs[0][k].cpu().numpy(), outs[1][k].cpu().numpy()) < 1e-5, k
 
 
+def test_backward_replay_detects_changed_inputs():
+    """The hit cache's content checksum covers every word of the inputs: with the same pointers and sizes
+    (so the cache key matches), a change of one word -- the first and the last word of a ray-origin array
+    that starts 4 bytes past a 16-byte boundary (the checksum's scalar head and tail), a word inside its
+    vector body, the last descriptor word -- makes the Backward re-traverse; no change lets it replay."""
+    c = Case(20000, 24, seed=2, eye=(0.0, 0.0, 2.0), fov=50.0)
+    R = c.R
+    buf = torch.empty(3 * R + 1, device="cuda")
+    buf[1:] = c.Og.flatten()
+    O = buf[1:].view(R, 3)
+    assert O.data_ptr() % 16 == 4
+
+    def backward_traces(touch):
+        for _ in range(2):  # the first forward on a renderer sizes the cache, the second fills it
+            bitmap, dacc, nacc, dai, sn = z(R, 3), z(R, 4), z(R, 4), z(R, 2), z(R, 3)
+            c.r.Forward_training(*c.dec(), O, c.vg, bitmap, 0.1, 0.2, 0.3, *c.geo(), 1e-4, dacc, REG_A, REG_B, dai,
+                                 sn, nacc)
+        undo = touch()
+        n = c.sc.n
+        G = dict(RGB=z(n, 3), A=z(n, 1), k=z(n, 1), m=z(n, 3), s=z(n, 2), q=z(n, 4), cond=z(n, 96), f=z(13154))
+        W = [z(1, 512), z(1, 64), z(1, 4096), z(1, 512), z(1, 8192), z(1, 512)]
+        c.r.profile(True)
+        c.r.Backward(*c.dec(), O, c.vg, 0.1, 0.2, 0.3, *c.geo(), bitmap.clone(), z(R, 3) + 1e-3, G["RGB"], G["A"],
+                     G["k"], *W, G["cond"], G["f"], G["m"], G["s"], G["q"], 1e-4, dacc, z(R, 4), 0.0, REG_A, REG_B,
+                     dai, sn, nacc, 0.0)
+        torch.cuda.synchronize()
+        traces = c.r.kernel_times()["trace"][1]
+        c.r.profile(False)
+        if undo:
+            undo()
+        return traces
+
+    def bump(t, i, d=1e-3):
+        def touch():
+            old = t.view(-1)[i].clone()
+            t.view(-1)[i] += d
+            return lambda: t.view(-1)[i].copy_(old)
+        return touch
+
+    assert backward_traces(lambda: None) == 0
+    assert backward_traces(bump(O, 0)) > 0
+    assert backward_traces(bump(O, 3 * R - 1)) > 0
+    assert backward_traces(bump(O, 3 * R // 2)) > 0
+    assert backward_traces(bump(c.g.cond, -1, 0.5)) > 0  # f16: a step it can represent
+    assert backward_traces(lambda: None) == 0
+
+
 def test_clustering_hierarchy_hits_bit_exact():
     """The alternative hierarchy builder (FLARE_BVH=ploc, read once per process) gives the same hit lists."""
     import subprocess
